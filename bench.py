@@ -1,0 +1,520 @@
+#!/usr/bin/env python
+"""INT4 dequant-GEMV benchmark on B200, and the reference's CPU path beside it.
+
+Workload, one step: every Llama-3.2-1B linear at M=1 in model order -- 16
+layers x (q_proj 2048->2048, k_proj / v_proj 2048->512, o_proj 2048->2048,
+gate_proj / up_proj 2048->8192, down_proj 8192->2048) + lm_head 2048->128256
+= 113 fused INT4 GEMVs (group 128) over distinct weights, seeded per layer
+(seed 1000*layer + shape index, lm_head layer 16), W ~ N(0, 0.02), x ~ N(0, 1).
+The step streams 658,160,128 algorithmic bytes (sum of K*N/2 + 4*(K/128)*N +
+2*M*K + 2*M*N), more than 2x the 126 MB L2, so every step reads its weights
+from HBM (no L2 flush needed).
+
+  value      whole-job GB/s with inputs resident in HBM: one CUDA graph of the
+             113 int4_linear_out calls replayed `--steps` times, CUDA events on
+             the replay stream, max over ranks.
+  e2e        the same step through the public API with host buffers: H2D copy
+             of the step's x vectors from pinned memory, the 113 calls (graph
+             replay), D2H copy of the 113 outputs, all inside the timed region.
+  roofline   the GEMV kernel (every launch in the timed region is one): bytes of
+             the step / its device time against the measured HBM copy peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With --gpus N > 1 (one process per GPU under torchrun) every rank runs its
+own replica of the stream (the decode GEMV path needs no data exchange):
+weak scaling, value = total bytes of all ranks / max time over ranks.
+--impl reference times the reference's CPU implementation (the oracle port
+of llama/quantize.py's v1 forward) on the host cores, on bounded samples.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "llama-efficient-inference_b200")
+for _p in (REPO, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "INT4 dequant-GEMV HBM GB/s (% of B200 peak) at M=1–16; 1B decode tokens/sec"
+LAYER_SHAPES = [("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
+                ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192)]
+LM_HEAD = ("lm_head", 128256, 2048)
+N_LAYERS = 16
+GROUP = 128
+L2_BYTES = 126 * 2 ** 20
+
+
+def stream_shapes():
+    """(name, N, K, seed) for the 113 GEMVs of one decode step, in model order."""
+    out = []
+    for layer in range(N_LAYERS):
+        for idx, (name, N, K) in enumerate(LAYER_SHAPES):
+            out.append((f"layers.{layer}.{name}", N, K, 1000 * layer + idx))
+    out.append((LM_HEAD[0], LM_HEAD[1], LM_HEAD[2], 1000 * N_LAYERS))
+    return out
+
+
+def gemv_bytes(N: int, K: int, M: int) -> int:
+    return K * N // 2 + 4 * (K // GROUP) * N + 2 * M * K + 2 * M * N
+
+
+def measured_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML, read-only)
+# ---------------------------------------------------------------------------
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+            0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device: torch.device, period_s: float = 0.05):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._thread = None
+        self.period = period_s
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(device).pci_bus_id if hasattr(
+                torch.cuda.get_device_properties(device), "pci_bus_id") else None
+            if bus is None:
+                props = torch.cuda.get_device_properties(device)
+                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 -- clocks are reported as unavailable, never guessed
+            self.nvml, self.err = None, str(e)
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "no nvml")}
+        reasons = [name for bit, name in _REASONS.items() if self.reasons & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing (one process per GPU; replicas, no data-path collective)
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int, device):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# The GPU arm
+# ---------------------------------------------------------------------------
+class Stream:
+    """Quantized weights + static x / y buffers of the 113-GEMV step on one GPU."""
+
+    def __init__(self, device: torch.device, M: int):
+        from llama.quantize import QuantizedLinear
+
+        self.device, self.M = device, M
+        self.shapes = stream_shapes()
+        self.weights = []
+        for name, N, K, seed in self.shapes:
+            gen = torch.Generator(device=device).manual_seed(seed)
+            w = (torch.randn(N, K, generator=gen, device=device) * 0.02).half()
+            self.weights.append(QuantizedLinear.quantize_tensor(w, GROUP))
+            del w
+        xk = sum(M * K for _, _, K, _ in self.shapes)
+        yn = sum(M * N for _, N, _, _ in self.shapes)
+        gen = torch.Generator(device=device).manual_seed(12345)
+        self.x_flat = torch.randn(xk, generator=gen, device=device).half()
+        self.y_flat = torch.empty(yn, dtype=torch.float16, device=device)
+        self.xs, self.ys = [], []
+        xo = yo = 0
+        for _, N, K, _ in self.shapes:
+            self.xs.append(self.x_flat[xo:xo + M * K].view(M, K))
+            self.ys.append(self.y_flat[yo:yo + M * N].view(M, N))
+            xo += M * K
+            yo += M * N
+        self.bytes_per_step = sum(gemv_bytes(N, K, M) for _, N, K, _ in self.shapes)
+        torch.cuda.synchronize(device)
+
+    def run_eager(self):
+        from llama.int4_gemv import int4_linear_out
+
+        for x, (p, s, z), y in zip(self.xs, self.weights, self.ys):
+            int4_linear_out(x, p, s, z, y, GROUP)
+
+    def capture(self):
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self.run_eager()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.run_eager()
+        torch.cuda.synchronize(self.device)
+
+
+def time_graph(stream: Stream, steps: int, warmup: int, world: int, sampler=None) -> float:
+    dev = stream.device
+    for _ in range(warmup):
+        stream.graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world, dev)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        start.record()
+        for _ in range(steps):
+            stream.graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+    barrier(world, dev)
+    return start.elapsed_time(end) / steps
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def time_e2e(stream: Stream, steps: int, warmup: int, world: int, eager: bool = False):
+    """H2D x (pinned) -> 113 calls -> D2H y (pinned), every step inside the timed region."""
+    dev = stream.device
+    hx = torch.empty(stream.x_flat.shape, dtype=torch.float16, pin_memory=True)
+    hx.copy_(stream.x_flat.cpu())
+    hy = torch.empty(stream.y_flat.shape, dtype=torch.float16, pin_memory=True)
+
+    def step():
+        stream.x_flat.copy_(hx, non_blocking=True)
+        if eager:
+            stream.run_eager()
+        else:
+            stream.graph.replay()
+        hy.copy_(stream.y_flat, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world, dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize(dev)
+    barrier(world, dev)
+    return start.elapsed_time(end) / steps, hx.numel() * 2, hy.numel() * 2
+
+
+def per_shape_isolated(stream: Stream, reps: int = 20):
+    """Each distinct shape timed alone (L2 flushed before every launch): kernel GB/s without stream overlap."""
+    from llama.int4_gemv import int4_linear_out
+
+    dev = stream.device
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    out = {}
+    seen = set()
+    for i, (name, N, K, _) in enumerate(stream.shapes):
+        short = name.split(".")[-1]
+        if short in seen:
+            continue
+        seen.add(short)
+        x, (p, s, z), y = stream.xs[i], stream.weights[i], stream.ys[i]
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            int4_linear_out(x, p, s, z, y, GROUP)
+            b.record()
+            torch.cuda.synchronize(dev)
+            times.append(a.elapsed_time(b))
+        us = statistics.median(times) * 1e3
+        out[short] = {"N": N, "K": K, "us": round(us, 2),
+                      "GBps": round(gemv_bytes(N, K, stream.M) / (us * 1e-6) / 1e9, 1)}
+    return out
+
+
+def roofline_traffic():
+    """DRAM bytes per step of the GEMV kernels from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", "gemv_stream_m1_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_step")
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# The CPU arm: the reference's v1 path as restated by the oracle
+# ---------------------------------------------------------------------------
+class CpuStream:
+    """Host copies of a stream's weights (random INT4 data; CPU cost is data-independent)."""
+
+    def __init__(self, M: int, seed: int = 0):
+        rng = np.random.default_rng(seed)
+        self.M = M
+        self.shapes = stream_shapes()
+        self.items = []
+        for name, N, K, _ in self.shapes:
+            packed = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+            scale = rng.uniform(0.002, 0.004, size=(N, K // GROUP)).astype(np.float16)
+            zero = rng.integers(0, 16, size=(N, K // GROUP)).astype(np.float16)
+            x = rng.standard_normal((M, K)).astype(np.float16)
+            self.items.append((name, N, K, x, packed, scale, zero))
+
+    def run_rows(self, start_row: int, n_rows: int):
+        """Process `n_rows` output rows of the stream starting at global row `start_row` (wrapping)."""
+        from oracle import oracle
+
+        total = sum(it[1] for it in self.items)
+        done_bytes = 0
+        row = start_row % total
+        remaining = n_rows
+        while remaining > 0:
+            acc = 0
+            for name, N, K, x, packed, scale, zero in self.items:
+                if row < acc + N:
+                    r0 = row - acc
+                    r1 = min(N, r0 + remaining)
+                    oracle.linear(x, packed[r0:r1], scale[r0:r1], zero[r0:r1], GROUP)
+                    rows = r1 - r0
+                    done_bytes += rows * (K // 2 + 4 * (K // GROUP) + 2 * self.M) + \
+                        2 * self.M * K * rows // N
+                    remaining -= rows
+                    row = (row + rows) % total
+                    break
+                acc += N
+        return done_bytes
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_rate(cs: CpuStream, seconds: float):
+    """Run the stream on the CPU for about `seconds`; returns (GB/s, rows, bytes, elapsed)."""
+    t0 = time.perf_counter()
+    nbytes = rows = 0
+    chunk = 4096
+    while time.perf_counter() - t0 < seconds:
+        nbytes += cs.run_rows(rows, chunk)
+        rows += chunk
+    dt = time.perf_counter() - t0
+    return nbytes / dt / 1e9, rows, nbytes, dt
+
+
+def run_reference(a):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    threads = cpu_threads()
+    oracle.set_threads(threads)
+    cs = CpuStream(a.m)
+    # calibrate, then size each step's sample so the whole run stays within ~2 minutes
+    rate, _, _, _ = cpu_rate(cs, 2.0)
+    budget_s = 90.0
+    total_rows = sum(it[1] for it in cs.items)
+    bytes_per_row = sum(gemv_bytes(N, K, a.m) for _, N, K, *_ in cs.items) / sum(it[1] for it in cs.items)
+    rows_per_step = max(64, int(rate * 1e9 * budget_s / (a.steps + a.warmup) / bytes_per_row))
+    rows_per_step = min(rows_per_step, total_rows)
+    row = 0
+    for _ in range(a.warmup):
+        cs.run_rows(row, rows_per_step)
+        row += rows_per_step
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(a.steps):
+        nbytes += cs.run_rows(row, rows_per_step)
+        row += rows_per_step
+    dt = time.perf_counter() - t0
+    gbps = nbytes / dt / 1e9
+    sample = (f"{rows_per_step} output rows of the 113-GEMV stream per step (model order, wrapping; "
+              f"{total_rows} rows = one full decode step)")
+    line = {
+        "metric": METRIC, "value": round(gbps, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (random INT4 weights, N(0,1) x)",
+        "config": {"workload": "llama3.2-1b int4 g128 decode linears, 16 layers x 7 + lm_head, M=%d" % a.m,
+                   "M": a.m, "gemvs_per_step": len(cs.items), "group_size": GROUP},
+        "cpu_baseline": {"value": round(gbps, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbps, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "world_size": world,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu(a):
+    world, rank, local = dist_setup(a.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = Stream(dev, a.m)
+    stream.capture()
+    sampler = ClockSampler(dev)
+    ms = time_graph(stream, a.steps, a.warmup, world, sampler)
+    ms_max = max_over_ranks(ms, world, dev)
+    e2e_steps = max(3, min(a.steps, 2000))
+    e2e_ms, h2d, d2h = time_e2e(stream, e2e_steps, max(3, a.warmup), world)
+    e2e_ms = max_over_ranks(e2e_ms, world, dev)
+    eager_steps = max(3, min(a.steps, 200))
+    eager_ms, _, _ = time_e2e(stream, eager_steps, 3, world, eager=True)
+    eager_ms = max_over_ranks(eager_ms, world, dev)
+
+    per_shape = per_shape_isolated(stream) if (rank == 0 and not a.no_per_shape) else None
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from oracle import oracle
+
+        threads = cpu_threads()
+        oracle.set_threads(threads)
+        cs = CpuStream(a.m)
+        gbps, rows, nbytes, dt = cpu_rate(cs, a.cpu_seconds)
+        total_rows = sum(it[1] for it in cs.items)
+        cpu = {"value": round(gbps, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{rows} output rows ({rows / total_rows:.2f} decode steps) of the 113-GEMV stream "
+                         f"in {dt:.1f} s"}
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    bps = stream.bytes_per_step
+    value = world * bps / (ms_max * 1e-3) / 1e9
+    achieved = bps / (ms * 1e-3) / 1e9
+    traffic = roofline_traffic()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (W ~ N(0,0.02) quantized INT4 g128 by the CUDA quantizer, x ~ N(0,1) fp16)",
+        "config": {"workload": "llama3.2-1b int4 g128 decode linears, 16 layers x 7 + lm_head, M=%d" % a.m,
+                   "M": a.m, "gemvs_per_step": len(stream.shapes), "bytes_per_step": bps, "group_size": GROUP,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
+                   "l2": "no flush: 658 MB of distinct weights per step > 2x the 126 MB L2",
+                   "timing": "one CUDA graph of the 113 int4_linear_out calls per step, CUDA events"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s",
+                     "kernel": "li4 fused INT4 GEMV (all 113 launches of the step)"},
+        "e2e": {"value": round(world * bps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
+                "path": "pinned H2D x -> graph of 113 int4_linear_out calls -> D2H y"},
+        "e2e_eager": {"value": round(world * bps / (eager_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                      "ms_per_step": round(eager_ms, 5),
+                      "path": "pinned H2D x -> 113 eager Python int4_linear_out calls -> D2H y"},
+        "gpu_launches": len(stream.shapes) * a.steps,
+        "clocks": sampler.summary(),
+        "cpu_baseline": cpu,
+        "per_shape_isolated": per_shape,
+        "gpu": torch.cuda.get_device_name(dev),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--m", type=int, default=1, help="rows of x per GEMV (decode batch), 1..16")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-shape", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_gpu(a)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and a.impl != "reference":
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,118 @@
+/*
+ * llama_int4_b200.h -- C ABI of the B200 (sm_100a) INT4 weight-only decode kernels.
+ *
+ * Weight format (identical to the reference's QuantizedLinear buffers,
+ * llama/quantize.py:29-36 and :44-75):
+ *   packed [N, K/2] uint8, row-major, row stride `stride_pn` bytes.
+ *          byte j of row n = q[n, 2j] | (q[n, 2j+1] << 4)   (low nibble = even k)
+ *   scale  [N, K/group] fp16, row stride `stride_sn` elements
+ *   zero   [N, K/group] fp16, same row stride as scale; integers 0..15
+ *   W[n, k] = fp16((q[n,k] - zero[n, k/group]) * scale[n, k/group])
+ *
+ * All pointers are device pointers unless stated otherwise; `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  No entry point
+ * allocates device memory, synchronises the device or aborts: each returns an
+ * li4_status and records a message readable with li4_last_error().
+ * fp16 values are passed as raw 16-bit IEEE half storage (uint16_t / void*).
+ */
+#ifndef LLAMA_INT4_B200_H
+#define LLAMA_INT4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum li4_status {
+  LI4_OK = 0,
+  LI4_ERR_INVALID_ARG = 1,   /* shape, stride or null-pointer precondition failed   */
+  LI4_ERR_ALIGNMENT = 2,     /* a pointer/stride breaks the 16-byte load contract    */
+  LI4_ERR_WORKSPACE = 3,     /* split-K workspace missing or too small               */
+  LI4_ERR_UNSUPPORTED = 4,   /* valid for the reference, not handled by these kernels */
+  LI4_ERR_CUDA = 5           /* a CUDA runtime call or kernel launch failed          */
+} li4_status;
+
+typedef enum li4_dtype {
+  LI4_F16 = 0,
+  LI4_BF16 = 1,
+  LI4_F32 = 2
+} li4_dtype;
+
+/* Largest M (rows of x) the decode kernels take.
+ * Replaces: MAX_M = 16 (llama/int4_gemv.py:29). */
+#define LI4_MAX_M 16
+
+/* Kernel families li4_int4_linear_ex can be forced to (LI4_KERNEL_AUTO lets the
+ * dispatcher choose from M, N, K and the SM count). */
+typedef enum li4_kernel {
+  LI4_KERNEL_AUTO = 0,
+  LI4_KERNEL_CUDA_CORE = 1,  /* fp32 FMA on CUDA cores, M <= 8                      */
+  LI4_KERNEL_MMA = 2         /* m16n8k16 tensor-core tiles (weights as the A side)  */
+} li4_kernel;
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int li4_version(void);
+
+/* Message describing the last failed call on this host thread ("" if none). */
+const char* li4_last_error(void);
+
+/* Bytes of split-K workspace li4_int4_linear needs for this problem on a
+ * device with `sm_count` SMs (0 = query the current device).  The workspace
+ * must be zero-filled once when it is allocated; every launch leaves its
+ * arrival counters at zero again, so it can be reused by later launches on
+ * the same stream (and inside CUDA graphs) without clearing.  Two launches
+ * that may run concurrently must not share a workspace. */
+size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count);
+
+/* y[M, N] (fp16, row stride stride_ym elements) = x[M, K] (fp16, row stride
+ * stride_xm) @ W^T, W given in the packed INT4 format above.  fp32
+ * accumulation; one kernel launch (split-K partial sums are reduced by the
+ * last-arriving CTA inside the same launch).  M in 1..16, K % 128 == 0,
+ * group_size a power of two >= 32 dividing K, packed rows 16-byte aligned.
+ * The launch is marked for programmatic dependent launch: its weight loads
+ * may overlap the tail of the preceding kernel on the stream; x is read only
+ * after that kernel has completed.
+ * Replaces: int4_linear (llama/int4_gemv.py:105-140) and its Triton kernel
+ * _int4_gemv_kernel (llama/int4_gemv.py:32-89), including the split-K
+ * zero-fill / atomic_add / .half() epilogue (llama/int4_gemv.py:126-139). */
+int li4_int4_linear(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                    int64_t M, int64_t N, int64_t K, int64_t group_size,
+                    int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* li4_int4_linear with an explicit kernel family and launch shape, for tuning
+ * sweeps: kernel (li4_kernel), rows_per_cta (16 or 32; 0 = auto), split
+ * (number of K ranges, 0 = auto), max_ctas (0 = auto).
+ * Replaces: the block_n / split_k / num_warps tuning knobs of int4_linear
+ * (llama/int4_gemv.py:105, swept by int4_gemv_bench.py:80-90). */
+int li4_int4_linear_ex(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                       int64_t M, int64_t N, int64_t K, int64_t group_size,
+                       int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
+                       void* workspace, size_t workspace_bytes, void* stream,
+                       int kernel, int rows_per_cta, int split, int max_ctas);
+
+/* w16[N, K] (fp16, row stride stride_wn elements) = dequantized weights,
+ * bit-identical to the reference's fp32 (q - zero) * scale rounded to fp16.
+ * Replaces: QuantizedLinear.dequantize_packed (llama/quantize.py:78-104) and
+ * the bit-identical dequantize_packed_v2 (llama/quantize.py:107-126). */
+int li4_dequantize(const void* packed, const void* scale, const void* zero, void* w16,
+                   int64_t N, int64_t K, int64_t group_size,
+                   int64_t stride_pn, int64_t stride_sn, int64_t stride_wn, void* stream);
+
+/* Quantize w[N, K] (dtype li4_dtype, row stride stride_wn elements) to the
+ * packed INT4 format: per-group min/max in fp32, scale = (max-min)/15 (0 -> 1),
+ * zero = clamp(round(-min/scale), 0, 15), q = clamp(round(w/scale + zero), 0, 15),
+ * round-half-to-even, IEEE fp32 division; scale and zero stored as fp16.
+ * Bit-identical to the reference (packed bytes, scale and zero bits).
+ * Outputs are contiguous: packed [N, K/2], scale/zero [N, K/group].
+ * Replaces: QuantizedLinear.quantize_tensor (llama/quantize.py:44-75). */
+int li4_quantize(const void* w, int w_dtype, void* packed, void* scale, void* zero,
+                 int64_t N, int64_t K, int64_t group_size, int64_t stride_wn, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLAMA_INT4_B200_H */

@@ -1,0 +1,751 @@
+// li4_gemv.cu -- fused INT4 dequant + GEMV / small-M GEMM for decode (M <= 16), sm_100a.
+//
+// y[M, N] = x[M, K] @ W[N, K]^T with W in the packed INT4 format of
+// llama/quantize.py:44-75 (see include/llama_int4_b200.h).
+//
+// Work decomposition (both kernel families):
+//   * a CTA (4 warps) owns a tile of ROWS = 16*RT consecutive output rows n
+//     and one K range of `ks_per_split` ksteps (a kstep = 128 k = 64 packed
+//     bytes per row); grid.y indexes the K range (split-K), grid.x walks the
+//     row tiles persistently;
+//   * the 4 warps interleave the ksteps of the K range; inside a warp, lane
+//     (grp = lane/4, quad = lane%4) reads rows grp and grp+8 of each 16-row
+//     slab, bytes [16*quad, 16*quad + 16) of each kstep: one 128-bit load
+//     covers 32 k values of one row, 4 lanes cover a 64-byte kstep, so every
+//     warp-wide load touches 8 rows x 64 contiguous bytes;
+//   * x for the CTA's K range is staged once in shared memory, permuted into
+//     the (k, k+4) pairs that the nibble unpack produces;
+//   * partial sums of the 4 warps are reduced in shared memory; with split-K
+//     the K ranges write fp32 partials to a workspace and the last CTA to
+//     arrive on a tile (arrival counter) sums them in fixed order, writes
+//     fp16 y and resets the counter -- one launch, no zero-fill, no cast
+//     kernel (replaces llama/int4_gemv.py:80-89, 126-139).
+//
+// Math:
+//   * MMA family: W slab (16 rows x 16 k, exact q - zero in fp16) is the A
+//     operand of mma.m16n8k16 and x^T the B operand (M in the n dimension,
+//     padded to 8 or 16); fp32 accumulation per 128-k kstep, then scaled by
+//     the group scale in fp32 (groups >= 128), or scale applied to A in fp16
+//     (groups 32/64: the fp16 weight equals the reference's bit for bit).
+//   * CUDA-core family (M <= 8): each lane forms sum_k (q - zero) * x over its
+//     32 k with sm_100 mixed-precision fp16 x fp16 + fp32 FMAs, scales by the
+//     group scale in fp32, and the 4 lanes of a row are reduced by warp
+//     shuffles.
+#include "li4_common.cuh"
+#include "li4_internal.h"
+
+#include <mutex>
+#include <vector>
+
+namespace li4 {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxKsPerCta = 16;  // K range of one CTA <= 16 * 128 = 2048 (x staging)
+constexpr int kBatch = 4;         // ksteps one warp loads before it computes
+
+struct GemvArgs {
+  const __half* x;
+  const uint8_t* packed;
+  const __half* scale;
+  const __half* zero;
+  __half* y;
+  int M, N, K;
+  int log2_group;
+  long long sxm, spn, ssn, sym;  // strides: x, scale/zero, y in elements; packed in bytes
+  int n_tiles;                   // ceil(N / ROWS)
+  int split;                     // number of K ranges (grid.y)
+  int ks_per_split;              // ksteps per K range
+  float* partial;                // [split][M][N] fp32, split > 1 only
+  unsigned* counters;            // [n_tiles] arrival counters, split > 1 only
+};
+
+// ---------------------------------------------------------------------------
+// x staging.  Block b = ((ks * NT + nt) * M8 + m8) * 4 + quad holds the 32
+// values x[m][k0 .. k0+32), m = nt*8 + m8, k0 = kstep*128 + 32*quad, as 16
+// half2 words; word 4w + i = (x[k0 + 8w + i], x[k0 + 8w + i + 4]).  Chunk w
+// (16 bytes) of block b sits at b*64 + ((w ^ ((b >> 1) & 3)) << 4), which
+// keeps the 128-bit reads of 8 consecutive blocks on distinct banks.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int xs_chunk_offset(int block, int w) {
+  return block * 64 + ((w ^ ((block >> 1) & 3)) << 4);
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+template <int NT>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs) {
+  const int total = nks * NT * M8 * 16;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
+  for (int idx = threadIdx.x; idx < total; idx += kThreads) {
+    const int w = idx & 3;
+    const int block = idx >> 2;
+    const int quad = block & 3;
+    const int t = block >> 2;
+    const int m8 = t % M8;
+    const int t2 = t / M8;
+    const int nt = t2 % NT;
+    const int ks = t2 / NT;
+    const int m = nt * 8 + m8;
+    uint4 out = make_uint4(0u, 0u, 0u, 0u);
+    if (m < a.M) {
+      const long long k = (long long)(ks0 + ks) * 128 + 32 * quad + 8 * w;
+      const __half* src = a.x + (long long)m * a.sxm + k;
+      uint32_t u[4];
+      if (vec_ok) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src);
+        u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
+      }
+      out.x = __byte_perm(u[0], u[2], 0x5410);  // (x0, x4)
+      out.y = __byte_perm(u[0], u[2], 0x7632);  // (x1, x5)
+      out.z = __byte_perm(u[1], u[3], 0x5410);  // (x2, x6)
+      out.w = __byte_perm(u[1], u[3], 0x7632);  // (x3, x7)
+    }
+    *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w)) = out;
+  }
+}
+
+// Start pulling the first row tile's weight bytes into L2 (TMA bulk prefetch)
+// before waiting on the preceding kernel.
+template <int ROWS>
+__device__ __forceinline__ void prefetch_first_tile(const GemvArgs& a, int ks0, int nks) {
+  const int tile = blockIdx.x;
+  if (tile >= a.n_tiles || nks == 0) return;
+  const int r = tile * ROWS + threadIdx.x;
+  if (threadIdx.x < ROWS && r < a.N) {
+    const uint8_t* p = a.packed + (long long)r * a.spn + (long long)ks0 * 64;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(nks * 64) : "memory");
+  }
+}
+
+// Sum the per-warp partials of one row tile and write y (split == 1) or the
+// split-K partials + last-arriver reduction (split > 1).
+template <int ROWS, int COLS>
+__device__ __forceinline__ void finish_tile(const GemvArgs& a, int tile, const float* red, int* s_flag) {
+  const int row0 = tile * ROWS;
+  const int M = a.M;
+  if (a.split == 1) {
+    for (int idx = threadIdx.x; idx < ROWS * M; idx += kThreads) {
+      const int row = idx / M, m = idx - (idx / M) * M;
+      const int n = row0 + row;
+      if (n < a.N) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += red[(w * ROWS + row) * COLS + m];
+        a.y[(long long)m * a.sym + n] = __float2half_rn(v);
+      }
+    }
+    return;
+  }
+  for (int idx = threadIdx.x; idx < ROWS * M; idx += kThreads) {
+    const int row = idx / M, m = idx - (idx / M) * M;
+    const int n = row0 + row;
+    if (n < a.N) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) v += red[(w * ROWS + row) * COLS + m];
+      a.partial[((long long)blockIdx.y * M + m) * a.N + n] = v;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&a.counters[tile], 1u);
+    *s_flag = (prev == (unsigned)(a.split - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (*s_flag) {
+    __threadfence();
+    for (int idx = threadIdx.x; idx < ROWS * M; idx += kThreads) {
+      const int row = idx / M, m = idx - (idx / M) * M;
+      const int n = row0 + row;
+      if (n < a.N) {
+        float v = 0.f;
+        for (int s = 0; s < a.split; ++s) v += __ldcg(&a.partial[((long long)s * M + m) * a.N + n]);
+        a.y[(long long)m * a.sym + n] = __float2half_rn(v);
+      }
+    }
+    if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core family.
+// ---------------------------------------------------------------------------
+template <int RT, int NT, bool SCALE_IN_A>
+__global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_flag;
+  constexpr int ROWS = 16 * RT;
+  constexpr int COLS = 8 * NT;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane >> 2, quad = lane & 3;
+  const int nks = a.ks_per_split;
+  const int ks0 = blockIdx.y * nks;
+  const int M8 = (NT == 1) ? a.M : 8;
+  uint8_t* xs = smem;
+  float* red = reinterpret_cast<float*>(smem + ((nks * NT * M8 * 256 + 127) & ~127));
+
+  pdl_launch_dependents();
+  prefetch_first_tile<ROWS>(a, ks0, nks);
+  pdl_wait_primary();
+  stage_x<NT>(a, ks0, nks, M8, xs);
+  __syncthreads();
+
+  for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+    const int row0 = tile * ROWS;
+    const uint8_t* prow[RT][2];
+    const __half* srow[RT][2];
+    const __half* zrow[RT][2];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        int r = row0 + rt * 16 + grp + 8 * h;
+        r = r < a.N ? r : a.N - 1;
+        prow[rt][h] = a.packed + (long long)r * a.spn + (long long)ks0 * 64 + quad * 16;
+        srow[rt][h] = a.scale + (long long)r * a.ssn;
+        zrow[rt][h] = a.zero + (long long)r * a.ssn;
+      }
+
+    float acc[RT][NT][4];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[rt][nt][e] = 0.f;
+
+    for (int kb = warp; kb < nks; kb += kWarps * kBatch) {
+      uint4 wv[kBatch][RT][2];
+      __half sv[kBatch][RT][2], zv[kBatch][RT][2];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int ks = kb + b * kWarps;
+        if (ks < nks) {
+          const int g = ((ks0 + ks) * 128 + 32 * quad) >> a.log2_group;
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              wv[b][rt][h] = ldg_stream_v4(prow[rt][h] + ks * 64);
+              sv[b][rt][h] = ldg_half(srow[rt][h] + g);
+              zv[b][rt][h] = ldg_half(zrow[rt][h] + g);
+            }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int ks = kb + b * kWarps;
+        if (ks < nks) {
+          ZeroConsts zc[RT][2];
+          __half2 s2[RT][2];
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              zc[rt][h] = make_zero_consts(zv[b][rt][h]);
+              s2[rt][h] = __halves2half2(sv[b][rt][h], sv[b][rt][h]);
+            }
+          float c[RT][NT][4];
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) c[rt][nt][e] = 0.f;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            __half2 p[RT][2][4];
+#pragma unroll
+            for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 v = wv[b][rt][h];
+                const uint32_t word = (w == 0) ? v.x : (w == 1) ? v.y : (w == 2) ? v.z : v.w;
+                unpack8_qz(word, zc[rt][h], p[rt][h]);
+                if (SCALE_IN_A) {
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) p[rt][h][i] = __hmul2(p[rt][h][i], s2[rt][h]);
+                }
+              }
+            uint4 bq[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (grp < M8)
+                bq[nt] = lds128(xs + xs_chunk_offset(((ks * NT + nt) * M8 + grp) * 4 + quad, w));
+              else
+                bq[nt] = make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                float* cc = SCALE_IN_A ? acc[rt][nt] : c[rt][nt];
+                mma_16816(cc, h2_as_u32(p[rt][0][0]), h2_as_u32(p[rt][1][0]), h2_as_u32(p[rt][0][1]),
+                          h2_as_u32(p[rt][1][1]), bq[nt].x, bq[nt].y);
+                mma_16816(cc, h2_as_u32(p[rt][0][2]), h2_as_u32(p[rt][1][2]), h2_as_u32(p[rt][0][3]),
+                          h2_as_u32(p[rt][1][3]), bq[nt].z, bq[nt].w);
+              }
+          }
+          if (!SCALE_IN_A) {
+#pragma unroll
+            for (int rt = 0; rt < RT; ++rt) {
+              const float s_lo = __half2float(sv[b][rt][0]);
+              const float s_hi = __half2float(sv[b][rt][1]);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                acc[rt][nt][0] = fmaf(s_lo, c[rt][nt][0], acc[rt][nt][0]);
+                acc[rt][nt][1] = fmaf(s_lo, c[rt][nt][1], acc[rt][nt][1]);
+                acc[rt][nt][2] = fmaf(s_hi, c[rt][nt][2], acc[rt][nt][2]);
+                acc[rt][nt][3] = fmaf(s_hi, c[rt][nt][3], acc[rt][nt][3]);
+              }
+            }
+          }
+        }
+      }
+    }
+
+    __syncthreads();  // previous tile's readers of `red` are done
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = rt * 16 + grp + 8 * (e >> 1);
+          const int col = nt * 8 + 2 * quad + (e & 1);
+          red[(warp * ROWS + row) * COLS + col] = acc[rt][nt][e];
+        }
+    __syncthreads();
+    finish_tile<ROWS, COLS>(a, tile, red, &s_flag);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core family (M <= 8).
+// ---------------------------------------------------------------------------
+template <int M, int RT>
+__global__ void __launch_bounds__(kThreads) gemv_cc_kernel(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_flag;
+  constexpr int ROWS = 16 * RT;
+  constexpr int COLS = 8;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane >> 2, quad = lane & 3;
+  const int nks = a.ks_per_split;
+  const int ks0 = blockIdx.y * nks;
+  uint8_t* xs = smem;
+  float* red = reinterpret_cast<float*>(smem + ((nks * M * 256 + 127) & ~127));
+
+  pdl_launch_dependents();
+  prefetch_first_tile<ROWS>(a, ks0, nks);
+  pdl_wait_primary();
+  stage_x<1>(a, ks0, nks, M, xs);
+  __syncthreads();
+
+  for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+    const int row0 = tile * ROWS;
+    const uint8_t* prow[RT][2];
+    const __half* srow[RT][2];
+    const __half* zrow[RT][2];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        int r = row0 + rt * 16 + grp + 8 * h;
+        r = r < a.N ? r : a.N - 1;
+        prow[rt][h] = a.packed + (long long)r * a.spn + (long long)ks0 * 64 + quad * 16;
+        srow[rt][h] = a.scale + (long long)r * a.ssn;
+        zrow[rt][h] = a.zero + (long long)r * a.ssn;
+      }
+
+    float acc[RT][2][M];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[rt][h][m] = 0.f;
+
+    for (int kb = warp; kb < nks; kb += kWarps * kBatch) {
+      uint4 wv[kBatch][RT][2];
+      __half sv[kBatch][RT][2], zv[kBatch][RT][2];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int ks = kb + b * kWarps;
+        if (ks < nks) {
+          const int g = ((ks0 + ks) * 128 + 32 * quad) >> a.log2_group;
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              wv[b][rt][h] = ldg_stream_v4(prow[rt][h] + ks * 64);
+              sv[b][rt][h] = ldg_half(srow[rt][h] + g);
+              zv[b][rt][h] = ldg_half(zrow[rt][h] + g);
+            }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int ks = kb + b * kWarps;
+        if (ks < nks) {
+          ZeroConsts zc[RT][2];
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) zc[rt][h] = make_zero_consts(zv[b][rt][h]);
+          float part[RT][2][M];
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int m = 0; m < M; ++m) part[rt][h][m] = 0.f;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            __half2 p[RT][2][4];
+#pragma unroll
+            for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 v = wv[b][rt][h];
+                const uint32_t word = (w == 0) ? v.x : (w == 1) ? v.y : (w == 2) ? v.z : v.w;
+                unpack8_qz(word, zc[rt][h], p[rt][h]);
+              }
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              const uint4 xq = lds128(xs + xs_chunk_offset((ks * M + m) * 4 + quad, w));
+#pragma unroll
+              for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  float t = part[rt][h][m];
+                  t = fma2_f16_f32(h2_as_u32(p[rt][h][0]), xq.x, t);
+                  t = fma2_f16_f32(h2_as_u32(p[rt][h][1]), xq.y, t);
+                  t = fma2_f16_f32(h2_as_u32(p[rt][h][2]), xq.z, t);
+                  t = fma2_f16_f32(h2_as_u32(p[rt][h][3]), xq.w, t);
+                  part[rt][h][m] = t;
+                }
+            }
+          }
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float s = __half2float(sv[b][rt][h]);
+#pragma unroll
+              for (int m = 0; m < M; ++m) acc[rt][h][m] = fmaf(s, part[rt][h][m], acc[rt][h][m]);
+            }
+        }
+      }
+    }
+
+    // reduce the 4 lanes (quads) that share a row
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          float v = acc[rt][h][m];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          acc[rt][h][m] = v;
+        }
+
+    __syncthreads();
+    if (quad == 0) {
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int m = 0; m < M; ++m) red[(warp * ROWS + rt * 16 + grp + 8 * h) * COLS + m] = acc[rt][h][m];
+    }
+    __syncthreads();
+    finish_tile<ROWS, COLS>(a, tile, red, &s_flag);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: planning and launch.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int kernel;      // LI4_KERNEL_CUDA_CORE / LI4_KERNEL_MMA
+  int rt;          // 1 or 2 (16 or 32 rows per CTA)
+  int nt;          // MMA: 1 (M <= 8) or 2
+  bool scale_in_a; // MMA with groups < 128
+  int n_ks;
+  int split;
+  int ks_per_split;
+  int n_tiles;
+  int grid_x;
+  bool auto_grid;  // size grid_x from the kernel's occupancy at launch
+  int sm;
+  size_t smem;
+  size_t ws_counters;  // bytes
+  size_t ws_bytes;     // total
+};
+
+static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int kernel_req, int rows_req,
+                     int split_req, int max_ctas, Plan* p) {
+  if (M < 1 || M > LI4_MAX_M)
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: M=%lld outside 1..%d", (long long)M, LI4_MAX_M);
+  if (N < 1) return set_error(LI4_ERR_INVALID_ARG, "int4_linear: N=%lld < 1", (long long)N);
+  if (K < 0 || K % 128 != 0)
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: K=%lld must be a multiple of 128", (long long)K);
+  if (!is_pow2(group) || group < 32 || (K > 0 && K % group != 0))
+    return set_error(LI4_ERR_UNSUPPORTED,
+                     "int4_linear: group_size=%lld must be a power of two >= 32 dividing K=%lld", (long long)group,
+                     (long long)K);
+  if (N > (int64_t(1) << 30) || K > (int64_t(1) << 24))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: N=%lld K=%lld too large", (long long)N, (long long)K);
+  if (sm <= 0) sm = 148;
+
+  int kernel = kernel_req;
+  if (kernel == LI4_KERNEL_AUTO) kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
+  if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel takes M <= 8 (M=%lld)", (long long)M);
+  if (kernel != LI4_KERNEL_CUDA_CORE && kernel != LI4_KERNEL_MMA)
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: unknown kernel %d", kernel);
+  p->kernel = kernel;
+  p->nt = (M <= 8) ? 1 : 2;
+  p->scale_in_a = group < 128;
+
+  if (rows_req == 16) p->rt = 1;
+  else if (rows_req == 32) p->rt = 2;
+  else if (rows_req == 0) p->rt = (N >= 4096) ? 2 : 1;
+  else return set_error(LI4_ERR_INVALID_ARG, "int4_linear: rows_per_cta=%d must be 0, 16 or 32", rows_req);
+  const int rows = 16 * p->rt;
+  p->n_tiles = (int)((N + rows - 1) / rows);
+  p->n_ks = (int)(K / 128);
+
+  int split = 1;
+  if (split_req > 0) {
+    split = split_req;
+    if (p->n_ks == 0 || p->n_ks % split != 0 || p->n_ks / split > kMaxKsPerCta)
+      return set_error(LI4_ERR_INVALID_ARG, "int4_linear: split=%d must divide K/128=%d into ranges of <= %d",
+                       split, p->n_ks, kMaxKsPerCta);
+  } else if (p->n_ks > 0) {
+    // smallest divisor of n_ks giving K ranges of at most kMaxKsPerCta ksteps
+    while (p->n_ks % split != 0 || p->n_ks / split > kMaxKsPerCta) ++split;
+    // more K ranges while the row tiles alone leave SMs idle and every warp keeps >= 1 kstep
+    while ((int64_t)p->n_tiles * split < 2 * sm && p->n_ks % (2 * split) == 0 &&
+           p->n_ks / (2 * split) >= kWarps)
+      split *= 2;
+  }
+  p->split = split;
+  p->ks_per_split = (p->n_ks == 0) ? 0 : p->n_ks / split;
+
+  p->sm = sm;
+  p->auto_grid = (max_ctas <= 0);
+  const int cap = (max_ctas > 0) ? max_ctas : sm * 4;
+  int gx = cap / split;
+  if (gx < 1) gx = 1;
+  if (gx > p->n_tiles) gx = p->n_tiles;
+  p->grid_x = gx;
+
+  const int m8 = (p->kernel == LI4_KERNEL_CUDA_CORE) ? (int)M : (p->nt == 1 ? (int)M : 8);
+  const int nt = (p->kernel == LI4_KERNEL_CUDA_CORE) ? 1 : p->nt;
+  const int cols = 8 * nt;
+  p->smem = round_up((size_t)p->ks_per_split * nt * m8 * 256, 128) + (size_t)kWarps * rows * cols * sizeof(float);
+
+  if (split > 1) {
+    p->ws_counters = round_up((size_t)p->n_tiles * sizeof(unsigned), 256);
+    p->ws_bytes = p->ws_counters + (size_t)split * M * N * sizeof(float);
+  } else {
+    p->ws_counters = 0;
+    p->ws_bytes = 0;
+  }
+  return LI4_OK;
+}
+
+// CTAs of `kernel` that fit on one SM with `smem` bytes of dynamic shared
+// memory (cached; the answer depends only on the kernel and smem size).
+template <typename KernelT>
+static int ctas_per_sm(KernelT kernel, size_t smem) {
+  struct Entry { const void* fn; size_t smem; int dev; int n; };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : cache)
+    if (e.fn == (const void*)kernel && e.smem == smem && e.dev == dev) return e.n;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem) != cudaSuccess || n < 1) n = 1;
+  cache.push_back(Entry{(const void*)kernel, smem, dev, n});
+  return n;
+}
+
+// Raise the kernel's dynamic shared memory limit once per (kernel, device)
+// to the largest size requested so far, so launches after the first (for
+// example inside CUDA-graph capture) make no attribute call.
+template <typename KernelT>
+static int ensure_smem_limit(KernelT kernel, size_t smem) {
+  if (smem <= 48 * 1024) return LI4_OK;
+  struct Entry { const void* fn; int dev; size_t limit; };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (Entry& e : cache)
+    if (e.fn == (const void*)kernel && e.dev == dev) {
+      if (e.limit >= smem) return LI4_OK;
+      const int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                "int4_linear: cudaFuncSetAttribute");
+      if (rc == LI4_OK) e.limit = smem;
+      return rc;
+    }
+  const int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                            "int4_linear: cudaFuncSetAttribute");
+  if (rc == LI4_OK) cache.push_back(Entry{(const void*)kernel, dev, smem});
+  return rc;
+}
+
+template <typename KernelT>
+static int launch(KernelT kernel, const Plan& p, const GemvArgs& args, cudaStream_t stream) {
+  int rc = ensure_smem_limit(kernel, p.smem);
+  if (rc != LI4_OK) return rc;
+  int grid_x = p.grid_x;
+  if (p.auto_grid) {  // persistent grid: every CTA resident at once
+    const int cap = ctas_per_sm(kernel, p.smem) * p.sm;
+    grid_x = cap / p.split;
+    if (grid_x < 1) grid_x = 1;
+    if (grid_x > p.n_tiles) grid_x = p.n_tiles;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid_x, (unsigned)p.split, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args), "int4_linear: kernel launch");
+}
+
+template <int M>
+static int launch_cc(const Plan& p, const GemvArgs& args, cudaStream_t s) {
+  return p.rt == 1 ? launch(gemv_cc_kernel<M, 1>, p, args, s) : launch(gemv_cc_kernel<M, 2>, p, args, s);
+}
+
+static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
+  if (p.kernel == LI4_KERNEL_CUDA_CORE) {
+    switch (args.M) {
+      case 1: return launch_cc<1>(p, args, s);
+      case 2: return launch_cc<2>(p, args, s);
+      case 3: return launch_cc<3>(p, args, s);
+      case 4: return launch_cc<4>(p, args, s);
+      case 5: return launch_cc<5>(p, args, s);
+      case 6: return launch_cc<6>(p, args, s);
+      case 7: return launch_cc<7>(p, args, s);
+      case 8: return launch_cc<8>(p, args, s);
+      default: return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel M=%d", args.M);
+    }
+  }
+  const int sel = (p.rt - 1) * 4 + (p.nt - 1) * 2 + (p.scale_in_a ? 1 : 0);
+  switch (sel) {
+    case 0: return launch(gemv_mma_kernel<1, 1, false>, p, args, s);
+    case 1: return launch(gemv_mma_kernel<1, 1, true>, p, args, s);
+    case 2: return launch(gemv_mma_kernel<1, 2, false>, p, args, s);
+    case 3: return launch(gemv_mma_kernel<1, 2, true>, p, args, s);
+    case 4: return launch(gemv_mma_kernel<2, 1, false>, p, args, s);
+    case 5: return launch(gemv_mma_kernel<2, 1, true>, p, args, s);
+    case 6: return launch(gemv_mma_kernel<2, 2, false>, p, args, s);
+    default: return launch(gemv_mma_kernel<2, 2, true>, p, args, s);
+  }
+}
+
+static int int4_linear_impl(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                            int64_t M, int64_t N, int64_t K, int64_t group, int64_t sxm, int64_t spn, int64_t ssn,
+                            int64_t sym, void* workspace, size_t workspace_bytes, void* stream, int kernel,
+                            int rows_req, int split_req, int max_ctas) {
+  Plan p = {};
+  const int sm = current_sm_count();
+  int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p);
+  if (rc != LI4_OK) return rc;
+  if (!x || !packed || !scale || !zero || !y)
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: null tensor pointer");
+  if (sxm < K || sym < N || spn < K / 2 || ssn < (K > 0 ? K / group : 0))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: row strides (x %lld, packed %lld, scale %lld, y %lld) "
+                     "smaller than the rows", (long long)sxm, (long long)spn, (long long)ssn, (long long)sym);
+  if (!aligned16(packed) || spn % 16 != 0)
+    return set_error(LI4_ERR_ALIGNMENT, "int4_linear: packed rows must start on 16-byte boundaries "
+                     "(base %p, row stride %lld bytes)", packed, (long long)spn);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(scale) |
+       reinterpret_cast<uintptr_t>(zero)) & 1u)
+    return set_error(LI4_ERR_ALIGNMENT, "int4_linear: fp16 tensors must be 2-byte aligned");
+  if (p.ws_bytes > 0) {
+    if (!workspace || workspace_bytes < p.ws_bytes)
+      return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "
+                       "workspace, got %zu", p.split, p.ws_bytes, workspace ? workspace_bytes : (size_t)0);
+    if (!aligned16(workspace)) return set_error(LI4_ERR_ALIGNMENT, "int4_linear: workspace must be 16-byte aligned");
+  }
+  GemvArgs args;
+  args.x = static_cast<const __half*>(x);
+  args.packed = static_cast<const uint8_t*>(packed);
+  args.scale = static_cast<const __half*>(scale);
+  args.zero = static_cast<const __half*>(zero);
+  args.y = static_cast<__half*>(y);
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.log2_group = ilog2(group);
+  args.sxm = sxm;
+  args.spn = spn;
+  args.ssn = ssn;
+  args.sym = sym;
+  args.n_tiles = p.n_tiles;
+  args.split = p.split;
+  args.ks_per_split = p.ks_per_split;
+  args.counters = p.ws_bytes ? static_cast<unsigned*>(workspace) : nullptr;
+  args.partial = p.ws_bytes ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.ws_counters) : nullptr;
+  rc = launch_plan(p, args, static_cast<cudaStream_t>(stream));
+  if (rc == LI4_OK) clear_error();
+  return rc;
+}
+
+}  // namespace li4
+
+extern "C" size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count) {
+  li4::Plan p = {};
+  const int sm = sm_count > 0 ? sm_count : li4::current_sm_count();
+  if (li4::make_plan(M, N, K, group_size, sm, LI4_KERNEL_AUTO, 0, 0, 0, &p) != LI4_OK) return 0;
+  // Enough for every kernel family and launch shape the dispatcher may pick.
+  size_t best = p.ws_bytes;
+  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_MMA; ++kernel) {
+    if (kernel == LI4_KERNEL_CUDA_CORE && M > 8) continue;
+    if (li4::make_plan(M, N, K, group_size, sm, kernel, 0, 0, 0, &p) == LI4_OK && p.ws_bytes > best) best = p.ws_bytes;
+  }
+  return best;
+}
+
+extern "C" int li4_int4_linear(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                               int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t stride_xm,
+                               int64_t stride_pn, int64_t stride_sn, int64_t stride_ym, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return li4::int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn,
+                               stride_ym, workspace, workspace_bytes, stream, LI4_KERNEL_AUTO, 0, 0, 0);
+}
+
+extern "C" int li4_int4_linear_ex(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                                  int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t stride_xm,
+                                  int64_t stride_pn, int64_t stride_sn, int64_t stride_ym, void* workspace,
+                                  size_t workspace_bytes, void* stream, int kernel, int rows_per_cta, int split,
+                                  int max_ctas) {
+  return li4::int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn,
+                               stride_ym, workspace, workspace_bytes, stream, kernel, rows_per_cta, split, max_ctas);
+}

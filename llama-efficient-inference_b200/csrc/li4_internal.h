@@ -1,0 +1,25 @@
+// li4_internal.h -- host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+
+#include "../../include/llama_int4_b200.h"
+
+namespace li4 {
+
+// Record a formatted message for li4_last_error() and return `status`.
+int set_error(int status, const char* fmt, ...);
+// Clear the per-thread message (successful call).
+void clear_error();
+// Map a CUDA error to LI4_ERR_CUDA with context; LI4_OK if err == cudaSuccess.
+int check_cuda(cudaError_t err, const char* what);
+// SM count of the current device (cached per device ordinal).
+int current_sm_count();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+inline int ilog2(int64_t v) { int r = 0; while ((int64_t(1) << r) < v) ++r; return r; }
+
+}  // namespace li4

@@ -1,0 +1,115 @@
+"""ctypes binding of the C-ABI kernel library (include/llama_int4_b200.h).
+
+The library is lib/libllama_int4_b200.so next to this package, built by
+build.py.  There is no fallback: if it is missing or fails to load, every
+entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libllama_int4_b200.so")
+
+LI4_OK = 0
+LI4_ERR_INVALID_ARG = 1
+LI4_ERR_ALIGNMENT = 2
+LI4_ERR_WORKSPACE = 3
+LI4_ERR_UNSUPPORTED = 4
+LI4_ERR_CUDA = 5
+
+LI4_F16, LI4_BF16, LI4_F32 = 0, 1, 2
+KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA = 0, 1, 2
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_SZ = ctypes.c_size_t
+_INT = ctypes.c_int
+
+# name -> (restype, argtypes); mirrors include/llama_int4_b200.h
+SIGNATURES = {
+    "li4_version": (_INT, []),
+    "li4_last_error": (ctypes.c_char_p, []),
+    "li4_int4_linear_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _INT]),
+    "li4_int4_linear": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
+    "li4_int4_linear_ex": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
+                                  _INT, _INT, _INT, _INT]),
+    "li4_dequantize": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "li4_quantize": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class Li4Error(RuntimeError):
+    """A C-ABI call returned a non-zero li4_status."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} (li4_status {status})")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load the kernel library (once)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(f"{LIB_PATH} is missing: build it with "
+                                  f"`python {os.path.join(PKG_DIR, 'build.py')}` (nvcc, sm_100a)")
+            l = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(l, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = l
+    return _lib
+
+
+def last_error() -> str:
+    return lib().li4_last_error().decode(errors="replace")
+
+
+def check(status: int, what: str = "") -> None:
+    if status != LI4_OK:
+        msg = last_error()
+        raise Li4Error(status, f"{what}: {msg}" if what else msg)
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# Split-K workspace: one zero-initialised buffer per device, grown outside
+# CUDA-graph capture.  Kernels leave its counters at zero, so launches that
+# follow each other on a stream (eager or replayed) can share it; launches that
+# may overlap on the GPU (different streams) must not.
+# ---------------------------------------------------------------------------
+_ws: dict[int, torch.Tensor] = {}
+_WS_MIN = 8 << 20
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _ws.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"int4_linear needs a {nbytes}-byte split-K workspace on cuda:{idx} but a CUDA graph "
+                               f"is being captured; run the same call once eagerly (warm-up) before capture, or "
+                               f"call llama.int4_gemv.reserve_workspace() first")
+        size = max(nbytes, _WS_MIN, 2 * (buf.numel() if buf is not None else 0))
+        buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _ws[idx] = buf
+    return buf

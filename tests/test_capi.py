@@ -1,0 +1,104 @@
+"""The C-ABI library: loads, exports every symbol include/llama_int4_b200.h
+declares, and rejects bad arguments with status codes before any launch.
+Runs without a GPU (no kernel is launched)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "llama_int4_b200.h")
+
+
+@pytest.fixture(scope="module")
+def native():
+    import build  # llama-efficient-inference_b200/build.py
+
+    build.build()
+    from llama import _native
+
+    return _native
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(li4_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "li4_int4_linear" in names and "li4_quantize" in names and "li4_dequantize" in names
+
+
+def test_library_exports_every_declared_symbol(native):
+    lib = native.lib()
+    names = declared_functions()
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert set(names) == set(native.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_version(native):
+    v = native.lib().li4_version()
+    assert v >> 16 == 0 and (v >> 8) & 0xFF >= 1
+
+
+def call_linear(native, M=1, N=64, K=256, group=128, x=16, packed=16, scale=16, zero=16, y=16,
+                sxm=None, spn=None, ssn=None, sym=None, ws=None, ws_len=0):
+    lib = native.lib()
+    return lib.li4_int4_linear(x, packed, scale, zero, y, M, N, K, group,
+                               K if sxm is None else sxm, K // 2 if spn is None else spn,
+                               max(1, K // group) if ssn is None else ssn, N if sym is None else sym,
+                               ws, ws_len, None)
+
+
+def test_rejects_m_above_16(native):
+    assert call_linear(native, M=17) == native.LI4_ERR_INVALID_ARG
+    assert "M=17" in native.last_error()
+
+
+def test_rejects_k_not_multiple_of_128(native):
+    assert call_linear(native, K=96, group=32) == native.LI4_ERR_UNSUPPORTED
+
+
+def test_rejects_bad_group(native):
+    assert call_linear(native, K=384, group=96) == native.LI4_ERR_UNSUPPORTED
+    assert call_linear(native, K=256, group=16) == native.LI4_ERR_UNSUPPORTED
+
+
+def test_rejects_null_pointers(native):
+    assert call_linear(native, x=0) == native.LI4_ERR_INVALID_ARG
+
+
+def test_rejects_short_strides(native):
+    assert call_linear(native, sxm=100) == native.LI4_ERR_INVALID_ARG
+
+
+def test_rejects_unaligned_packed(native):
+    assert call_linear(native, packed=17) == native.LI4_ERR_ALIGNMENT
+    assert call_linear(native, spn=136) == native.LI4_ERR_ALIGNMENT  # row stride not a multiple of 16
+
+
+def test_rejects_missing_workspace(native):
+    # N=512, K=2048 on 148 SMs needs split-K (32 row tiles of 16 rows)
+    lib = native.lib()
+    need = lib.li4_int4_linear_workspace_bytes(1, 512, 2048, 128, 148)
+    assert need > 0
+    assert lib.li4_int4_linear_workspace_bytes(1, 128256, 2048, 128, 148) == 0  # enough row tiles, no split
+    rc = call_linear(native, M=1, N=512, K=2048)
+    # the SM count of a machine without a GPU falls back to 148, so split-K is chosen
+    assert rc == native.LI4_ERR_WORKSPACE
+
+
+def test_workspace_bytes_invalid_shape_is_zero(native):
+    assert native.lib().li4_int4_linear_workspace_bytes(17, 64, 256, 128, 148) == 0
+
+
+def test_quantize_dequantize_validate(native):
+    lib = native.lib()
+    assert lib.li4_quantize(16, 0, 16, 16, 16, 4, 100, 128, 100, None) == native.LI4_ERR_INVALID_ARG
+    assert lib.li4_quantize(16, 9, 16, 16, 16, 4, 256, 128, 256, None) == native.LI4_ERR_INVALID_ARG
+    assert lib.li4_dequantize(0, 16, 16, 16, 4, 256, 128, 128, 2, 256, None) == native.LI4_ERR_INVALID_ARG
+    assert lib.li4_quantize(16, 0, 16, 16, 16, 0, 256, 128, 256, None) == native.LI4_OK  # empty: no launch

@@ -1,0 +1,272 @@
+"""Fused INT4 GEMV on the GPU against the oracle and the reference's outputs.
+
+The acceptance bound is the one the reference's kernel is held to:
+    max|y - y_ref| <= 2e-3 * max|y_ref|
+where y_ref is the reference's dequantize-to-fp16 + matmul (golden
+fixtures) or the oracle's restatement of it.  Every call goes through the
+C-ABI (li4_int4_linear / li4_int4_linear_ex) from the int4_linear mirror.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+LLAMA_SHAPES = [  # (name, N = out_features, K = in_features)
+    ("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
+    ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192), ("lm_head", 128256, 2048),
+]
+KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2}
+
+
+@pytest.fixture(scope="module")
+def g(cuda_device):
+    from llama import int4_gemv, _native
+
+    return int4_gemv, _native
+
+
+def make_problem(N, K, M, group=128, seed=0, device="cuda", x_scale=1.0):
+    gen = torch.Generator().manual_seed(seed)
+    w = (torch.randn(N, K, generator=gen) * 0.02).half()
+    x = (torch.randn(M, K, generator=gen) * x_scale).half()
+    packed, scale, zero = oracle.quantize(w.numpy(), group)
+    dev = torch.device(device)
+    return (x.to(dev), torch.from_numpy(packed).to(dev), torch.from_numpy(scale).to(dev),
+            torch.from_numpy(zero).to(dev), (x.numpy(), packed, scale, zero))
+
+
+def check_close(y_gpu: torch.Tensor, y_ref: np.ndarray, y32: np.ndarray = None):
+    y = y_gpu.float().cpu().numpy()
+    ref = y_ref.astype(np.float32)
+    err = np.abs(y - ref).max()
+    tol = oracle.tolerance(y_ref)
+    assert err <= tol, f"max|y - y_ref| = {err:.3e} > {tol:.3e}"
+    if y32 is not None:  # fp32 accumulation: within a couple of fp16 ulps of the exact sums
+        ulp = np.maximum(np.abs(y32), 6.1e-5) * 2.0 ** -10
+        assert np.all(np.abs(y - y32) <= 2.0 * ulp + 1e-4 * np.abs(y32).max()), "accumulation error too large"
+
+
+@pytest.mark.parametrize("kernel", list(KERNELS))
+@pytest.mark.parametrize("case", cases.GEMV_CASES, ids=[c[0] for c in cases.GEMV_CASES])
+def test_golden_cases(case, kernel, golden, g, cuda_device):
+    int4_gemv, _ = g
+    meta, arr = golden
+    name, N, K, M, group = case[:5]
+    if kernel == "cuda_core" and M > 8:
+        pytest.skip("CUDA-core family takes M <= 8")
+    w, x = cases.make_gemv_inputs(case)
+    packed, scale, zero = oracle.quantize(w.numpy(), group)
+    dev = cuda_device
+    xg = x.to(dev)
+    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    int4_gemv.int4_linear_out(xg, torch.from_numpy(packed).to(dev), torch.from_numpy(scale).to(dev),
+                              torch.from_numpy(zero).to(dev), y, group, kernel=KERNELS[kernel])
+    check_close(y, arr[f"gemv/{name}/y"], arr[f"gemv/{name}/y32"])
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("shape", LLAMA_SHAPES, ids=[s[0] for s in LLAMA_SHAPES])
+def test_llama_shapes(shape, M, g, cuda_device):
+    int4_gemv, _ = g
+    name, N, K = shape
+    x, p, s, z, host = make_problem(N, K, M, seed=sum(map(ord, name)) + M)
+    y_ref, y32 = oracle.linear(*host)
+    for kernel in ("auto", "cuda_core", "mma"):
+        if kernel == "cuda_core" and M > 8:
+            continue
+        y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+        int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS[kernel])
+        check_close(y, y_ref, y32)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 11, 16])
+@pytest.mark.parametrize("N,K", [(1, 128), (7, 256), (16, 128), (31, 1152), (100, 2048), (1000, 512), (5000, 4096),
+                                 (257, 8192)])
+def test_shape_sweep(N, K, M, g, cuda_device):
+    int4_gemv, _ = g
+    x, p, s, z, host = make_problem(N, K, M, seed=N * 31 + K + M)
+    y_ref, y32 = oracle.linear(*host)
+    y = int4_gemv.int4_linear(x, p, s, z, 128)
+    check_close(y, y_ref, y32)
+
+
+@pytest.mark.parametrize("group", [32, 64, 256, 512])
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_group_sizes(group, M, g, cuda_device):
+    int4_gemv, _ = g
+    x, p, s, z, host = make_problem(300, 2048, M, group=group, seed=group + M)
+    y_ref, y32 = oracle.linear(*host, group_size=group)
+    for kernel in ("auto", "cuda_core", "mma"):
+        if kernel == "cuda_core" and M > 8:
+            continue
+        y = torch.empty(M, 300, dtype=torch.float16, device=cuda_device)
+        int4_gemv.int4_linear_out(x, p, s, z, y, group, kernel=KERNELS[kernel])
+        check_close(y, y_ref, y32)
+
+
+@pytest.mark.parametrize("kernel", ["cuda_core", "mma"])
+@pytest.mark.parametrize("rows", [16, 32])
+@pytest.mark.parametrize("split", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("max_ctas", [0, 1, 5])
+def test_forced_launch_shapes(kernel, rows, split, max_ctas, g, cuda_device):
+    """Every split-K / tile / persistent-grid combination gives the same answer, deterministically."""
+    int4_gemv, _ = g
+    M, N, K = 3, 700, 2048
+    x, p, s, z, host = make_problem(N, K, M, seed=99)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS[kernel], rows_per_cta=rows, split=split,
+                              max_ctas=max_ctas)
+    check_close(y, y_ref, y32)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS[kernel], rows_per_cta=rows, split=split,
+                              max_ctas=max_ctas)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "split-K result is not deterministic"
+
+
+def test_split_counters_reset_across_launches(g, cuda_device):
+    """The arrival counters are left at zero: 40 back-to-back split-K launches all reduce correctly."""
+    int4_gemv, _ = g
+    M, N, K = 1, 512, 2048  # k/v shape: split-K on a 148-SM part
+    x, p, s, z, host = make_problem(N, K, M, seed=3)
+    xs = [(torch.randn(M, K, generator=torch.Generator().manual_seed(i))).half() for i in range(40)]
+    outs = [int4_gemv.int4_linear(xi.to(cuda_device), p, s, z, 128) for xi in xs]
+    torch.cuda.synchronize()
+    for xi, yi in zip(xs, outs):
+        y_ref, y32 = oracle.linear(xi.numpy(), *host[1:])
+        check_close(yi, y_ref, y32)
+
+
+def test_leading_dims_and_noncontiguous_x(g, cuda_device):
+    int4_gemv, _ = g
+    N, K = 96, 512
+    x, p, s, z, host = make_problem(N, K, 6, seed=4)
+    x3 = x.reshape(2, 3, K)
+    y = int4_gemv.int4_linear(x3, p, s, z, 128)
+    assert y.shape == (2, 3, N)
+    y_ref, _ = oracle.linear(*host)
+    check_close(y.reshape(6, N), y_ref)
+    wide = torch.zeros(6, 2 * K, dtype=torch.float16, device=cuda_device)
+    wide[:, :K] = x
+    y2 = int4_gemv.int4_linear(wide[:, :K], p, s, z, 128)  # row stride 2K, made contiguous by the wrapper
+    check_close(y2, y_ref)
+
+
+def test_strided_operands_through_c_abi(g, cuda_device):
+    """x, packed, scale/zero and y with row strides wider than their rows (no copies)."""
+    int4_gemv, native = g
+    M, N, K = 4, 200, 1024
+    x, p, s, z, host = make_problem(N, K, M, seed=5)
+    y_ref, y32 = oracle.linear(*host)
+    dev = cuda_device
+    xw = torch.zeros(M, K + 64, dtype=torch.float16, device=dev)
+    xw[:, :K] = x
+    pw = torch.zeros(N, K // 2 + 48, dtype=torch.uint8, device=dev)
+    pw[:, :K // 2] = p
+    sw = torch.zeros(N, K // 128 + 3, dtype=torch.float16, device=dev)
+    zw = torch.zeros_like(sw)
+    sw[:, :K // 128] = s
+    zw[:, :K // 128] = z
+    yw = torch.full((M, N + 40), 7.0, dtype=torch.float16, device=dev)
+    lib = native.lib()
+    ws = native.workspace(dev, lib.li4_int4_linear_workspace_bytes(M, N, K, 128, 0))
+    for kernel in (1, 2):
+        rc = lib.li4_int4_linear_ex(xw.data_ptr(), pw.data_ptr(), sw.data_ptr(), zw.data_ptr(), yw.data_ptr(),
+                                    M, N, K, 128, xw.stride(0), pw.stride(0), sw.stride(0), yw.stride(0),
+                                    ws.data_ptr(), ws.numel(), native.stream_ptr(dev), kernel, 0, 0, 0)
+        native.check(rc)
+        check_close(yw[:, :N], y_ref, y32)
+        assert torch.all(yw[:, N:] == 7.0), "wrote past the row"
+
+
+def test_misaligned_packed_is_rejected(g, cuda_device):
+    int4_gemv, native = g
+    x, p, s, z, _ = make_problem(64, 256, 1, seed=6)
+    buf = torch.zeros(p.numel() + 16, dtype=torch.uint8, device=cuda_device)
+    pv = buf[1:1 + p.numel()].view(p.shape)
+    pv.copy_(p)
+    with pytest.raises(native.Li4Error) as e:
+        int4_gemv.int4_linear(x, pv, s, z, 128)
+    assert e.value.status == native.LI4_ERR_ALIGNMENT
+
+
+def test_reference_asserts(g, cuda_device):
+    int4_gemv, _ = g
+    x, p, s, z, _ = make_problem(64, 256, 17, seed=7)
+    with pytest.raises(AssertionError):
+        int4_gemv.int4_linear(x, p, s, z, 128)  # M > MAX_M
+    with pytest.raises(AssertionError):
+        int4_gemv.int4_linear(x[:1].float(), p, s, z, 128)  # not fp16
+    with pytest.raises(AssertionError):
+        int4_gemv.int4_linear(x[:1], p, s, z, 96)  # K % group_size
+
+
+def test_empty_m(g, cuda_device):
+    int4_gemv, _ = g
+    x, p, s, z, _ = make_problem(64, 256, 1, seed=8)
+    y = int4_gemv.int4_linear(x[:0], p, s, z, 128)
+    assert y.shape == (0, 64)
+
+
+def test_cuda_graph_capture_and_replay(g, cuda_device):
+    """Static-buffer capture of several launches (one split-K) replays like eager."""
+    int4_gemv, _ = g
+    probs = [make_problem(N, K, M, seed=10 + i) for i, (N, K, M) in enumerate([(512, 2048, 1), (2048, 8192, 2),
+                                                                               (8192, 2048, 16)])]
+    xs = [pr[0].clone() for pr in probs]
+    ys = [torch.empty(pr[0].shape[0], pr[1].shape[0], dtype=torch.float16, device=cuda_device) for pr in probs]
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for xi, (_, p, s, z, _), yi in zip(xs, probs, ys):  # warm-up sizes the workspace
+            int4_gemv.int4_linear_out(xi, p, s, z, yi, 128)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for xi, (_, p, s, z, _), yi in zip(xs, probs, ys):
+            int4_gemv.int4_linear_out(xi, p, s, z, yi, 128)
+    for rep in range(3):
+        for i, xi in enumerate(xs):
+            xi.copy_(torch.randn(xi.shape, generator=torch.Generator().manual_seed(100 * rep + i)).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        for xi, (_, p, s, z, host), yi in zip(xs, probs, ys):
+            y_ref, y32 = oracle.linear(xi.cpu().numpy(), *host[1:])
+            check_close(yi, y_ref, y32)
+
+
+def test_quantized_linear_module(cuda_device):
+    from llama import quantize
+
+    lin = torch.nn.Linear(1024, 384, bias=False).half().to(cuda_device)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(384, 1024, generator=torch.Generator().manual_seed(9)).half() * 0.02)
+    ql = quantize.QuantizedLinear.from_linear(lin, 128).to(cuda_device)
+    assert set(ql.state_dict()) == {"packed_weight", "scale", "zero_point"}
+    x = torch.randn(1, 3, 1024, generator=torch.Generator().manual_seed(10)).half().to(cuda_device)
+    old = quantize.DEQUANT_IMPL
+    try:
+        quantize.set_dequant_impl("v4")
+        y4 = ql(x)
+        quantize.set_dequant_impl("v1")
+        y1 = ql(x)
+    finally:
+        quantize.set_dequant_impl(old)
+    packed, scale, zero = (t.cpu().numpy() for t in (ql.packed_weight, ql.scale, ql.zero_point))
+    y_ref, y32 = oracle.linear(x.reshape(3, 1024).cpu().numpy(), packed, scale, zero)
+    check_close(y4.reshape(3, 384), y_ref, y32)
+    check_close(y1.reshape(3, 384), y_ref)
+
+
+def test_int4_linear_fn_is_path_loaded_and_patchable(cuda_device):
+    from llama import quantize
+
+    fn = quantize.int4_linear_fn()
+    assert callable(fn) and fn.__name__ == "int4_linear"
+    assert quantize.int4_linear_fn() is fn
