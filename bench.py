@@ -96,13 +96,13 @@ class ClockSampler:
         try:
             import pynvml
 
+            props = torch.cuda.get_device_properties(device)
+            ids = (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+            if not all(isinstance(v, int) for v in ids):  # NVML takes the id as a C string only
+                raise TypeError(f"unexpected PCI id fields {ids!r}")
+            bus_id = "%08x:%02x:%02x.0" % ids
             pynvml.nvmlInit()
-            bus = torch.cuda.get_device_properties(device).pci_bus_id if hasattr(
-                torch.cuda.get_device_properties(device), "pci_bus_id") else None
-            if bus is None:
-                props = torch.cuda.get_device_properties(device)
-                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
-            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus_id)
             self.nvml = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception as e:  # noqa: BLE001 -- clocks are reported as unavailable, never guessed
@@ -113,7 +113,9 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.reasons |= reasons(self.h)
             except Exception:  # noqa: BLE001
                 pass
             self._stop.wait(self.period)
@@ -426,15 +428,25 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+def log(msg: str) -> None:
+    """Phase markers on stderr (the JSON line alone goes to stdout)."""
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def run_gpu(a):
     world, rank, local = dist_setup(a.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    log("building the quantized weights of the 113-GEMV stream")
     stream = Stream(dev, a.m)
+    log("capturing the step graph")
     stream.capture()
+    log("clock sampler")
     sampler = ClockSampler(dev)
+    log(f"timing {a.steps} graph replays")
     ms = time_graph(stream, a.steps, a.warmup, world, sampler)
     ms_max = max_over_ranks(ms, world, dev)
+    log("e2e timing")
     e2e_steps = max(3, min(a.steps, 2000))
     e2e_ms, h2d, d2h = time_e2e(stream, e2e_steps, max(3, a.warmup), world)
     e2e_ms = max_over_ranks(e2e_ms, world, dev)
@@ -442,11 +454,13 @@ def run_gpu(a):
     eager_ms, _, _ = time_e2e(stream, eager_steps, 3, world, eager=True)
     eager_ms = max_over_ranks(eager_ms, world, dev)
 
+    log("per-shape isolated timing")
     per_shape = per_shape_isolated(stream) if (rank == 0 and not a.no_per_shape) else None
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         from oracle import oracle
 
+        log("CPU baseline (oracle port of the reference path)")
         threads = cpu_threads()
         oracle.set_threads(threads)
         cs = CpuStream(a.m)

@@ -58,12 +58,18 @@ int li4_version(void);
 /* Message describing the last failed call on this host thread ("" if none). */
 const char* li4_last_error(void);
 
+/* Split-K workspace layout: the first LI4_WORKSPACE_COUNTER_BYTES bytes hold
+ * per-row-tile arrival counters (never used for anything else), fp32 partial
+ * sums follow. */
+#define LI4_WORKSPACE_COUNTER_BYTES 65536
+
 /* Bytes of split-K workspace li4_int4_linear needs for this problem on a
- * device with `sm_count` SMs (0 = query the current device).  The workspace
- * must be zero-filled once when it is allocated; every launch leaves its
- * arrival counters at zero again, so it can be reused by later launches on
- * the same stream (and inside CUDA graphs) without clearing.  Two launches
- * that may run concurrently must not share a workspace. */
+ * device with `sm_count` SMs (0 = query the current device); 0 when the
+ * launch needs none.  The workspace must be zero-filled once when it is
+ * allocated; every launch leaves its arrival counters at zero again, so it can
+ * be reused by later launches of any shape on the same stream (and inside
+ * CUDA graphs) without clearing.  Two launches that may run concurrently must
+ * not share a workspace. */
 size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count);
 
 /* y[M, N] (fp16, row stride stride_ym elements) = x[M, K] (fp16, row stride

@@ -560,7 +560,14 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   p->smem = round_up((size_t)p->ks_per_split * nt * m8 * 256, 128) + (size_t)kWarps * rows * cols * sizeof(float);
 
   if (split > 1) {
-    p->ws_counters = round_up((size_t)p->n_tiles * sizeof(unsigned), 256);
+    // Counters live in a fixed region at the start of the workspace that no
+    // launch ever uses for partial sums, so they stay zero between launches
+    // of different shapes sharing the workspace.
+    if ((size_t)p->n_tiles * sizeof(unsigned) > LI4_WORKSPACE_COUNTER_BYTES)
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: N=%lld needs %d split-K row tiles, more than the %d "
+                       "arrival counters of the workspace", (long long)N, p->n_tiles,
+                       (int)(LI4_WORKSPACE_COUNTER_BYTES / sizeof(unsigned)));
+    p->ws_counters = LI4_WORKSPACE_COUNTER_BYTES;
     p->ws_bytes = p->ws_counters + (size_t)split * M * N * sizeof(float);
   } else {
     p->ws_counters = 0;

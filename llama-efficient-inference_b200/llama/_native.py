@@ -23,6 +23,7 @@ LI4_ERR_UNSUPPORTED = 4
 LI4_ERR_CUDA = 5
 
 LI4_F16, LI4_BF16, LI4_F32 = 0, 1, 2
+WORKSPACE_COUNTER_BYTES = 65536  # LI4_WORKSPACE_COUNTER_BYTES
 KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA = 0, 1, 2
 
 _P = ctypes.c_void_p

@@ -84,8 +84,8 @@ def int4_linear_out(x2: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor,
     ws_ptr, ws_len = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     stream = _native.stream_ptr(dev)
     if kernel or rows_per_cta or split or max_ctas:
-        if split > 1:  # counters for up to ceil(N/16) row tiles + split fp32 partials of [M, N]
-            need = ((N + 15) // 16 * 4 + 255) // 256 * 256 + split * M * N * 4
+        if split > 1:  # the fixed counter region + split fp32 partials of [M, N]
+            need = _native.WORKSPACE_COUNTER_BYTES + split * M * N * 4
             ws = _native.workspace(dev, max(need, nbytes))
             ws_ptr, ws_len = ws.data_ptr(), ws.numel()
         rc = lib.li4_int4_linear_ex(x2.data_ptr(), packed.data_ptr(), scale.data_ptr(), zp.data_ptr(), y.data_ptr(),

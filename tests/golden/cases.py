@@ -98,3 +98,49 @@ def make_quant_input(case) -> torch.Tensor:
     if mult == "edge":
         return _edge_weights(N, K, gen)
     return (torch.randn(N, K, generator=gen) * mult).half()
+
+
+# ---------------------------------------------------------------------------
+# Tiny Llama for model-level golden vectors (same architecture, small sizes;
+# every K is a multiple of 128 so the INT4 kernels take it).
+# ---------------------------------------------------------------------------
+TINY_MODEL = dict(dim=256, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=1000, multiple_of=64,
+                  ffn_dim_multiplier=1.5, norm_eps=1e-5, rope_theta=500000.0, max_batch_size=2, max_seq_len=24)
+TINY_PROMPT_LEN = 8
+TINY_DECODE_STEPS = 6
+TINY_SEED = 77
+
+
+def tiny_state_dict(args: dict, seed: int = TINY_SEED) -> dict:
+    """Seeded fp16 weights keyed like the reference's Llama state dict."""
+    gen = torch.Generator().manual_seed(seed)
+    dim, L = args["dim"], args["n_layers"]
+    hd = dim // args["n_heads"]
+    kv = args["n_kv_heads"] * hd
+    hidden = int(2 * 4 * dim / 3)
+    hidden = int(args["ffn_dim_multiplier"] * hidden)
+    hidden = args["multiple_of"] * ((hidden + args["multiple_of"] - 1) // args["multiple_of"])
+
+    def randn(*shape, std):
+        return (torch.randn(*shape, generator=gen) * std).half()
+
+    sd = {"tok_embeddings.weight": randn(args["vocab_size"], dim, std=1.0)}
+    for i in range(L):
+        p = f"layers.{i}."
+        sd[p + "attention.wq.weight"] = randn(dim, dim, std=0.05)
+        sd[p + "attention.wk.weight"] = randn(kv, dim, std=0.05)
+        sd[p + "attention.wv.weight"] = randn(kv, dim, std=0.05)
+        sd[p + "attention.wo.weight"] = randn(dim, dim, std=0.05)
+        sd[p + "feed_forward.w1.weight"] = randn(hidden, dim, std=0.05)
+        sd[p + "feed_forward.w2.weight"] = randn(dim, hidden, std=0.05)
+        sd[p + "feed_forward.w3.weight"] = randn(hidden, dim, std=0.05)
+        sd[p + "attention_norm.weight"] = (1.0 + 0.1 * torch.randn(dim, generator=gen)).half()
+        sd[p + "ffn_norm.weight"] = (1.0 + 0.1 * torch.randn(dim, generator=gen)).half()
+    sd["norm.weight"] = (1.0 + 0.1 * torch.randn(dim, generator=gen)).half()
+    sd["output.weight"] = randn(args["vocab_size"], dim, std=0.05)
+    return sd
+
+
+def tiny_prompt(args: dict, seed: int = TINY_SEED + 1) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(0, args["vocab_size"], (args["max_batch_size"], TINY_PROMPT_LEN), generator=gen)

@@ -36,6 +36,63 @@ def load_reference_quantize(ref_root: str):
     return mod
 
 
+def load_reference_model(ref_root: str):
+    """llama/model.py by path under a package stub (no tokenizer import), .cuda() as identity."""
+    import types
+
+    pkg = types.ModuleType("llama")
+    pkg.__path__ = [os.path.join(ref_root, "llama")]
+    sys.modules["llama"] = pkg
+    importlib.import_module("llama.generation")
+    return importlib.import_module("llama.model")
+
+
+@torch.inference_mode()
+def run_reference_model(model, prompt, steps):
+    """Prefill logits, then greedy decode steps as the reference's bench.py:154-161 does."""
+    logits = [model(prompt, 0)]
+    nxt = logits[0][:, -1].argmax(-1, keepdim=True)
+    toks = [nxt]
+    for i in range(steps):
+        lg = model(nxt, prompt.shape[1] + i)
+        logits.append(lg)
+        nxt = lg[:, -1].argmax(-1, keepdim=True)
+        toks.append(nxt)
+    return logits, torch.cat(toks, 1)
+
+
+def model_golden(ref_root, ref_quantize, arrays, meta):
+    rm = load_reference_model(ref_root)
+    saved_cuda = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *a, **k: self  # Attention.__init__ allocates its cache with .cuda()
+    try:
+        args = rm.ModelArgs(**cases.TINY_MODEL)
+        sd = cases.tiny_state_dict(cases.TINY_MODEL)
+        prompt = cases.tiny_prompt(cases.TINY_MODEL)
+        torch.set_default_dtype(torch.float16)
+        model = rm.Llama(args)
+        torch.set_default_dtype(torch.float32)
+        model.load_state_dict(sd, strict=True)
+        model.eval()
+        for tag in ("fp16", "int4"):
+            if tag == "int4":
+                ref_quantize.quantize_model(model, 128)  # DEQUANT_IMPL "v1": dequantize + F.linear
+            for layer in model.layers:  # fresh caches for each run
+                layer.attention.cache_k.zero_()
+                layer.attention.cache_v.zero_()
+            logits, toks = run_reference_model(model, prompt, cases.TINY_DECODE_STEPS)
+            arrays[f"model/{tag}/prefill_logits"] = logits[0].numpy()
+            arrays[f"model/{tag}/decode_logits"] = torch.cat(logits[1:], 1).numpy()
+            arrays[f"model/{tag}/tokens"] = toks.numpy()
+            print(f"tiny model {tag}: greedy tokens {toks.tolist()}")
+        arrays["model/prompt"] = prompt.numpy()
+        meta["model"] = {"args": cases.TINY_MODEL, "steps": cases.TINY_DECODE_STEPS,
+                         "note": "reference llama/model.py on the CPU, fp16 weights; int4 = quantize_model + v1"}
+    finally:
+        torch.Tensor.cuda = saved_cuda
+        torch.set_default_dtype(torch.float32)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -83,6 +140,8 @@ def main() -> None:
                 arrays[f"gemv/{name}/{key}"] = t.numpy()
         print(f"{name:>10} N={N:>5} K={K:>5} M={M:>2} g={group:>3} max|y|={info['max_abs_y']:.3f} "
               f"fp16-vs-fp32 {info['ref_fp16_vs_fp32_max_err']:.2e}")
+
+    model_golden(a.reference, ref, arrays, meta)
 
     np.savez_compressed(os.path.join(a.out, "golden.npz"), **arrays)
     with open(os.path.join(a.out, "golden.json"), "w") as f:

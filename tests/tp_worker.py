@@ -1,0 +1,77 @@
+"""One rank of the CPU tensor-parallel tests (launched by tests/test_tp_cpu.py).
+
+modes:
+  parity     shard the tiny Llama over the gloo group, compare prefill and decode_step
+             logits with the unsharded model on every rank; prints one JSON line
+  dead_peer  rank 1 leaves right after joining; rank 0's next collective must fail
+             with an error (not hang); prints one JSON line from rank 0
+"""
+import datetime
+import json
+import os
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+sys.path[:0] = [REPO, os.path.join(REPO, "llama-efficient-inference_b200"), os.path.join(HERE, "golden")]
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def parity():
+    import cases
+    from llama.model import Llama, ModelArgs
+    from llama.tp import shard_model
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    args = ModelArgs(**cases.TINY_MODEL)
+    sd = {k: v.float() for k, v in cases.tiny_state_dict(cases.TINY_MODEL).items()}
+    full = Llama(args)
+    full.load_state_dict(sd)
+    part = Llama(args)
+    part.load_state_dict(sd)
+    shard_model(part)
+    prompt = cases.tiny_prompt(cases.TINY_MODEL)
+    worst = 0.0
+    with torch.no_grad():
+        a, b = full(prompt, 0), part(prompt, 0)
+        worst = max(worst, float((a - b).abs().max() / a.abs().max()))
+        nxt = a[:, -1].argmax(-1, keepdim=True)
+        pos = torch.tensor([prompt.shape[1]], dtype=torch.long)
+        for _ in range(3):
+            la, lb = full.decode_step(nxt, pos), part.decode_step(nxt, pos)
+            worst = max(worst, float((la - lb).abs().max() / la.abs().max()))
+            nxt = la[:, -1].argmax(-1, keepdim=True)
+            pos += 1
+    local_heads = part.layers[0].attention.n_local_heads
+    print(json.dumps({"rank": rank, "world": world, "max_rel_err": worst, "local_heads": local_heads,
+                      "wq_rows": part.layers[0].attention.wq.weight.shape[0],
+                      "w2_cols": part.layers[0].feed_forward.w2.weight.shape[1]}), flush=True)
+
+
+def dead_peer():
+    rank = dist.get_rank()
+    if rank == 1:
+        os._exit(0)  # leaves between steps, with nothing in flight
+    time.sleep(1.0)
+    t0 = time.time()
+    try:
+        t = torch.ones(4)
+        dist.all_reduce(t)
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 -- the failure is the expected outcome
+        outcome = f"error: {type(e).__name__}"
+    print(json.dumps({"rank": rank, "outcome": outcome, "seconds": round(time.time() - t0, 2)}), flush=True)
+
+
+if __name__ == "__main__":
+    mode = sys.argv[1]
+    timeout = datetime.timedelta(seconds=float(os.environ.get("TP_TEST_TIMEOUT", "60")))
+    dist.init_process_group("gloo", timeout=timeout)
+    {"parity": parity, "dead_peer": dead_peer}[mode]()
+    if mode == "parity":
+        dist.barrier()
+        dist.destroy_process_group()
+    os._exit(0)
