@@ -99,6 +99,30 @@ int li4_int4_linear_ex(const void* x, const void* packed, const void* scale, con
                        void* workspace, size_t workspace_bytes, void* stream,
                        int kernel, int rows_per_cta, int split, int max_ctas);
 
+/* Size of the static device scratch behind li4_int4_linear_noalloc. */
+#define LI4_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* li4_int4_linear for callers that cannot allocate device memory: code running
+ * while a CUDA graph is captured, runtimes whose allocator refuses new device
+ * allocations after warm-up (cudaMalloc may synchronise the device), and
+ * hosts that bind only this C ABI and own no device allocator.  The caller
+ * still passes x and y; the split-K partial sums and arrival counters live in
+ * a static device array of LI4_NOALLOC_SCRATCH_BYTES (4 MiB) that every GPU
+ * loading the library holds until the process exits.  This function calls no
+ * cudaMalloc / cudaFree; it clears the counters it uses with cudaMemsetAsync
+ * on `stream` before each launch.  Problems whose split-K scratch would exceed
+ * the array are rejected with LI4_ERR_WORKSPACE (for example M=16, N=32768,
+ * K=8192).  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, which may load the module): make that first call
+ * before any stream capture.  All calls share the array, so calls that may
+ * overlap on the GPU (different streams) race; keep them on one stream.
+ * No counterpart in the reference: its int4_linear allocates its split-K
+ * buffer with torch.zeros on every call. */
+int li4_int4_linear_noalloc(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                            int64_t M, int64_t N, int64_t K, int64_t group_size,
+                            int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
+                            void* stream);
+
 /* w16[N, K] (fp16, row stride stride_wn elements) = dequantized weights,
  * bit-identical to the reference's fp32 (q - zero) * scale rounded to fp16.
  * Replaces: QuantizedLinear.dequantize_packed (llama/quantize.py:78-104) and

@@ -756,3 +756,72 @@ extern "C" int li4_int4_linear_ex(const void* x, const void* packed, const void*
   return li4::int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn,
                                stride_ym, workspace, workspace_bytes, stream, kernel, rows_per_cta, split, max_ctas);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot hand this library a workspace: code that runs while a
+// CUDA graph is being captured or under an allocator that forbids new device
+// allocations after warm-up (cudaMalloc can synchronise the device), and hosts
+// that bind only this C ABI and own no device allocator of their own.  For
+// them the split-K partial sums and arrival counters live in one static device
+// array of this translation unit, sized once for the decode shapes.  The
+// array exists on every GPU that loads the library, for the life of the
+// process.  All calls share it, so two calls that may overlap on the GPU (for
+// example on two streams) race; keep such calls on one stream.
+// ---------------------------------------------------------------------------
+namespace li4 {
+
+constexpr size_t kNoAllocScratchBytes = LI4_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// symbol is only a stand-in for the array, so the address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* by_device[64] = {};
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "int4_linear_noalloc: cudaGetDevice");
+  if (rc != LI4_OK) return rc;
+  if (dev < 0 || dev >= 64) return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_noalloc: device ordinal %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (by_device[dev] == nullptr) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "int4_linear_noalloc: cudaGetSymbolAddress");
+    if (rc != LI4_OK) return rc;
+    by_device[dev] = p;
+  }
+  *out = by_device[dev];
+  return LI4_OK;
+}
+
+}  // namespace li4
+
+extern "C" int li4_int4_linear_noalloc(const void* x, const void* packed, const void* scale, const void* zero,
+                                       void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                       int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
+                                       void* stream) {
+  using namespace li4;
+  Plan p = {};
+  int rc = make_plan(M, N, K, group_size, current_sm_count(), LI4_KERNEL_AUTO, 0, 0, 0, &p);
+  if (rc != LI4_OK) return rc;
+  void* scratch = nullptr;
+  if (p.ws_bytes > 0) {
+    if (p.ws_bytes > kNoAllocScratchBytes)
+      return set_error(LI4_ERR_WORKSPACE, "int4_linear_noalloc: M=%lld N=%lld K=%lld needs %zu bytes of split-K "
+                       "scratch, more than the %zu-byte static scratch of this entry point; call li4_int4_linear "
+                       "with a workspace instead", (long long)M, (long long)N, (long long)K, p.ws_bytes,
+                       kNoAllocScratchBytes);
+    rc = noalloc_scratch(&scratch);
+    if (rc != LI4_OK) return rc;
+    // The counters must start at zero: clear the ones this launch uses (the
+    // array keeps whatever the previous call left in it).
+    rc = check_cuda(cudaMemsetAsync(scratch, 0, (size_t)p.n_tiles * sizeof(unsigned),
+                                    static_cast<cudaStream_t>(stream)),
+                    "int4_linear_noalloc: clearing the arrival counters");
+    if (rc != LI4_OK) return rc;
+  }
+  return int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn, stride_ym,
+                          scratch, scratch ? kNoAllocScratchBytes : 0, stream, LI4_KERNEL_AUTO, 0, 0, 0);
+}

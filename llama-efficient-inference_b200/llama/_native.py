@@ -39,6 +39,7 @@ SIGNATURES = {
     "li4_int4_linear": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "li4_int4_linear_ex": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
                                   _INT, _INT, _INT, _INT]),
+    "li4_int4_linear_noalloc": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_dequantize": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_quantize": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
 }
