@@ -428,6 +428,77 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Decode: Llama-3.2-1B, all 113 linears INT4, one CUDA graph per step
+# ---------------------------------------------------------------------------
+def build_decode_model(device, bs: int, max_seq_len: int, seed: int = 0):
+    """Random-init Llama-3.2-1B (N(0, 0.02) weights, output tied to the embeddings), quantized INT4 g128."""
+    from llama import quantize
+    from llama.model import Llama, ModelArgs
+
+    args = ModelArgs(max_batch_size=bs, max_seq_len=max_seq_len)
+    torch.manual_seed(seed)
+    torch.set_default_dtype(torch.float16)
+    try:
+        with torch.device(device):
+            model = Llama(args)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    with torch.no_grad():
+        for name, prm in model.named_parameters():
+            if name.endswith("norm.weight"):
+                prm.fill_(1.0)
+            else:
+                prm.normal_(0.0, 0.02)
+        model.output.weight = model.tok_embeddings.weight  # tied, as in the released checkpoint
+    model.eval()
+    quantize.quantize_model(model, GROUP)
+    quantize.set_dequant_impl("v4")
+    return model
+
+
+def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int):
+    """Prefill + `gen` greedy decode steps replayed from one graph; timings are the max over ranks."""
+    from llama.generation import DecodeGraph
+
+    model = build_decode_model(device, bs, prompt_len + gen)
+    if world > 1:
+        from llama.tp import shard_model
+
+        shard_model(model)
+    torch.cuda.synchronize(device)
+    graph = DecodeGraph(model, bs)
+    gen_t = torch.Generator(device=device).manual_seed(1)
+    tokens = torch.randint(0, model.params.vocab_size, (bs, prompt_len), generator=gen_t, device=device)
+    steps, prefills, e2es = [], [], []
+    for rep in range(reps + 1):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(gen + 1)]
+        barrier(world, device)
+        ev[0].record()
+        with torch.no_grad():
+            graph.start(tokens)
+        ev[1].record()
+        for i in range(gen - 1):
+            graph.replay()
+            ev[i + 2].record()
+        torch.cuda.synchronize(device)
+        if rep == 0:
+            continue  # warm-up
+        prefills.append(ev[0].elapsed_time(ev[1]))
+        steps += [ev[i].elapsed_time(ev[i + 1]) for i in range(1, gen)]
+        e2es.append(ev[0].elapsed_time(ev[gen]))
+    step_ms = max_over_ranks(statistics.median(steps), world, device)
+    e2e_ms = max_over_ranks(statistics.median(e2es), world, device)
+    prefill_ms = max_over_ranks(statistics.median(prefills), world, device)
+    q = statistics.quantiles(steps, n=10)
+    del graph, model
+    torch.cuda.empty_cache()
+    return {"bs": bs, "prompt": prompt_len, "generated": gen, "tp": world, "reps": reps,
+            "decode_ms_per_step": round(step_ms, 4), "decode_p10_ms": round(q[0], 4), "decode_p90_ms": round(q[-1], 4),
+            "decode_tok_s": round(bs / (step_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 3),
+            "e2e_tok_s": round(bs * gen / (e2e_ms * 1e-3), 1)}
+
+
 def log(msg: str) -> None:
     """Phase markers on stderr (the JSON line alone goes to stdout)."""
     print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
@@ -454,6 +525,11 @@ def run_gpu(a):
     eager_ms, _, _ = time_e2e(stream, eager_steps, 3, world, eager=True)
     eager_ms = max_over_ranks(eager_ms, world, dev)
 
+    decode = []
+    if not a.no_decode:
+        for bs in a.decode_bs:
+            log(f"decode: Llama-3.2-1B INT4, bs={bs}, {a.decode_prompt}-token prefill, {a.decode_gen} steps, tp={world}")
+            decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world))
     log("per-shape isolated timing")
     per_shape = per_shape_isolated(stream) if (rank == 0 and not a.no_per_shape) else None
     cpu = None
@@ -501,6 +577,7 @@ def run_gpu(a):
         "clocks": sampler.summary(),
         "cpu_baseline": cpu,
         "per_shape_isolated": per_shape,
+        "decode": decode,
         "gpu": torch.cuda.get_device_name(dev),
     }
     print(json.dumps(line), flush=True)
@@ -516,9 +593,17 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-shape", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the full-model decode measurement")
+    ap.add_argument("--decode-bs", type=int, nargs="+", default=None,
+                    help="decode batch sizes (default: 1 and 16 on one GPU, 16 under tensor parallelism)")
+    ap.add_argument("--decode-prompt", type=int, default=512)
+    ap.add_argument("--decode-gen", type=int, default=128)
+    ap.add_argument("--decode-reps", type=int, default=3)
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
+    if a.decode_bs is None:
+        a.decode_bs = [1, 16] if int(os.environ.get("WORLD_SIZE", "1")) == 1 else [16]
     if a.impl == "reference":
         run_reference(a)
     else:

@@ -1,0 +1,23 @@
+"""Tensor-parallel INT4 decode on 2 GPUs (NCCL): the sharded tiny model matches the
+unsharded one, and decode replayed from one CUDA graph (collectives inside the graph)
+gives the same greedy tokens as eager decoding.  Runs as child processes; skipped on
+machines with fewer than 2 GPUs."""
+import json
+
+import pytest
+import torch
+
+from test_tp_cpu import launch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_tp2_int4_model_matches_unsharded():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    outs = launch("gpu_parity", world=2, timeout_s=300, env_extra={"NCCL_NVLS_ENABLE": "0", "TP_TEST_TIMEOUT": "120"})
+    for rc, out, err in outs:
+        assert rc == 0, err[-3000:]
+        rec = json.loads(out.strip().splitlines()[-1])
+        assert rec["prefill_rel_err"] < 1e-2, rec
+        assert rec["eager_tokens_equal"] and rec["graph_tokens_equal"], rec

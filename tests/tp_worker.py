@@ -51,6 +51,52 @@ def parity():
                       "w2_cols": part.layers[0].feed_forward.w2.weight.shape[1]}), flush=True)
 
 
+def gpu_parity():
+    """NCCL ranks on GPUs: the sharded INT4 tiny model against the unsharded one, eager and graph decode."""
+    import cases
+    from llama import quantize
+    from llama.generation import DecodeGraph, eager_tokens
+    from llama.model import Llama, ModelArgs
+    from llama.tp import shard_model
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", rank)
+    args = ModelArgs(**cases.TINY_MODEL)
+    sd = cases.tiny_state_dict(cases.TINY_MODEL)
+
+    def build():
+        torch.set_default_dtype(torch.float16)
+        try:
+            m = Llama(args)
+        finally:
+            torch.set_default_dtype(torch.float32)
+        m.load_state_dict(sd)
+        m = m.to(dev).eval()
+        quantize.quantize_model(m, 128)
+        return m
+
+    quantize.set_dequant_impl("v4")
+    full, part = build(), build()
+    shard_model(part)
+    prompt = cases.tiny_prompt(cases.TINY_MODEL).to(dev)
+    steps = cases.TINY_DECODE_STEPS
+    with torch.no_grad():
+        a, b = full(prompt, 0), part(prompt, 0)
+        prefill_err = float((a - b).abs().max() / a.abs().max())
+        full.reset_cache()
+        part.reset_cache()
+        t_full = eager_tokens(full, prompt, steps)
+        t_part = eager_tokens(part, prompt, steps)
+        graph = DecodeGraph(part, prompt.shape[0])
+        t_graph = graph.tokens(prompt, steps)
+        torch.cuda.synchronize(dev)
+    same_eager = bool(torch.equal(t_full, t_part))
+    same_graph = bool(torch.equal(t_part, t_graph))
+    del graph
+    print(json.dumps({"rank": rank, "world": world, "prefill_rel_err": prefill_err, "eager_tokens_equal": same_eager,
+                      "graph_tokens_equal": same_graph}), flush=True)
+
+
 def dead_peer():
     rank = dist.get_rank()
     if rank == 1:
@@ -69,9 +115,14 @@ def dead_peer():
 if __name__ == "__main__":
     mode = sys.argv[1]
     timeout = datetime.timedelta(seconds=float(os.environ.get("TP_TEST_TIMEOUT", "60")))
-    dist.init_process_group("gloo", timeout=timeout)
-    {"parity": parity, "dead_peer": dead_peer}[mode]()
-    if mode == "parity":
+    if mode == "gpu_parity":
+        torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+        dist.init_process_group("nccl", timeout=timeout,
+                                device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
+    else:
+        dist.init_process_group("gloo", timeout=timeout)
+    {"parity": parity, "dead_peer": dead_peer, "gpu_parity": gpu_parity}[mode]()
+    if mode in ("parity", "gpu_parity"):
         dist.barrier()
         dist.destroy_process_group()
     os._exit(0)
