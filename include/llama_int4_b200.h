@@ -49,7 +49,9 @@ typedef enum li4_dtype {
 typedef enum li4_kernel {
   LI4_KERNEL_AUTO = 0,
   LI4_KERNEL_CUDA_CORE = 1,  /* fp32 FMA on CUDA cores, M <= 8                      */
-  LI4_KERNEL_MMA = 2         /* m16n8k16 tensor-core tiles (weights as the A side)  */
+  LI4_KERNEL_MMA = 2,        /* m16n8k16 tensor-core tiles (weights as the A side)  */
+  LI4_KERNEL_STREAM = 3,     /* streaming warps, m16n8k16 tiles, groups >= 128      */
+  LI4_KERNEL_TILE = 4        /* tile-streaming warps: group 128, K ranges of 2048  */
 } li4_kernel;
 
 /* Library version, (major << 16) | (minor << 8) | patch. */

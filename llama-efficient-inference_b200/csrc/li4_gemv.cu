@@ -64,14 +64,29 @@ struct GemvArgs {
 // x staging.  Block b = ((ks * NT + nt) * M8 + m8) * 4 + quad holds the 32
 // values x[m][k0 .. k0+32), m = nt*8 + m8, k0 = kstep*128 + 32*quad, as 16
 // half2 words; word 4w + i = (x[k0 + 8w + i], x[k0 + 8w + i + 4]).  Chunk w
-// (16 bytes) of block b sits at b*64 + ((w ^ ((b >> 1) & 3)) << 4), which
-// keeps the 128-bit reads of 8 consecutive blocks on distinct banks.
+// (16 bytes) of block b sits at b*64 + ((w ^ key) << 4) with
+// key = (2*m8 + (quad >> 1)) & 3, which keeps the 128-bit reads of 8
+// consecutive blocks on distinct banks and does not depend on the kstep (so a
+// reader can precompute its offsets).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int xs_chunk_offset(int block, int w) {
-  return block * 64 + ((w ^ ((block >> 1) & 3)) << 4);
+__device__ __forceinline__ int xs_key(int m8, int quad) { return (2 * m8 + (quad >> 1)) & 3; }
+
+// block = ((kstep * NT + nt) * M8 + m8) * 4 + quad
+__device__ __forceinline__ int xs_chunk_offset(int block, int w, int m8) {
+  return block * 64 + ((w ^ xs_key(m8, block & 3)) << 4);
 }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// The same load as an ordered instruction: loop-invariant B fragments stay in
+// shared memory instead of being hoisted into registers across tiles.
+__device__ __forceinline__ uint4 lds128_ordered(const uint8_t* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+  return r;
+}
 
 template <int NT>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs) {
@@ -105,7 +120,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int
       out.z = __byte_perm(u[1], u[3], 0x5410);  // (x2, x6)
       out.w = __byte_perm(u[1], u[3], 0x7632);  // (x3, x7)
     }
-    *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w)) = out;
+    *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8)) = out;
   }
 }
 
@@ -278,7 +293,7 @@ __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const __grid_constan
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
               if (grp < M8)
-                bq[nt] = lds128(xs + xs_chunk_offset(((ks * NT + nt) * M8 + grp) * 4 + quad, w));
+                bq[nt] = lds128(xs + xs_chunk_offset(((ks * NT + nt) * M8 + grp) * 4 + quad, w, grp));
               else
                 bq[nt] = make_uint4(0u, 0u, 0u, 0u);
             }
@@ -421,7 +436,7 @@ __global__ void __launch_bounds__(kThreads) gemv_cc_kernel(const __grid_constant
               }
 #pragma unroll
             for (int m = 0; m < M; ++m) {
-              const uint4 xq = lds128(xs + xs_chunk_offset((ks * M + m) * 4 + quad, w));
+              const uint4 xq = lds128(xs + xs_chunk_offset((ks * M + m) * 4 + quad, w, m));
 #pragma unroll
               for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -475,6 +490,469 @@ __global__ void __launch_bounds__(kThreads) gemv_cc_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------
+// Streaming-warp tensor-core kernel (groups >= 128).
+//
+// Work unit: one kstep (128 k) of one 16-row tile.  Each warp walks its own
+// sequence of units through a register ring kStreamDepth units deep: the loads
+// of unit u + D are issued right after unit u is consumed, so every warp keeps
+// D units (D KiB) in flight at all times, and the first D units are requested
+// before griddepcontrol.wait (weights never depend on the preceding kernel).
+// Row, scale and zero addresses are rebuilt only when a warp moves to a new
+// tile.  Thread (grp, quad) computes rows grp and grp + 8 of the tile with
+// m16n8k16 MMAs (exact q - zero in fp16, fp32 accumulation per kstep, scaled
+// by the group scale in fp32), exactly as the classic MMA kernel.
+//
+// Rows mode: a warp owns whole tiles (all ksteps of its K range), so nothing
+// is shared between warps.  K-split mode (few tiles): the 8 warps of a CTA share
+// every tile, warp w taking ksteps w, w + 8, ...; the partial sums meet in
+// shared memory once per tile.
+// ---------------------------------------------------------------------------
+constexpr int kStreamWarps = 8;
+constexpr int kStreamThreads = kStreamWarps * 32;
+constexpr int kStreamDepth = 5;
+
+struct StreamUnit {
+  uint4 lo, hi;          // bytes [16 quad, +16) of the kstep for rows grp and grp + 8
+  uint32_t sz_lo, sz_hi; // fp16 bits: scale | zero << 16, for the two rows
+};
+
+// Per-warp walk over (tile, kstep) units.
+struct StreamCursor {
+  int tile;   // current tile (>= n_tiles: done)
+  int j;      // unit index inside the tile for this warp
+};
+
+template <bool KSPLIT>
+__device__ __forceinline__ void stream_advance(StreamCursor& c, int units_per_tile, int tile_step) {
+  if (++c.j == units_per_tile) {
+    c.j = 0;
+    c.tile += tile_step;
+  }
+}
+
+// Base pointers of a warp-thread for one tile (rows grp, grp + 8).
+struct StreamRows {
+  const uint8_t* p_lo;
+  const uint8_t* p_hi;
+  const unsigned short* s_lo;
+  const unsigned short* s_hi;
+  const unsigned short* z_lo;
+  const unsigned short* z_hi;
+};
+
+__device__ __forceinline__ StreamRows stream_rows(const GemvArgs& a, int tile, int ks0, int grp, int quad) {
+  int r0 = tile * 16 + grp, r1 = r0 + 8;
+  r0 = r0 < a.N ? r0 : a.N - 1;
+  r1 = r1 < a.N ? r1 : a.N - 1;
+  const long long off = (long long)ks0 * 64 + quad * 16;
+  const int g0 = (ks0 * 128) >> a.log2_group;
+  StreamRows r;
+  r.p_lo = a.packed + (long long)r0 * a.spn + off;
+  r.p_hi = a.packed + (long long)r1 * a.spn + off;
+  r.s_lo = reinterpret_cast<const unsigned short*>(a.scale) + (long long)r0 * a.ssn + g0;
+  r.s_hi = reinterpret_cast<const unsigned short*>(a.scale) + (long long)r1 * a.ssn + g0;
+  r.z_lo = reinterpret_cast<const unsigned short*>(a.zero) + (long long)r0 * a.ssn + g0;
+  r.z_hi = reinterpret_cast<const unsigned short*>(a.zero) + (long long)r1 * a.ssn + g0;
+  return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_u16(const unsigned short* p) {
+  unsigned short r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void stream_load(const GemvArgs& a, StreamUnit& u, const StreamRows& r, int ks) {
+  u.lo = ldg_stream_v4(r.p_lo + ks * 64);
+  u.hi = ldg_stream_v4(r.p_hi + ks * 64);
+  const int g = (ks * 128) >> a.log2_group;
+  u.sz_lo = ldg_u16(r.s_lo + g) | (ldg_u16(r.z_lo + g) << 16);
+  u.sz_hi = ldg_u16(r.s_hi + g) | (ldg_u16(r.z_hi + g) << 16);
+}
+
+// acc += s * (W[rows] . x) for one unit.  xs_ks: the unit's kstep in the x
+// staging; n-tile nt of it starts nt * nt_stride bytes further.
+template <int NT>
+__device__ __forceinline__ void stream_compute(const StreamUnit& u, const uint8_t* xs_ks, int nt_stride,
+                                               const int boff[4], bool bvalid, float acc[NT][4]) {
+  const ZeroConsts zl = make_zero_consts(__ushort_as_half((unsigned short)(u.sz_lo >> 16)));
+  const ZeroConsts zh = make_zero_consts(__ushort_as_half((unsigned short)(u.sz_hi >> 16)));
+  float c[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[nt][e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    __half2 pl[4], ph[4];
+    unpack8_qz((w == 0) ? u.lo.x : (w == 1) ? u.lo.y : (w == 2) ? u.lo.z : u.lo.w, zl, pl);
+    unpack8_qz((w == 0) ? u.hi.x : (w == 1) ? u.hi.y : (w == 2) ? u.hi.z : u.hi.w, zh, ph);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      uint4 bq = make_uint4(0u, 0u, 0u, 0u);
+      if (bvalid) bq = lds128(xs_ks + nt * nt_stride + boff[w]);
+      mma_16816(c[nt], h2_as_u32(pl[0]), h2_as_u32(ph[0]), h2_as_u32(pl[1]), h2_as_u32(ph[1]), bq.x, bq.y);
+      mma_16816(c[nt], h2_as_u32(pl[2]), h2_as_u32(ph[2]), h2_as_u32(pl[3]), h2_as_u32(ph[3]), bq.z, bq.w);
+    }
+  }
+  const float sl = __half2float(__ushort_as_half((unsigned short)(u.sz_lo & 0xFFFFu)));
+  const float sh = __half2float(__ushort_as_half((unsigned short)(u.sz_hi & 0xFFFFu)));
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    acc[nt][0] = fmaf(sl, c[nt][0], acc[nt][0]);
+    acc[nt][1] = fmaf(sl, c[nt][1], acc[nt][1]);
+    acc[nt][2] = fmaf(sh, c[nt][2], acc[nt][2]);
+    acc[nt][3] = fmaf(sh, c[nt][3], acc[nt][3]);
+  }
+}
+
+template <int NT, bool KSPLIT>
+__global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int D = kStreamDepth;
+  constexpr int COLS = 8 * NT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 2, quad = lane & 3;
+  const int nks = a.ks_per_split;
+  const int ks0 = blockIdx.y * nks;
+  const int M8 = (NT == 1) ? a.M : 8;
+  uint8_t* xs = smem;
+  float* red = reinterpret_cast<float*>(smem + ((nks * NT * M8 * 256 + 127) & ~127));  // K-split: [2][8][16][COLS]
+
+  // unit walk of this warp
+  const int units_per_tile = KSPLIT ? (nks - warp + kStreamWarps - 1) / kStreamWarps : nks;
+  const int tile_step = KSPLIT ? gridDim.x : gridDim.x * kStreamWarps;
+  StreamCursor lc{KSPLIT ? (int)blockIdx.x : (int)(blockIdx.x * kStreamWarps + warp), 0};
+  StreamCursor cc = lc;
+  int lrows_tile = -1;
+  StreamRows lrows{};
+
+  pdl_launch_dependents();
+  StreamUnit buf[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+    if (lc.tile < a.n_tiles && units_per_tile > 0) {
+      if (lc.tile != lrows_tile) { lrows = stream_rows(a, lc.tile, ks0, grp, quad); lrows_tile = lc.tile; }
+      stream_load(a, buf[d], lrows, KSPLIT ? warp + kStreamWarps * lc.j : lc.j);
+    }
+    stream_advance<KSPLIT>(lc, units_per_tile, tile_step);
+  }
+  pdl_wait_primary();  // x is written by the preceding kernel
+  stage_x<NT>(a, ks0, nks, M8, xs);
+  __syncthreads();
+
+  // this thread's B-fragment offsets inside one (kstep, n-tile) group
+  const bool bvalid = grp < M8;
+  int boff[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) boff[w] = (grp * 4 + quad) * 64 + ((w ^ xs_key(grp, quad)) << 4);
+  const int ks_stride = NT * M8 * 256;
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+  int tiles_done = 0;
+
+  bool more = cc.tile < a.n_tiles && units_per_tile > 0;
+  while (more) {
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      if (!more) break;
+      const int ks = KSPLIT ? warp + kStreamWarps * cc.j : cc.j;
+      stream_compute<NT>(buf[d], xs + ks * ks_stride, M8 * 256, boff, bvalid, acc);
+      const int tile = cc.tile;
+      const bool tile_end = (cc.j == units_per_tile - 1);
+      // refill this ring slot with the unit D ahead
+      if (lc.tile < a.n_tiles) {
+        if (lc.tile != lrows_tile) { lrows = stream_rows(a, lc.tile, ks0, grp, quad); lrows_tile = lc.tile; }
+        stream_load(a, buf[d], lrows, KSPLIT ? warp + kStreamWarps * lc.j : lc.j);
+      }
+      stream_advance<KSPLIT>(lc, units_per_tile, tile_step);
+      stream_advance<KSPLIT>(cc, units_per_tile, tile_step);
+      more = cc.tile < a.n_tiles;
+      if (tile_end) {
+        const int row0 = tile * 16;
+        const int rows = min(16, a.N - row0);
+        if (!KSPLIT) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
+              if (r < rows && m < a.M) {
+                if (a.split == 1) a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(acc[nt][e]);
+                else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
+              }
+              acc[nt][e] = 0.f;
+            }
+          if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
+            __threadfence();
+            __syncwarp();
+            unsigned last = 0;
+            if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1u : 0u;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+              __threadfence();
+              for (int idx = lane; idx < rows * a.M; idx += 32) {
+                const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+                float v = 0.f;
+                for (int sp = 0; sp < a.split; ++sp) v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
+                a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
+              }
+              __syncwarp();
+              if (lane == 0) a.counters[tile] = 0u;
+            }
+          }
+        } else {
+          float* rb = red + (tiles_done & 1) * (kStreamWarps * 16 * COLS);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              rb[(warp * 16 + grp + 8 * (e >> 1)) * COLS + nt * 8 + 2 * quad + (e & 1)] = acc[nt][e];
+              acc[nt][e] = 0.f;
+            }
+          __syncthreads();
+          for (int idx = threadIdx.x; idx < rows * a.M; idx += kStreamThreads) {
+            const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kStreamWarps; ++w) v += rb[(w * 16 + r) * COLS + m];
+            if (a.split == 1) a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
+            else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = v;
+          }
+          if (a.split > 1) {
+            __threadfence();  // every writer publishes its partials before the arrival count
+            __syncthreads();
+            if (warp == 0) {
+              unsigned last = 0;
+              if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1u : 0u;
+              last = __shfl_sync(0xffffffffu, last, 0);
+              if (last) {
+                __threadfence();
+                for (int idx = lane; idx < rows * a.M; idx += 32) {
+                  const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+                  float v = 0.f;
+                  for (int sp = 0; sp < a.split; ++sp)
+                    v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
+                  a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
+                }
+                __syncwarp();
+                if (lane == 0) a.counters[tile] = 0u;
+              }
+            }
+          }
+          ++tiles_done;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tile-streaming kernel for the common decode configuration: group 128 and a
+// K range of exactly 16 ksteps (2048 k) per CTA.  Each warp owns whole tiles
+// of 16*RT rows and walks them with the 16 ksteps fully unrolled, so every
+// weight / scale / x offset is an immediate and the pointers change once per
+// tile.  A register ring of D = 8 / RT units keeps 8 KiB per warp in flight;
+// while the last D ksteps of a tile are computed, the first D units of the
+// warp's next tile are already being fetched, and the first tile's units are
+// requested before griddepcontrol.wait.  Math as in the streaming kernel.
+// ---------------------------------------------------------------------------
+constexpr int kTileKs = 16;    // ksteps of 128 k per K range
+#ifndef LI4_TILE_DEPTH
+#define LI4_TILE_DEPTH 4
+#endif
+constexpr int kTileDepth = LI4_TILE_DEPTH;  // register-ring units (of 16 rows) in flight per warp
+
+template <int RT>
+struct TileUnit {
+  uint4 w[RT][2];        // rows rt*16 + grp (+8), bytes [16 quad, +16) of one kstep
+  uint32_t sz[RT][2];    // scale | zero << 16
+};
+
+// Per-lane offsets of one tile's rows: bytes into `packed`, elements into
+// `scale` / `zero` (which share a row stride).  32-bit: the planner only picks
+// this kernel when every offset fits.
+template <int RT>
+struct TileRows {
+  uint32_t p[RT][2];
+  uint32_t s[RT][2];
+};
+
+template <int RT>
+__device__ __forceinline__ TileRows<RT> tile_rows(const GemvArgs& a, int tile, int ks0, int grp, int quad) {
+  TileRows<RT> t;
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int r = tile * 16 * RT + rt * 16 + grp + 8 * h;
+      r = r < a.N ? r : a.N - 1;
+      t.p[rt][h] = (uint32_t)r * (uint32_t)a.spn + (uint32_t)(ks0 * 64 + quad * 16);
+      t.s[rt][h] = (uint32_t)r * (uint32_t)a.ssn + (uint32_t)ks0;
+    }
+  return t;
+}
+
+template <int RT>
+__device__ __forceinline__ void tile_load(TileUnit<RT>& u, const GemvArgs& a, const TileRows<RT>& t, int ks) {
+  const unsigned short* sc = reinterpret_cast<const unsigned short*>(a.scale);
+  const unsigned short* ze = reinterpret_cast<const unsigned short*>(a.zero);
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      u.w[rt][h] = ldg_stream_v4(a.packed + t.p[rt][h] + ks * 64);
+      u.sz[rt][h] = ldg_u16(sc + t.s[rt][h] + ks) | (ldg_u16(ze + t.s[rt][h] + ks) << 16);
+    }
+}
+
+template <int NT, int RT>
+__device__ __forceinline__ void tile_compute(const TileUnit<RT>& u, const uint8_t* xs_ks, int nt_stride,
+                                             const int boff[4], bool bvalid, float acc[RT][NT][4]) {
+  ZeroConsts zc[RT][2];
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) zc[rt][h] = make_zero_consts(__ushort_as_half((unsigned short)(u.sz[rt][h] >> 16)));
+  float c[RT][NT][4];
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[rt][nt][e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint4 bq[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      bq[nt] = make_uint4(0u, 0u, 0u, 0u);
+      if (bvalid) bq[nt] = lds128_ordered(xs_ks + nt * nt_stride + boff[w]);
+    }
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt) {
+      __half2 pl[4], ph[4];
+      const uint4& lo = u.w[rt][0];
+      const uint4& hi = u.w[rt][1];
+      unpack8_qz((w == 0) ? lo.x : (w == 1) ? lo.y : (w == 2) ? lo.z : lo.w, zc[rt][0], pl);
+      unpack8_qz((w == 0) ? hi.x : (w == 1) ? hi.y : (w == 2) ? hi.z : hi.w, zc[rt][1], ph);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        mma_16816(c[rt][nt], h2_as_u32(pl[0]), h2_as_u32(ph[0]), h2_as_u32(pl[1]), h2_as_u32(ph[1]), bq[nt].x,
+                  bq[nt].y);
+        mma_16816(c[rt][nt], h2_as_u32(pl[2]), h2_as_u32(ph[2]), h2_as_u32(pl[3]), h2_as_u32(ph[3]), bq[nt].z,
+                  bq[nt].w);
+      }
+    }
+  }
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt) {
+    const float sl = __half2float(__ushort_as_half((unsigned short)(u.sz[rt][0] & 0xFFFFu)));
+    const float sh = __half2float(__ushort_as_half((unsigned short)(u.sz[rt][1] & 0xFFFFu)));
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[rt][nt][0] = fmaf(sl, c[rt][nt][0], acc[rt][nt][0]);
+      acc[rt][nt][1] = fmaf(sl, c[rt][nt][1], acc[rt][nt][1]);
+      acc[rt][nt][2] = fmaf(sh, c[rt][nt][2], acc[rt][nt][2]);
+      acc[rt][nt][3] = fmaf(sh, c[rt][nt][3], acc[rt][nt][3]);
+    }
+  }
+}
+
+template <int NT, int RT>
+__global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_kernel(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int NKS = kTileKs;
+  constexpr int D = kTileDepth / RT;
+  constexpr int ROWS = 16 * RT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 2, quad = lane & 3;
+  const int ks0 = blockIdx.y * NKS;
+  constexpr int M8 = 8;  // x rows padded to 8 per n-tile: every B-fragment offset is an immediate
+  uint8_t* xs = smem;
+  const int tile_step = gridDim.x * kStreamWarps;
+  int tile = blockIdx.x * kStreamWarps + warp;
+
+  pdl_launch_dependents();
+  TileUnit<RT> buf[D];
+  TileRows<RT> cur = tile_rows<RT>(a, tile < a.n_tiles ? tile : 0, ks0, grp, quad);
+  if (tile < a.n_tiles) {
+#pragma unroll
+    for (int d = 0; d < D; ++d) tile_load<RT>(buf[d], a, cur, d);
+  }
+  pdl_wait_primary();  // x is written by the preceding kernel
+  stage_x<NT>(a, ks0, NKS, M8, xs);
+  __syncthreads();
+
+  const bool bvalid = grp < ((NT == 1) ? a.M : 8);
+  int boff[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) boff[w] = (grp * 4 + quad) * 64 + ((w ^ xs_key(grp, quad)) << 4);
+  constexpr int nt_stride = M8 * 256;
+  constexpr int ks_stride = NT * nt_stride;
+
+  for (; tile < a.n_tiles; tile += tile_step) {
+    const int next = tile + tile_step;
+    const bool has_next = next < a.n_tiles;
+    TileRows<RT> nxt;
+    float acc[RT][NT][4];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[rt][nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < NKS; ++ks) {
+      tile_compute<NT, RT>(buf[ks % D], xs + ks * ks_stride, nt_stride, boff, bvalid, acc);
+      if (ks + D < NKS) {
+        tile_load<RT>(buf[ks % D], a, cur, ks + D);
+      } else {
+        if (ks + D == NKS) nxt = tile_rows<RT>(a, has_next ? next : tile, ks0, grp, quad);
+        if (has_next) tile_load<RT>(buf[ks % D], a, nxt, ks + D - NKS);
+      }
+    }
+    const int row0 = tile * ROWS;
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = row0 + rt * 16 + grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
+          if (r < a.N && m < a.M) {
+            if (a.split == 1) a.y[(long long)m * a.sym + r] = __float2half_rn(acc[rt][nt][e]);
+            else a.partial[((long long)blockIdx.y * a.M + m) * a.N + r] = acc[rt][nt][e];
+          }
+        }
+    if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
+      const int rows = min(ROWS, a.N - row0);
+      __threadfence();
+      __syncwarp();
+      unsigned last = 0;
+      if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1u : 0u;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        for (int idx = lane; idx < rows * a.M; idx += 32) {
+          const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+          float v = 0.f;
+          for (int sp = 0; sp < a.split; ++sp) v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
+          a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
+        }
+        __syncwarp();
+        if (lane == 0) a.counters[tile] = 0u;
+      }
+    }
+    cur = nxt;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: planning and launch.
 // ---------------------------------------------------------------------------
 struct Plan {
@@ -492,6 +970,7 @@ struct Plan {
   size_t smem;
   size_t ws_counters;  // bytes
   size_t ws_bytes;     // total
+  bool stream_ksplit;  // LI4_KERNEL_STREAM: K-split mode
 };
 
 static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -512,11 +991,20 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (sm <= 0) sm = 148;
 
   int kernel = kernel_req;
-  if (kernel == LI4_KERNEL_AUTO) kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
+  if (kernel == LI4_KERNEL_AUTO) {
+    if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
+    else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
+  }
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel takes M <= 8 (M=%lld)", (long long)M);
-  if (kernel != LI4_KERNEL_CUDA_CORE && kernel != LI4_KERNEL_MMA)
+  if (kernel == LI4_KERNEL_STREAM && (group < 128 || K == 0))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the streaming kernel needs group_size >= 128 and K > 0");
+  if (kernel == LI4_KERNEL_TILE && (group != 128 || K == 0 || (K / 128) % kTileKs != 0))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the tile kernel needs group_size 128 and K a multiple of %d",
+                     kTileKs * 128);
+  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_TILE)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: unknown kernel %d", kernel);
+  p->stream_ksplit = false;
   p->kernel = kernel;
   p->nt = (M <= 8) ? 1 : 2;
   p->scale_in_a = group < 128;
@@ -543,6 +1031,27 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
            p->n_ks / (2 * split) >= kWarps)
       split *= 2;
   }
+  if (kernel == LI4_KERNEL_STREAM) {  // 16-row tiles; rows mode for many tiles, K-split mode for few
+    p->rt = 1;
+    p->n_tiles = (int)((N + 15) / 16);
+    if (split_req <= 0) {
+      split = 1;
+      while (p->n_ks % split != 0 || p->n_ks / split > kMaxKsPerCta) ++split;
+    }
+    p->stream_ksplit = (int64_t)p->n_tiles < 4LL * sm && p->n_ks / split >= kStreamWarps;
+    if (split_req <= 0 && p->stream_ksplit)
+      while ((int64_t)p->n_tiles * split * 2 <= sm && p->n_ks % (2 * split) == 0 &&
+             p->n_ks / (2 * split) >= kStreamWarps)
+        split *= 2;
+  }
+  if (kernel == LI4_KERNEL_TILE) {  // K ranges of exactly kTileKs ksteps; 16 or 32 rows per warp tile
+    if (split_req > 0 && split_req != p->n_ks / kTileKs)
+      return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the tile kernel takes split=%d for K=%lld",
+                       p->n_ks / kTileKs, (long long)K);
+    split = p->n_ks / kTileKs;
+    p->rt = (rows_req == 32) ? 2 : 1;
+    p->n_tiles = (int)((N + 16 * p->rt - 1) / (16 * p->rt));
+  }
   p->split = split;
   p->ks_per_split = (p->n_ks == 0) ? 0 : p->n_ks / split;
 
@@ -558,6 +1067,19 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   const int nt = (p->kernel == LI4_KERNEL_CUDA_CORE) ? 1 : p->nt;
   const int cols = 8 * nt;
   p->smem = round_up((size_t)p->ks_per_split * nt * m8 * 256, 128) + (size_t)kWarps * rows * cols * sizeof(float);
+  if (kernel == LI4_KERNEL_STREAM) {
+    p->smem = round_up((size_t)p->ks_per_split * p->nt * (p->nt == 1 ? (int)M : 8) * 256, 128) +
+              (p->stream_ksplit ? (size_t)2 * kStreamWarps * 16 * 8 * p->nt * sizeof(float) : 0);
+    int gx = p->stream_ksplit ? p->n_tiles : (p->n_tiles + kStreamWarps - 1) / kStreamWarps;
+    if (max_ctas > 0 && gx > max_ctas / split) gx = max_ctas / split > 0 ? max_ctas / split : 1;
+    p->grid_x = gx;  // capped by occupancy at launch
+  }
+  if (kernel == LI4_KERNEL_TILE) {
+    p->smem = (size_t)kTileKs * p->nt * 8 * 256;
+    int gx = (p->n_tiles + kStreamWarps - 1) / kStreamWarps;
+    if (max_ctas > 0 && gx > max_ctas / split) gx = max_ctas / split > 0 ? max_ctas / split : 1;
+    p->grid_x = gx;  // capped by occupancy at launch
+  }
 
   if (split > 1) {
     // Counters live in a fixed region at the start of the workspace that no
@@ -649,7 +1171,57 @@ static int launch_cc(const Plan& p, const GemvArgs& args, cudaStream_t s) {
   return p.rt == 1 ? launch(gemv_cc_kernel<M, 1>, p, args, s) : launch(gemv_cc_kernel<M, 2>, p, args, s);
 }
 
+template <typename KernelT>
+static int launch_stream_kernel(KernelT kernel, const Plan& p, const GemvArgs& args, cudaStream_t stream) {
+  int rc = ensure_smem_limit(kernel, p.smem);
+  if (rc != LI4_OK) return rc;
+  int occ = 0;
+  {
+    static std::mutex mu;
+    struct Entry { const void* fn; size_t smem; int dev; int n; };
+    static std::vector<Entry> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& e : cache)
+      if (e.fn == (const void*)kernel && e.smem == p.smem && e.dev == dev) occ = e.n;
+    if (occ == 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kStreamThreads, p.smem) != cudaSuccess || occ < 1)
+        occ = 1;
+      cache.push_back(Entry{(const void*)kernel, p.smem, dev, occ});
+    }
+  }
+  int gx = p.grid_x;
+  const int cap = occ * p.sm / p.split;
+  if (gx > cap) gx = cap > 0 ? cap : 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gx, (unsigned)p.split, 1);
+  cfg.blockDim = dim3(kStreamThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args), "int4_linear: streaming kernel launch");
+}
+
 static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
+  if (p.kernel == LI4_KERNEL_TILE) {
+    if (p.nt == 1)
+      return p.rt == 1 ? launch_stream_kernel(gemv_tile_kernel<1, 1>, p, args, s)
+                       : launch_stream_kernel(gemv_tile_kernel<1, 2>, p, args, s);
+    return p.rt == 1 ? launch_stream_kernel(gemv_tile_kernel<2, 1>, p, args, s)
+                     : launch_stream_kernel(gemv_tile_kernel<2, 2>, p, args, s);
+  }
+  if (p.kernel == LI4_KERNEL_STREAM) {
+    if (p.nt == 1)
+      return p.stream_ksplit ? launch_stream_kernel(gemv_stream_kernel<1, true>, p, args, s)
+                             : launch_stream_kernel(gemv_stream_kernel<1, false>, p, args, s);
+    return p.stream_ksplit ? launch_stream_kernel(gemv_stream_kernel<2, true>, p, args, s)
+                           : launch_stream_kernel(gemv_stream_kernel<2, false>, p, args, s);
+  }
   if (p.kernel == LI4_KERNEL_CUDA_CORE) {
     switch (args.M) {
       case 1: return launch_cc<1>(p, args, s);
@@ -695,6 +1267,14 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(scale) |
        reinterpret_cast<uintptr_t>(zero)) & 1u)
     return set_error(LI4_ERR_ALIGNMENT, "int4_linear: fp16 tensors must be 2-byte aligned");
+  if (p.kernel == LI4_KERNEL_TILE && ((N - 1) * spn + K / 2 > (int64_t)UINT32_MAX ||
+                                      (N - 1) * ssn + K / group > (int64_t)UINT32_MAX)) {
+    // the tile kernel addresses rows with 32-bit offsets
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: the tile kernel needs packed / scale offsets below 2^32");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p);
+    if (rc != LI4_OK) return rc;
+  }
   if (p.ws_bytes > 0) {
     if (!workspace || workspace_bytes < p.ws_bytes)
       return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "
@@ -733,7 +1313,7 @@ extern "C" size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t 
   if (li4::make_plan(M, N, K, group_size, sm, LI4_KERNEL_AUTO, 0, 0, 0, &p) != LI4_OK) return 0;
   // Enough for every kernel family and launch shape the dispatcher may pick.
   size_t best = p.ws_bytes;
-  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_MMA; ++kernel) {
+  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_TILE; ++kernel) {
     if (kernel == LI4_KERNEL_CUDA_CORE && M > 8) continue;
     if (li4::make_plan(M, N, K, group_size, sm, kernel, 0, 0, 0, &p) == LI4_OK && p.ws_bytes > best) best = p.ws_bytes;
   }

@@ -21,7 +21,18 @@ LLAMA_SHAPES = [  # (name, N = out_features, K = in_features)
     ("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
     ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192), ("lm_head", 128256, 2048),
 ]
-KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2}
+KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4}
+
+
+def supported(kernel: str, M: int, group: int = 128, K: int = 2048) -> bool:
+    """Which forced kernel families take the problem."""
+    if kernel == "cuda_core":
+        return M <= 8
+    if kernel == "stream":
+        return group >= 128 and K > 0
+    if kernel == "tile":
+        return group == 128 and K > 0 and K % 2048 == 0
+    return True
 
 
 @pytest.fixture(scope="module")
@@ -69,8 +80,8 @@ def test_golden_cases(case, kernel, golden, g, cuda_device):
     int4_gemv, _ = g
     meta, arr = golden
     name, N, K, M, group = case[:5]
-    if kernel == "cuda_core" and M > 8:
-        pytest.skip("CUDA-core family takes M <= 8")
+    if not supported(kernel, M, group, K):
+        pytest.skip(f"{kernel} does not take M={M} group={group} K={K}")
     w, x = cases.make_gemv_inputs(case)
     packed, scale, zero = oracle.quantize(w.numpy(), group)
     dev = cuda_device
@@ -89,8 +100,8 @@ def test_llama_shapes(shape, M, g, cuda_device):
     name, N, K = shape
     x, p, s, z, host = make_problem(N, K, M, seed=sum(map(ord, name)) + M)
     y_ref, y32 = oracle.linear(*host)
-    for kernel in ("auto", "cuda_core", "mma"):
-        if kernel == "cuda_core" and M > 8:
+    for kernel in KERNELS:
+        if not supported(kernel, M, 128, K):
             continue
         y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
         int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS[kernel])
@@ -114,8 +125,8 @@ def test_group_sizes(group, M, g, cuda_device):
     int4_gemv, _ = g
     x, p, s, z, host = make_problem(300, 2048, M, group=group, seed=group + M)
     y_ref, y32 = oracle.linear(*host, group_size=group)
-    for kernel in ("auto", "cuda_core", "mma"):
-        if kernel == "cuda_core" and M > 8:
+    for kernel in KERNELS:
+        if not supported(kernel, M, group):
             continue
         y = torch.empty(M, 300, dtype=torch.float16, device=cuda_device)
         int4_gemv.int4_linear_out(x, p, s, z, y, group, kernel=KERNELS[kernel])
@@ -140,6 +151,43 @@ def test_forced_launch_shapes(kernel, rows, split, max_ctas, g, cuda_device):
     int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS[kernel], rows_per_cta=rows, split=split,
                               max_ctas=max_ctas)
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "split-K result is not deterministic"
+
+
+@pytest.mark.parametrize("M", [1, 3, 9, 16])
+@pytest.mark.parametrize("split", [0, 1, 2, 4, 8, 16])
+@pytest.mark.parametrize("max_ctas", [0, 1, 5])
+@pytest.mark.parametrize("N", [700, 4100, 20000])
+def test_stream_launch_shapes(M, split, max_ctas, N, g, cuda_device):
+    """Streaming-warp kernel: rows mode (many tiles) and K-split mode (few), split-K, short grids (each warp
+    walks many tiles, the register ring runs across tile boundaries), a partial last tile; deterministic."""
+    int4_gemv, _ = g
+    K = 2048
+    x, p, s, z, host = make_problem(N, K, M, seed=N + M + split + max_ctas)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["stream"], split=split, max_ctas=max_ctas)
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["stream"], split=split, max_ctas=max_ctas)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+@pytest.mark.parametrize("M", [1, 5, 9, 16])
+@pytest.mark.parametrize("rows", [16, 32])
+@pytest.mark.parametrize("max_ctas", [0, 1, 3])
+@pytest.mark.parametrize("N,K", [(1, 2048), (300, 4096), (4100, 2048), (20000, 2048), (2049, 8192)])
+def test_tile_launch_shapes(M, rows, max_ctas, N, K, g, cuda_device):
+    """Tile-streaming kernel: 16- and 32-row warp tiles, K ranges of 2048 (split-K above), short grids (each
+    warp walks many tiles and prefetches the next one), partial last tiles, N=1; deterministic."""
+    int4_gemv, _ = g
+    x, p, s, z, host = make_problem(N, K, M, seed=N + K + M + rows + max_ctas)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["tile"], rows_per_cta=rows, max_ctas=max_ctas)
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["tile"], rows_per_cta=rows, max_ctas=max_ctas)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
 
 
 def test_split_counters_reset_across_launches(g, cuda_device):
