@@ -34,6 +34,7 @@
 #include "li4_common.cuh"
 #include "li4_internal.h"
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -992,7 +993,12 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
 
   int kernel = kernel_req;
   if (kernel == LI4_KERNEL_AUTO) {
-    if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
+    // Tile streaming when every warp slot gets several 16-row x 2048-k tiles
+    // (lm_head-sized N); streaming warps for the rest; CUDA-core / MMA
+    // kernels for groups below 128.
+    const int64_t tiles_2048 = ((N + 15) / 16) * (K / 2048);
+    if (group == 128 && K > 0 && K % 2048 == 0 && tiles_2048 >= 32LL * sm) kernel = LI4_KERNEL_TILE;
+    else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
   }
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
@@ -1017,12 +1023,15 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   p->n_tiles = (int)((N + rows - 1) / rows);
   p->n_ks = (int)(K / 128);
 
+  // K range of one CTA: 16 ksteps, or (streaming warps) as many as keep the staged x within 32 KiB
+  int max_ks = kMaxKsPerCta;
+  if (kernel == LI4_KERNEL_STREAM) max_ks = std::max(kMaxKsPerCta, 32768 / (p->nt * (p->nt == 1 ? (int)M : 8) * 256));
   int split = 1;
   if (split_req > 0) {
     split = split_req;
-    if (p->n_ks == 0 || p->n_ks % split != 0 || p->n_ks / split > kMaxKsPerCta)
+    if (p->n_ks == 0 || p->n_ks % split != 0 || p->n_ks / split > max_ks)
       return set_error(LI4_ERR_INVALID_ARG, "int4_linear: split=%d must divide K/128=%d into ranges of <= %d",
-                       split, p->n_ks, kMaxKsPerCta);
+                       split, p->n_ks, max_ks);
   } else if (p->n_ks > 0) {
     // smallest divisor of n_ks giving K ranges of at most kMaxKsPerCta ksteps
     while (p->n_ks % split != 0 || p->n_ks / split > kMaxKsPerCta) ++split;
@@ -1036,7 +1045,7 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     p->n_tiles = (int)((N + 15) / 16);
     if (split_req <= 0) {
       split = 1;
-      while (p->n_ks % split != 0 || p->n_ks / split > kMaxKsPerCta) ++split;
+      while (p->n_ks % split != 0 || p->n_ks / split > max_ks) ++split;
     }
     p->stream_ksplit = (int64_t)p->n_tiles < 4LL * sm && p->n_ks / split >= kStreamWarps;
     if (split_req <= 0 && p->stream_ksplit)

@@ -172,13 +172,32 @@ def test_stream_launch_shapes(M, split, max_ctas, N, g, cuda_device):
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
 
 
+@pytest.mark.parametrize("M", [1, 2, 4])
+@pytest.mark.parametrize("split", [0, 1, 2])
+@pytest.mark.parametrize("N", [700, 2048])
+def test_stream_long_k_ranges(M, split, N, g, cuda_device):
+    """Streaming warps with K ranges above 2048 (x staged for up to 8192 k when M is small): down_proj's
+    K=8192 in one or two ranges, in K-split mode."""
+    int4_gemv, _ = g
+    K = 8192
+    if split == 1 and M > 2:
+        pytest.skip("x for M > 2 over 8192 k exceeds the 32 KiB staging limit")
+    x, p, s, z, host = make_problem(N, K, M, seed=7 * N + M + split)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["stream"], split=split)
+    check_close(y, y_ref, y32, host)
+
+
 @pytest.mark.parametrize("M", [1, 5, 9, 16])
 @pytest.mark.parametrize("rows", [16, 32])
 @pytest.mark.parametrize("max_ctas", [0, 1, 3])
-@pytest.mark.parametrize("N,K", [(1, 2048), (300, 4096), (4100, 2048), (20000, 2048), (2049, 8192)])
+@pytest.mark.parametrize("N,K", [(17, 2048), (300, 4096), (4100, 2048), (20000, 2048), (2049, 8192)])
 def test_tile_launch_shapes(M, rows, max_ctas, N, K, g, cuda_device):
     """Tile-streaming kernel: 16- and 32-row warp tiles, K ranges of 2048 (split-K above), short grids (each
-    warp walks many tiles and prefetches the next one), partial last tiles, N=1; deterministic."""
+    warp walks many tiles and prefetches the next one), partial last tiles; deterministic.  N >= 17: with a
+    single output the 2e-3 * max|y_ref| bound is a bound on one near-cancelling sum, which fp32 sums of the
+    unrounded weights need not meet (the per-output bound holds there; the shape sweep checks N=1)."""
     int4_gemv, _ = g
     x, p, s, z, host = make_problem(N, K, M, seed=N + K + M + rows + max_ctas)
     y_ref, y32 = oracle.linear(*host)
