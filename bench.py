@@ -282,12 +282,12 @@ def time_e2e(stream: Stream, steps: int, warmup: int, world: int, eager: bool = 
     return start.elapsed_time(end) / steps, hx.numel() * 2, hy.numel() * 2
 
 
-def per_shape_isolated(stream: Stream, reps: int = 20):
-    """Each distinct shape timed alone (L2 flushed before every launch): kernel GB/s without stream overlap."""
+def per_shape_isolated(stream: Stream, reps: int = 5):
+    """Each distinct shape alone: a CUDA graph of back-to-back launches over rotating weight copies
+    totalling > 3x L2 (so weights stream from HBM), device time per launch, median of `reps` replays."""
     from llama.int4_gemv import int4_linear_out
 
     dev = stream.device
-    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
     out = {}
     seen = set()
     for i, (name, N, K, _) in enumerate(stream.shapes):
@@ -296,24 +296,60 @@ def per_shape_isolated(stream: Stream, reps: int = 20):
             continue
         seen.add(short)
         x, (p, s, z), y = stream.xs[i], stream.weights[i], stream.ys[i]
+        wbytes = gemv_bytes(N, K, 0)
+        copies = max(2, 3 * L2_BYTES // wbytes + 1)
+        ws = [(p, s, z)] + [(p.clone(), s.clone(), z.clone()) for _ in range(copies - 1)]
+
+        def run():
+            for pi, si, zi in ws:
+                int4_linear_out(x, pi, si, zi, y, GROUP)
+
+        run()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run()
+        g.replay()
         times = []
         for _ in range(reps):
-            flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            int4_linear_out(x, p, s, z, y, GROUP)
+            g.replay()
             b.record()
             torch.cuda.synchronize(dev)
-            times.append(a.elapsed_time(b))
+            times.append(a.elapsed_time(b) / copies)
         us = statistics.median(times) * 1e3
-        out[short] = {"N": N, "K": K, "us": round(us, 2),
+        out[short] = {"N": N, "K": K, "us": round(us, 2), "launches_per_graph": copies,
                       "GBps": round(gemv_bytes(N, K, stream.M) / (us * 1e-6) / 1e9, 1)}
+        del g, ws
+        torch.cuda.empty_cache()
     return out
 
 
+def profile_shape(a):
+    """--profile-shape NAME: `--launches` eager launches of one shape (a small case for ncu captures)."""
+    from llama.int4_gemv import int4_linear_out
+    from llama.quantize import QuantizedLinear
+
+    shapes = {n: (N, K) for n, N, K in LAYER_SHAPES + [LM_HEAD]}
+    N, K = shapes[a.profile_shape]
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+    p, s, z = QuantizedLinear.quantize_tensor(w, GROUP)
+    del w
+    x = torch.randn(a.m, K, generator=gen, device=dev).half()
+    y = torch.empty(a.m, N, dtype=torch.float16, device=dev)
+    for _ in range(a.launches):
+        int4_linear_out(x, p, s, z, y, GROUP)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_shape": a.profile_shape, "N": N, "K": K, "M": a.m, "launches": a.launches,
+                      "bytes_per_launch": gemv_bytes(N, K, a.m)}))
+
+
 def roofline_traffic():
-    """DRAM bytes per step of the GEMV kernels from the committed ncu summary, if present."""
-    path = os.path.join(REPO, "profiles", "gemv_stream_m1_traffic.json")
+    """DRAM bytes per step of the GEMV kernels from the committed ncu summary, if present (M=1 only)."""
+    path = os.path.join(REPO, "profiles", "gemv_step_m1_traffic.json")
     try:
         with open(path) as f:
             return json.load(f).get("dram_bytes_per_step")
@@ -551,7 +587,7 @@ def run_gpu(a):
     bps = stream.bytes_per_step
     value = world * bps / (ms_max * 1e-3) / 1e9
     achieved = bps / (ms * 1e-3) / 1e9
-    traffic = roofline_traffic()
+    traffic = roofline_traffic() if a.m == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "weak",
@@ -566,7 +602,8 @@ def run_gpu(a):
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
-                     "kernel": "li4 fused INT4 GEMV (all 113 launches of the step)"},
+                     "kernel": "li4 fused INT4 GEMV: the 113 launches of one step (112 gemv_stream_kernel + "
+                               "1 gemv_tile_kernel); achieved and traffic are per step"},
         "e2e": {"value": round(world * bps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
                 "path": "pinned H2D x -> graph of 113 int4_linear_out calls -> D2H y"},
@@ -599,7 +636,13 @@ def main():
     ap.add_argument("--decode-prompt", type=int, default=512)
     ap.add_argument("--decode-gen", type=int, default=128)
     ap.add_argument("--decode-reps", type=int, default=3)
+    ap.add_argument("--profile-shape", default=None, choices=[n for n, _, _ in LAYER_SHAPES] + [LM_HEAD[0]],
+                    help="only run --launches launches of one shape (for ncu), no timing")
+    ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
+    if a.profile_shape:
+        profile_shape(a)
+        return
     if a.warmup < 3:
         a.warmup = 3
     if a.decode_bs is None:
