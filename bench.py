@@ -493,8 +493,9 @@ def build_decode_model(device, bs: int, max_seq_len: int, seed: int = 0):
     return model
 
 
-def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int):
-    """Prefill + `gen` greedy decode steps replayed from one graph; timings are the max over ranks."""
+def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int, fused: bool = True):
+    """Prefill + `gen` greedy decode steps replayed from one graph; timings are the max over ranks.
+    fused: the step as llama.fused kernels (five launches per block), else the module-by-module step."""
     from llama.generation import DecodeGraph
 
     model = build_decode_model(device, bs, prompt_len + gen)
@@ -502,6 +503,8 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
         from llama.tp import shard_model
 
         shard_model(model)
+    if fused:
+        model.enable_fused_decode()
     torch.cuda.synchronize(device)
     graph = DecodeGraph(model, bs)
     gen_t = torch.Generator(device=device).manual_seed(1)
@@ -530,6 +533,7 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
     del graph, model
     torch.cuda.empty_cache()
     return {"bs": bs, "prompt": prompt_len, "generated": gen, "tp": world, "reps": reps,
+            "step": "fused (llama.fused)" if fused else "unfused (module by module)",
             "decode_ms_per_step": round(step_ms, 4), "decode_p10_ms": round(q[0], 4), "decode_p90_ms": round(q[-1], 4),
             "decode_tok_s": round(bs / (step_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 3),
             "e2e_tok_s": round(bs * gen / (e2e_ms * 1e-3), 1)}
@@ -566,6 +570,8 @@ def run_gpu(a):
         for bs in a.decode_bs:
             log(f"decode: Llama-3.2-1B INT4, bs={bs}, {a.decode_prompt}-token prefill, {a.decode_gen} steps, tp={world}")
             decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world))
+            if a.decode_unfused:
+                decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
     log("per-shape isolated timing")
     per_shape = per_shape_isolated(stream) if (rank == 0 and not a.no_per_shape) else None
     cpu = None
@@ -636,6 +642,8 @@ def main():
     ap.add_argument("--decode-prompt", type=int, default=512)
     ap.add_argument("--decode-gen", type=int, default=128)
     ap.add_argument("--decode-reps", type=int, default=3)
+    ap.add_argument("--decode-unfused", action="store_true",
+                    help="also time the module-by-module decode step (ATen ops around the INT4 GEMVs)")
     ap.add_argument("--profile-shape", default=None, choices=[n for n, _, _ in LAYER_SHAPES] + [LM_HEAD[0]],
                     help="only run --launches launches of one shape (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)

@@ -125,6 +125,85 @@ int li4_int4_linear_noalloc(const void* x, const void* packed, const void* scale
                             int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
                             void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Fused decode-step operations.  The decode step of a Llama block is
+ *   h   = x + wo(attn(rope(wq(norm1(x))), rope(wk(norm1(x))), wv(norm1(x))))
+ *   out = h + w2(silu(w1(norm2(h))) * w3(norm2(h)))
+ * (llama/model.py:222-277, 310-315, 358-362).  li4_int4_linear_fused folds the
+ * RMSNorm into the GEMV's x staging and RoPE + KV-cache write, SwiGLU or the
+ * residual add into its epilogue, so a block is five launches: QKV, attention,
+ * wo, gate/up, w2.  The rounding points are the reference's: every GEMV output
+ * is rounded to fp16 before the epilogue works on it, and every intermediate
+ * the reference holds in fp16 is rounded to fp16 here too.
+ *
+ * Paired rows.  SwiGLU and RoPE combine two GEMV outputs.  These epilogues take
+ * the packed weight with its rows arranged so that rows 16t + j and 16t + 8 + j
+ * (j < 8) form pair 8t + j, which puts both values in one thread; N must then be
+ * a multiple of 16.
+ *   LI4_EPI_SWIGLU:   pair p = (row p of w1, row p of w3); y[m, p], y has N/2
+ *                     columns.
+ *   LI4_EPI_QKV_ROPE: the rows of [wq; wk; wv] (q_rows + k_rows + v_rows = N),
+ *                     pair p = rows (2p, 2p + 1), the (even, odd) pair that RoPE
+ *                     rotates as one complex number (llama/model.py:126-152).
+ * --------------------------------------------------------------------------- */
+typedef enum li4_epilogue_kind {
+  LI4_EPI_STORE = 0,     /* y = fp16(x W^T)                                          */
+  LI4_EPI_RESIDUAL = 1,  /* y = fp16(residual + fp16(x W^T))                         */
+  LI4_EPI_SWIGLU = 2,    /* y = fp16(fp16(silu(g)) * u), g, u = fp16 outputs of pair  */
+  LI4_EPI_QKV_ROPE = 3   /* RoPE on q, k pairs at position *pos; q -> q_out,
+                            k and v -> cache_k / cache_v at row *pos (y unused)       */
+} li4_epilogue_kind;
+
+typedef struct li4_fusion {
+  /* Prologue: x -> fp16(fp16(x * rsqrt(mean(x^2) + eps)) * norm_weight), the
+   * mean over all K columns in fp32 (llama/model.py:61-75).  NULL = no norm. */
+  const void* norm_weight;  /* fp16 [K] */
+  float norm_eps;
+  int epilogue;             /* li4_epilogue_kind */
+  /* LI4_EPI_RESIDUAL: fp16 [M, N], row stride stride_rm elements; may equal y. */
+  const void* residual;
+  int64_t stride_rm;
+  /* LI4_EPI_QKV_ROPE (M = batch rows, one new token each, all at *pos). */
+  int64_t q_rows, k_rows, head_dim;         /* v_rows = N - q_rows - k_rows           */
+  const int64_t* pos;                       /* device scalar                         */
+  const float* rope_cos;                    /* [positions, head_dim / 2] fp32         */
+  const float* rope_sin;
+  int64_t rope_stride;                      /* elements between positions             */
+  void* q_out;                              /* fp16 [M, q_rows], row stride stride_qm */
+  int64_t stride_qm;
+  void* cache_k;                            /* fp16 [batch, seq, k_rows] with strides */
+  void* cache_v;                            /* (elements) cache_stride_b / _s         */
+  int64_t cache_stride_b, cache_stride_s;
+} li4_fusion;
+
+/* li4_int4_linear with a fused prologue / epilogue (`fusion` NULL = plain).
+ * Uses the streaming-warp or tile kernel (group_size >= 128).  The workspace
+ * rule is li4_int4_linear's.  Replaces, inside one launch: RMSNorm.forward
+ * (llama/model.py:61-75), apply_rotary_emb and the cache writes of
+ * Attention.forward (:126-152, :251-262), F.silu(w1(x)) * w3(x) (:315) and the
+ * residual adds of TransformerBlock.forward (:358-362). */
+int li4_int4_linear_fused(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                          int64_t M, int64_t N, int64_t K, int64_t group_size,
+                          int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
+                          const li4_fusion* fusion, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Decode attention for one new token per sequence at position *pos:
+ *   out[b, h] = softmax(q[b, h] . K[b, 0..pos, h / rep]^T / sqrt(head_dim)) V[b, 0..pos, h / rep]
+ * with rep = n_heads / n_kv_heads (grouped-query attention without the
+ * repeat_kv copies).  Scores are rounded to fp16 (the reference's fp16
+ * matmul), the softmax is fp32, the probabilities are rounded to fp16 and
+ * P.V accumulates in fp32 (llama/model.py:266-275).  q: fp16 [batch, n_heads *
+ * head_dim] (row stride stride_qb); cache_k / cache_v: fp16 [batch, seq,
+ * n_kv_heads, head_dim] with element strides cache_stride_b / cache_stride_s;
+ * out: fp16 [batch, n_heads * head_dim] (row stride stride_ob).  head_dim 32, 64 or 128;
+ * *pos < max_seq (the kernel clamps to max_seq - 1).
+ * Replaces: Attention.forward's repeat_kv, two matmuls and softmax
+ * (llama/model.py:262-275) at seqlen 1. */
+int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, const void* cache_v,
+                         int64_t cache_stride_b, int64_t cache_stride_s, void* out, int64_t stride_ob,
+                         int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                         const int64_t* pos, int64_t max_seq, void* stream);
+
 /* w16[N, K] (fp16, row stride stride_wn elements) = dequantized weights,
  * bit-identical to the reference's fp32 (q - zero) * scale rounded to fp16.
  * Replaces: QuantizedLinear.dequantize_packed (llama/quantize.py:78-104) and

@@ -1,0 +1,299 @@
+// li4_attention.cu -- decode attention (one new token per sequence), sm_100a.
+//
+// One CTA per (KV head, sequence): it reads that head's cached keys and values
+// once for all `REP` query heads that share them (grouped-query attention
+// without the reference's repeat_kv copies, llama/model.py:155-164, 265-266).
+// The arithmetic follows the reference's fp16 decode step
+// (llama/model.py:266-275):
+//   s = fp16(q . k)             fp16 matmul, fp32 accumulation
+//   s = fp16(s / sqrt(d))
+//   p = fp16(softmax_fp32(s))   softmax(scores.float()).type_as(q)
+//   o = fp16(sum_j p_j v_j)     fp16 matmul, fp32 accumulation
+// The position lives in device memory, so one captured CUDA graph serves every
+// position: keys 0 .. *pos are attended (the reference's cache slice
+// [:start_pos + 1]).
+#include "li4_common.cuh"
+#include "li4_internal.h"
+
+#include <mutex>
+#include <vector>
+
+namespace li4 {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+// DPL = HD / 32 consecutive fp16 values of one cached row as floats.
+template <int DPL>
+__device__ __forceinline__ void load_lane_dims(const __half* p, float (&v)[DPL]) {
+  if constexpr (DPL == 1) {
+    v[0] = __half2float(*p);
+  } else if constexpr (DPL == 2) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = f.x;
+    v[1] = f.y;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = b.x;
+    v[3] = b.y;
+  }
+}
+
+struct AttnArgs {
+  const __half* q;
+  long long sqb;
+  const __half* cache_k;
+  const __half* cache_v;
+  long long csb, css;
+  __half* out;
+  long long sob;
+  int n_kv_heads;
+  const long long* pos;
+  int max_seq;
+};
+
+template <int REP, int HD>
+__global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __grid_constant__ AttnArgs a) {
+  constexpr int kHeadDim = HD;
+  constexpr int DPL = HD / 32;  // dims per lane in P.V
+  extern __shared__ __align__(16) float smem[];
+  float* q_s = smem;                              // [REP][HD]
+  float* red = q_s + REP * kHeadDim;              // [warps][REP][HD]
+  float* scores = red + kAttnWarps * REP * kHeadDim;  // [REP][max_seq]
+  __shared__ float s_max[kAttnWarps][REP], s_sum[kAttnWarps][REP];
+
+  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_launch_dependents();
+  pdl_wait_primary();  // q and the cache row of this step come from the preceding kernel
+
+  long long p = *a.pos;
+  p = p < 0 ? 0 : (p >= a.max_seq ? a.max_seq - 1 : p);
+  const int L = (int)p + 1;
+  const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * kHeadDim;
+  const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * kHeadDim;
+
+  for (int t = tid; t < REP * kHeadDim; t += kAttnThreads)
+    q_s[t] = __half2float(a.q[(long long)b * a.sqb + (long long)kvh * REP * kHeadDim + t]);
+  __syncthreads();
+
+  // scores: one key per thread, REP dot products over its HD dims
+  const float inv_scale = 1.0f / sqrtf((float)kHeadDim);
+  float mx[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) mx[r] = -INFINITY;
+  for (int j = tid; j < L; j += kAttnThreads) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kbase + (long long)j * a.css);
+    float dot[REP];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) dot[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kHeadDim / 8; ++c) {
+      const uint4 kv = kr[c];
+      const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+#pragma unroll
+        for (int r = 0; r < REP; ++r) {
+          dot[r] = fmaf(q_s[r * kHeadDim + c * 8 + 2 * e], kf.x, dot[r]);
+          dot[r] = fmaf(q_s[r * kHeadDim + c * 8 + 2 * e + 1], kf.y, dot[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float s16 = __half2float(__float2half_rn(dot[r]));
+      const float s = __half2float(__float2half_rn(s16 * inv_scale));  // torch divides by a scalar as a product with its reciprocal
+      scores[r * a.max_seq + j] = s;
+      mx[r] = fmaxf(mx[r], s);
+    }
+  }
+  // softmax over j < L per head, fp32
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float v = mx[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) s_max[warp][r] = v;
+  }
+  __syncthreads();
+  float gmax[REP], sum[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float v = s_max[0][r];
+#pragma unroll
+    for (int w = 1; w < kAttnWarps; ++w) v = fmaxf(v, s_max[w][r]);
+    gmax[r] = v;
+    sum[r] = 0.f;
+  }
+  for (int j = tid; j < L; j += kAttnThreads) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float e = expf(scores[r * a.max_seq + j] - gmax[r]);
+      scores[r * a.max_seq + j] = e;
+      sum[r] += e;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float v = sum[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) s_sum[warp][r] = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) v += s_sum[w][r];
+    sum[r] = v;
+  }
+  for (int j = tid; j < L; j += kAttnThreads) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r)
+      scores[r * a.max_seq + j] = __half2float(__float2half_rn(scores[r * a.max_seq + j] / sum[r]));
+  }
+  __syncthreads();
+
+  // P.V: warp w takes keys w, w + 8, ...; lane holds dims DPL lane .. DPL lane + DPL - 1
+  float acc[REP][DPL];
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
+  int j = warp;
+  for (; j + 3 * kAttnWarps < L; j += 4 * kAttnWarps) {
+    float v4[4][DPL];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) load_lane_dims<DPL>(vbase + (long long)(j + u * kAttnWarps) * a.css + DPL * lane, v4[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const float pj = scores[r * a.max_seq + j + u * kAttnWarps];
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[r][e] = fmaf(pj, v4[u][e], acc[r][e]);
+      }
+  }
+  for (; j < L; j += kAttnWarps) {
+    float vv[DPL];
+    load_lane_dims<DPL>(vbase + (long long)j * a.css + DPL * lane, vv);
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float pj = scores[r * a.max_seq + j];
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) acc[r][e] = fmaf(pj, vv[e], acc[r][e]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) red[(warp * REP + r) * kHeadDim + DPL * lane + e] = acc[r][e];
+  __syncthreads();
+  for (int t = tid; t < REP * kHeadDim; t += kAttnThreads) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) v += red[w * REP * kHeadDim + t];
+    a.out[(long long)b * a.sob + (long long)kvh * REP * kHeadDim + t] = __float2half_rn(v);
+  }
+}
+
+static size_t attn_smem_bytes(int rep, int head_dim, int max_seq) {
+  return sizeof(float) * ((size_t)rep * head_dim * (1 + kAttnWarps) + (size_t)rep * max_seq);
+}
+
+template <int REP, int HD>
+static int launch_attention(const AttnArgs& a, int batch, size_t smem, cudaStream_t stream) {
+  auto kernel = decode_attention_kernel<REP, HD>;
+  if (smem > 48 * 1024) {
+    static std::mutex mu;
+    static std::vector<std::pair<int, size_t>> raised;  // (device, bytes) of this instantiation
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    bool ok = false;
+    for (auto& e : raised)
+      if (e.first == dev && e.second >= smem) ok = true;
+    if (!ok) {
+      const int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                "decode_attention: cudaFuncSetAttribute");
+      if (rc != LI4_OK) return rc;
+      raised.emplace_back(dev, smem);
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.n_kv_heads, (unsigned)batch, 1);
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, a), "decode_attention: kernel launch");
+}
+
+}  // namespace li4
+
+extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, const void* cache_v,
+                                    int64_t cache_stride_b, int64_t cache_stride_s, void* out, int64_t stride_ob,
+                                    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                                    const int64_t* pos, int64_t max_seq, void* stream) {
+  using namespace li4;
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: head_dim=%lld (32, 64 or 128)", (long long)head_dim);
+  if (batch < 0 || n_kv_heads < 1 || n_heads < n_kv_heads || n_heads % n_kv_heads != 0 || max_seq < 1)
+    return set_error(LI4_ERR_INVALID_ARG, "decode_attention: batch=%lld n_heads=%lld n_kv_heads=%lld max_seq=%lld",
+                     (long long)batch, (long long)n_heads, (long long)n_kv_heads, (long long)max_seq);
+  const int64_t rep = n_heads / n_kv_heads;
+  if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
+    return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: n_heads / n_kv_heads = %lld (1, 2, 4 or 8)",
+                     (long long)rep);
+  if (!q || !cache_k || !cache_v || !out || !pos)
+    return set_error(LI4_ERR_INVALID_ARG, "decode_attention: null pointer");
+  if (stride_qb < n_heads * head_dim || stride_ob < n_heads * head_dim || cache_stride_s < n_kv_heads * head_dim ||
+      cache_stride_b < cache_stride_s * max_seq)
+    return set_error(LI4_ERR_INVALID_ARG, "decode_attention: strides smaller than the rows");
+  if (!aligned16(cache_k) || !aligned16(cache_v) || cache_stride_s % 8 != 0 || cache_stride_b % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(q) & 1u) || (reinterpret_cast<uintptr_t>(out) & 1u))
+    return set_error(LI4_ERR_ALIGNMENT, "decode_attention: cache rows must be 16-byte aligned");
+  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, (int)max_seq);
+  if (max_seq > (1 << 20) || smem > 200 * 1024)
+    return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld needs %zu bytes of shared memory",
+                     (long long)max_seq, smem);
+  if (batch == 0) return LI4_OK;
+  AttnArgs a;
+  a.q = static_cast<const __half*>(q);
+  a.sqb = stride_qb;
+  a.cache_k = static_cast<const __half*>(cache_k);
+  a.cache_v = static_cast<const __half*>(cache_v);
+  a.csb = cache_stride_b;
+  a.css = cache_stride_s;
+  a.out = static_cast<__half*>(out);
+  a.sob = stride_ob;
+  a.n_kv_heads = (int)n_kv_heads;
+  a.pos = reinterpret_cast<const long long*>(pos);
+  a.max_seq = (int)max_seq;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  const int sel = (int)rep * 1000 + (int)head_dim;
+  switch (sel) {
+#define LI4_ATTN_CASE(R, H) \
+  case R * 1000 + H: rc = launch_attention<R, H>(a, (int)batch, smem, s); break;
+    LI4_ATTN_CASE(1, 32) LI4_ATTN_CASE(2, 32) LI4_ATTN_CASE(4, 32) LI4_ATTN_CASE(8, 32)
+    LI4_ATTN_CASE(1, 64) LI4_ATTN_CASE(2, 64) LI4_ATTN_CASE(4, 64) LI4_ATTN_CASE(8, 64)
+    LI4_ATTN_CASE(1, 128) LI4_ATTN_CASE(2, 128) LI4_ATTN_CASE(4, 128) LI4_ATTN_CASE(8, 128)
+#undef LI4_ATTN_CASE
+    default: rc = set_error(LI4_ERR_UNSUPPORTED, "decode_attention: rep=%lld head_dim=%lld", (long long)rep,
+                            (long long)head_dim);
+  }
+  if (rc == LI4_OK) clear_error();
+  return rc;
+}

@@ -59,7 +59,120 @@ struct GemvArgs {
   int ks_per_split;              // ksteps per K range
   float* partial;                // [split][M][N] fp32, split > 1 only
   unsigned* counters;            // [n_tiles] arrival counters, split > 1 only
+  // li4_int4_linear_fused (zero / null otherwise)
+  const __half* norm_w;          // RMSNorm weight [K] applied while staging x
+  float norm_eps;
+  int epi;                       // li4_epilogue_kind
+  const __half* res;             // LI4_EPI_RESIDUAL
+  long long srm;
+  int q_rows, k_rows, head_dim;  // LI4_EPI_QKV_ROPE
+  const long long* pos;
+  const float* rope_cos;
+  const float* rope_sin;
+  long long rope_stride;
+  __half* q_out;
+  long long sqm;
+  __half* cache_k;
+  __half* cache_v;
+  long long cache_sb, cache_ss;
 };
+
+// ---------------------------------------------------------------------------
+// Fused epilogues.  Every GEMV output is rounded to fp16 first, as the
+// reference's fp16 Linear output is, and each later fp16 intermediate of the
+// reference is rounded again at the same point.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool epi_paired(const GemvArgs& a) { return a.epi >= LI4_EPI_SWIGLU; }
+
+// One output y[m, row] (LI4_EPI_STORE / LI4_EPI_RESIDUAL).
+__device__ __noinline__ void emit_one(const GemvArgs& a, int m, int row, float v) {
+  __half h = __float2half_rn(v);
+  if (a.epi == LI4_EPI_RESIDUAL)  // h = x + wo(...): fp16 + fp16 (llama/model.py:358-362)
+    h = __float2half_rn(__half2float(h) + __half2float(a.res[(long long)m * a.srm + row]));
+  a.y[(long long)m * a.sym + row] = h;
+}
+
+// Pair `pair` of a paired-row weight: v0 from tile row j, v1 from tile row j + 8.
+__device__ __noinline__ void emit_pair(const GemvArgs& a, int m, int pair, float v0, float v1) {
+  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+  if (a.epi == LI4_EPI_SWIGLU) {  // F.silu(w1(x)) * w3(x) (llama/model.py:315)
+    const float g = __half2float(h0);
+    const float sg = __half2float(__float2half_rn(g / (1.0f + expf(-g))));
+    a.y[(long long)m * a.sym + pair] = __float2half_rn(sg * __half2float(h1));
+    return;
+  }
+  // LI4_EPI_QKV_ROPE: rows (2 pair, 2 pair + 1) of [q | k | v]
+  const int row = 2 * pair;
+  const long long p = *a.pos;
+  if (row < a.q_rows + a.k_rows) {  // (even, odd) as one complex number times e^{i pos f_i} (llama/model.py:126-152)
+    const int d = row < a.q_rows ? row : row - a.q_rows;
+    const int i = (d % a.head_dim) >> 1;
+    const float c = a.rope_cos[p * a.rope_stride + i], s = a.rope_sin[p * a.rope_stride + i];
+    const float x0 = __half2float(h0), x1 = __half2float(h1);
+    const __half2 o = __floats2half2_rn(x0 * c - x1 * s, x0 * s + x1 * c);
+    __half* dst = row < a.q_rows ? a.q_out + (long long)m * a.sqm + d
+                                 : a.cache_k + (long long)m * a.cache_sb + p * a.cache_ss + d;
+    *reinterpret_cast<__half2*>(dst) = o;
+  } else {  // v goes to the cache unrotated (llama/model.py:257-258)
+    const int d = row - a.q_rows - a.k_rows;
+    *reinterpret_cast<__half2*>(a.cache_v + (long long)m * a.cache_sb + p * a.cache_ss + d) = __halves2half2(h0, h1);
+  }
+}
+
+// The reduced outputs of one 16-row tile, value(r, m) for local row r, emitted
+// by threads tid = 0 .. nthr-1 of the caller's group.
+template <typename F>
+__device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, int nthr, F value) {
+  const int row0 = tile * 16;
+  if (epi_paired(a)) {  // N is a multiple of 16: full tiles
+    for (int idx = tid; idx < 8 * a.M; idx += nthr) {
+      const int j = idx / a.M, m = idx - j * a.M;
+      emit_pair(a, m, tile * 8 + j, value(j, m), value(j + 8, m));
+    }
+  } else {
+    const int rows = min(16, a.N - row0);
+    for (int idx = tid; idx < rows * a.M; idx += nthr) {
+      const int r = idx / a.M, m = idx - r * a.M;
+      emit_one(a, m, row0 + r, value(r, m));
+    }
+  }
+}
+
+// Per-row 1 / rms of x for the RMSNorm prologue: s_rstd[m] = rsqrt(mean_k x[m,k]^2 + eps),
+// the mean in fp32 over all K columns (llama/model.py:61).  All THREADS threads call it.
+template <int THREADS>
+__device__ __forceinline__ void compute_rstd(const GemvArgs& a, float* s_rstd) {
+  __shared__ float part[THREADS / 32][LI4_MAX_M];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int m = 0; m < a.M; ++m) {
+    const __half* row = a.x + (long long)m * a.sxm;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < a.K; k += THREADS) {
+      const float v = __half2float(row[k]);
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) part[warp][m] = ss;
+  }
+  __syncthreads();
+  if (threadIdx.x < a.M) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) t += part[w][threadIdx.x];
+    s_rstd[threadIdx.x] = rsqrtf(t / (float)a.K + a.norm_eps);
+  }
+  __syncthreads();
+}
+
+// fp16(fp16(x * rstd) * w): RMSNorm's output cast (type_as) and its fp16 weight product.
+__device__ __forceinline__ uint32_t norm_pair(uint32_t xv, uint32_t wv, float rstd) {
+  const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xv));
+  const float2 wf = __half22float2(*reinterpret_cast<const __half2*>(&wv));
+  const float2 n = __half22float2(__floats2half2_rn(xf.x * rstd, xf.y * rstd));
+  const __half2 o = __floats2half2_rn(n.x * wf.x, n.y * wf.y);
+  return *reinterpret_cast<const uint32_t*>(&o);
+}
 
 // ---------------------------------------------------------------------------
 // x staging.  Block b = ((ks * NT + nt) * M8 + m8) * 4 + quad holds the 32
@@ -89,11 +202,13 @@ __device__ __forceinline__ uint4 lds128_ordered(const uint8_t* p) {
   return r;
 }
 
-template <int NT>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs) {
+// s_rstd: per-row RMSNorm factors (compute_rstd) when a.norm_w is set, else unused.
+template <int NT, int THREADS = kThreads>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
+                                        const float* s_rstd = nullptr) {
   const int total = nks * NT * M8 * 16;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
-  for (int idx = threadIdx.x; idx < total; idx += kThreads) {
+  for (int idx = threadIdx.x; idx < total; idx += THREADS) {
     const int w = idx & 3;
     const int block = idx >> 2;
     const int quad = block & 3;
@@ -115,6 +230,14 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
+      }
+      if (a.norm_w != nullptr) {  // 16-byte aligned weight (checked by the host)
+        const uint4 w = *reinterpret_cast<const uint4*>(a.norm_w + k);
+        const float r = s_rstd[m];
+        u[0] = norm_pair(u[0], w.x, r);
+        u[1] = norm_pair(u[1], w.y, r);
+        u[2] = norm_pair(u[2], w.z, r);
+        u[3] = norm_pair(u[3], w.w, r);
       }
       out.x = __byte_perm(u[0], u[2], 0x5410);  // (x0, x4)
       out.y = __byte_perm(u[0], u[2], 0x7632);  // (x1, x5)
@@ -639,7 +762,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
     stream_advance<KSPLIT>(lc, units_per_tile, tile_step);
   }
   pdl_wait_primary();  // x is written by the preceding kernel
-  stage_x<NT>(a, ks0, nks, M8, xs);
+  __shared__ float s_rstd[LI4_MAX_M];
+  if (a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
+  stage_x<NT, kStreamThreads>(a, ks0, nks, M8, xs, s_rstd);
   __syncthreads();
 
   // this thread's B-fragment offsets inside one (kstep, n-tile) group
@@ -678,16 +803,26 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
         const int rows = min(16, a.N - row0);
         if (!KSPLIT) {
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
+          for (int nt = 0; nt < NT; ++nt) {
+            if (a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
-              if (r < rows && m < a.M) {
-                if (a.split == 1) a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(acc[nt][e]);
-                else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
+              for (int e = 0; e < 2; ++e) {
+                const int m = nt * 8 + 2 * quad + e;
+                if (m < a.M) emit_pair(a, m, tile * 8 + grp, acc[nt][e], acc[nt][e + 2]);
               }
-              acc[nt][e] = 0.f;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
+                if (r < rows && m < a.M) {
+                  if (a.split == 1) emit_one(a, m, row0 + r, acc[nt][e]);
+                  else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
+                }
+              }
             }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+          }
           if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
             __threadfence();
             __syncwarp();
@@ -696,12 +831,11 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
               __threadfence();
-              for (int idx = lane; idx < rows * a.M; idx += 32) {
-                const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+              emit_tile(a, tile, lane, 32, [&](int r, int m) {
                 float v = 0.f;
                 for (int sp = 0; sp < a.split; ++sp) v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
-                a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
-              }
+                return v;
+              });
               __syncwarp();
               if (lane == 0) a.counters[tile] = 0u;
             }
@@ -716,13 +850,19 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               acc[nt][e] = 0.f;
             }
           __syncthreads();
-          for (int idx = threadIdx.x; idx < rows * a.M; idx += kStreamThreads) {
-            const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+          auto tile_sum = [&](int r, int m) {
             float v = 0.f;
 #pragma unroll
             for (int w = 0; w < kStreamWarps; ++w) v += rb[(w * 16 + r) * COLS + m];
-            if (a.split == 1) a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
-            else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = v;
+            return v;
+          };
+          if (a.split == 1) {
+            emit_tile(a, tile, threadIdx.x, kStreamThreads, tile_sum);
+          } else {
+            for (int idx = threadIdx.x; idx < rows * a.M; idx += kStreamThreads) {
+              const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+              a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = tile_sum(r, m);
+            }
           }
           if (a.split > 1) {
             __threadfence();  // every writer publishes its partials before the arrival count
@@ -733,13 +873,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               last = __shfl_sync(0xffffffffu, last, 0);
               if (last) {
                 __threadfence();
-                for (int idx = lane; idx < rows * a.M; idx += 32) {
-                  const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
+                emit_tile(a, tile, lane, 32, [&](int r, int m) {
                   float v = 0.f;
                   for (int sp = 0; sp < a.split; ++sp)
                     v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
-                  a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
-                }
+                  return v;
+                });
                 __syncwarp();
                 if (lane == 0) a.counters[tile] = 0u;
               }
@@ -886,7 +1025,9 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
     for (int d = 0; d < D; ++d) tile_load<RT>(buf[d], a, cur, d);
   }
   pdl_wait_primary();  // x is written by the preceding kernel
-  stage_x<NT>(a, ks0, NKS, M8, xs);
+  __shared__ float s_rstd[LI4_MAX_M];
+  if (a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
+  stage_x<NT, kStreamThreads>(a, ks0, NKS, M8, xs, s_rstd);
   __syncthreads();
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
@@ -921,17 +1062,26 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
 #pragma unroll
     for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+      for (int nt = 0; nt < NT; ++nt) {
+        if (a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of each 16-row subtile are a pair
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int m = nt * 8 + 2 * quad + e;
+            if (m < a.M && row0 + rt * 16 < a.N)
+              emit_pair(a, m, (tile * RT + rt) * 8 + grp, acc[rt][nt][e], acc[rt][nt][e + 2]);
+          }
+          continue;
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = row0 + rt * 16 + grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
           if (r < a.N && m < a.M) {
-            if (a.split == 1) a.y[(long long)m * a.sym + r] = __float2half_rn(acc[rt][nt][e]);
+            if (a.split == 1) emit_one(a, m, r, acc[rt][nt][e]);
             else a.partial[((long long)blockIdx.y * a.M + m) * a.N + r] = acc[rt][nt][e];
           }
         }
+      }
     if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
-      const int rows = min(ROWS, a.N - row0);
       __threadfence();
       __syncwarp();
       unsigned last = 0;
@@ -939,11 +1089,16 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
         __threadfence();
-        for (int idx = lane; idx < rows * a.M; idx += 32) {
-          const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
-          float v = 0.f;
-          for (int sp = 0; sp < a.split; ++sp) v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
-          a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(v);
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt) {
+          const int sub = tile * RT + rt;
+          if (sub * 16 >= a.N) break;
+          emit_tile(a, sub, lane, 32, [&](int r, int m) {
+            float v = 0.f;
+            for (int sp = 0; sp < a.split; ++sp)
+              v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + sub * 16 + r]);
+            return v;
+          });
         }
         __syncwarp();
         if (lane == 0) a.counters[tile] = 0u;
@@ -977,7 +1132,7 @@ struct Plan {
 static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int kernel_req, int rows_req,
-                     int split_req, int max_ctas, Plan* p) {
+                     int split_req, int max_ctas, Plan* p, bool fused = false) {
   if (M < 1 || M > LI4_MAX_M)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: M=%lld outside 1..%d", (long long)M, LI4_MAX_M);
   if (N < 1) return set_error(LI4_ERR_INVALID_ARG, "int4_linear: N=%lld < 1", (long long)N);
@@ -1001,6 +1156,12 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
   }
+  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE)
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp "
+                     "and tile kernels (group_size >= 128)");
+  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE)
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp "
+                     "and tile kernels (group_size >= 128)");
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel takes M <= 8 (M=%lld)", (long long)M);
   if (kernel == LI4_KERNEL_STREAM && (group < 128 || K == 0))
@@ -1257,17 +1418,73 @@ static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
   }
 }
 
+static bool aligned4(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3u) == 0; }
+
+// Preconditions of the fused prologue / epilogues (li4_fusion).
+static int check_fusion(const li4_fusion& f, int64_t M, int64_t N, int64_t K) {
+  if (f.norm_weight != nullptr) {
+    if (!aligned16(f.norm_weight))
+      return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: norm_weight must be 16-byte aligned");
+    if (!(f.norm_eps >= 0.f)) return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: norm_eps must be >= 0");
+  }
+  switch (f.epilogue) {
+    case LI4_EPI_STORE:
+      return LI4_OK;
+    case LI4_EPI_RESIDUAL:
+      if (!f.residual || f.stride_rm < N || (reinterpret_cast<uintptr_t>(f.residual) & 1u))
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: residual epilogue needs a residual [M, N] "
+                         "(row stride >= N)");
+      return LI4_OK;
+    case LI4_EPI_SWIGLU:
+      if (N % 16 != 0)
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: SwiGLU pairs need N %% 16 == 0 (N=%lld)",
+                         (long long)N);
+      return LI4_OK;
+    case LI4_EPI_QKV_ROPE: {
+      const int64_t v_rows = N - f.q_rows - f.k_rows;
+      if (f.head_dim < 2 || f.head_dim % 2 != 0 || f.q_rows < 0 || f.k_rows <= 0 || f.q_rows % 16 != 0 ||
+          f.k_rows % 16 != 0 || f.q_rows % f.head_dim != 0 || f.k_rows % f.head_dim != 0 || v_rows != f.k_rows)
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: QKV epilogue needs q_rows, k_rows multiples of "
+                         "16 and of head_dim, and N = q_rows + 2 k_rows (N=%lld q=%lld k=%lld head_dim=%lld)",
+                         (long long)N, (long long)f.q_rows, (long long)f.k_rows, (long long)f.head_dim);
+      if (!f.pos || !f.rope_cos || !f.rope_sin || (f.q_rows > 0 && !f.q_out) || !f.cache_k || !f.cache_v)
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: QKV epilogue needs pos, rope_cos/sin, q_out and "
+                         "cache_k/v");
+      if (f.rope_stride < f.head_dim / 2 || f.stride_qm < f.q_rows || f.cache_stride_s < f.k_rows ||
+          f.cache_stride_b < f.cache_stride_s)
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: QKV epilogue strides smaller than the rows");
+      if (!aligned4(f.cache_k) || !aligned4(f.cache_v) || (f.q_rows > 0 && !aligned4(f.q_out)) ||
+          f.stride_qm % 2 != 0 || f.cache_stride_b % 2 != 0 || f.cache_stride_s % 2 != 0)
+        return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: q_out / cache rows must be 4-byte aligned "
+                         "(pairs are stored as half2)");
+      (void)M;
+      (void)K;
+      return LI4_OK;
+    }
+    default:
+      return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: unknown epilogue %d", f.epilogue);
+  }
+}
+
 static int int4_linear_impl(const void* x, const void* packed, const void* scale, const void* zero, void* y,
                             int64_t M, int64_t N, int64_t K, int64_t group, int64_t sxm, int64_t spn, int64_t ssn,
                             int64_t sym, void* workspace, size_t workspace_bytes, void* stream, int kernel,
-                            int rows_req, int split_req, int max_ctas) {
+                            int rows_req, int split_req, int max_ctas, const li4_fusion* f = nullptr) {
   Plan p = {};
   const int sm = current_sm_count();
-  int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p);
+  const bool fused = f != nullptr && (f->norm_weight != nullptr || f->epilogue != LI4_EPI_STORE);
+  int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p, fused);
   if (rc != LI4_OK) return rc;
-  if (!x || !packed || !scale || !zero || !y)
+  const int epi = f ? f->epilogue : LI4_EPI_STORE;
+  // columns of y: N, N/2 for SwiGLU pairs, none for the QKV epilogue (outputs go to q_out and the cache)
+  const int64_t y_cols = epi == LI4_EPI_SWIGLU ? N / 2 : (epi == LI4_EPI_QKV_ROPE ? 0 : N);
+  if (fused) {
+    rc = check_fusion(*f, M, N, K);
+    if (rc != LI4_OK) return rc;
+  }
+  if (!x || !packed || !scale || !zero || (!y && y_cols > 0))
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: null tensor pointer");
-  if (sxm < K || sym < N || spn < K / 2 || ssn < (K > 0 ? K / group : 0))
+  if (sxm < K || sym < y_cols || spn < K / 2 || ssn < (K > 0 ? K / group : 0))
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: row strides (x %lld, packed %lld, scale %lld, y %lld) "
                      "smaller than the rows", (long long)sxm, (long long)spn, (long long)ssn, (long long)sym);
   if (!aligned16(packed) || spn % 16 != 0)
@@ -1281,7 +1498,7 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     // the tile kernel addresses rows with 32-bit offsets
     if (kernel != LI4_KERNEL_AUTO)
       return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: the tile kernel needs packed / scale offsets below 2^32");
-    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p);
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
     if (rc != LI4_OK) return rc;
   }
   if (p.ws_bytes > 0) {
@@ -1290,7 +1507,27 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
                        "workspace, got %zu", p.split, p.ws_bytes, workspace ? workspace_bytes : (size_t)0);
     if (!aligned16(workspace)) return set_error(LI4_ERR_ALIGNMENT, "int4_linear: workspace must be 16-byte aligned");
   }
-  GemvArgs args;
+  GemvArgs args = {};
+  if (fused) {
+    args.norm_w = static_cast<const __half*>(f->norm_weight);
+    args.norm_eps = f->norm_eps;
+    args.epi = epi;
+    args.res = static_cast<const __half*>(f->residual);
+    args.srm = f->stride_rm;
+    args.q_rows = (int)f->q_rows;
+    args.k_rows = (int)f->k_rows;
+    args.head_dim = (int)f->head_dim;
+    args.pos = reinterpret_cast<const long long*>(f->pos);
+    args.rope_cos = f->rope_cos;
+    args.rope_sin = f->rope_sin;
+    args.rope_stride = f->rope_stride;
+    args.q_out = static_cast<__half*>(f->q_out);
+    args.sqm = f->stride_qm;
+    args.cache_k = static_cast<__half*>(f->cache_k);
+    args.cache_v = static_cast<__half*>(f->cache_v);
+    args.cache_sb = f->cache_stride_b;
+    args.cache_ss = f->cache_stride_s;
+  }
   args.x = static_cast<const __half*>(x);
   args.packed = static_cast<const uint8_t*>(packed);
   args.scale = static_cast<const __half*>(scale);
@@ -1344,6 +1581,14 @@ extern "C" int li4_int4_linear_ex(const void* x, const void* packed, const void*
                                   int max_ctas) {
   return li4::int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn,
                                stride_ym, workspace, workspace_bytes, stream, kernel, rows_per_cta, split, max_ctas);
+}
+
+extern "C" int li4_int4_linear_fused(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                                     int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t stride_xm,
+                                     int64_t stride_pn, int64_t stride_sn, int64_t stride_ym, const li4_fusion* fusion,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  return li4::int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn,
+                               stride_ym, workspace, workspace_bytes, stream, LI4_KERNEL_AUTO, 0, 0, 0, fusion);
 }
 
 // ---------------------------------------------------------------------------

@@ -31,6 +31,34 @@ _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
 _INT = ctypes.c_int
 
+LI4_EPI_STORE, LI4_EPI_RESIDUAL, LI4_EPI_SWIGLU, LI4_EPI_QKV_ROPE = 0, 1, 2, 3
+
+
+class Fusion(ctypes.Structure):
+    """struct li4_fusion (include/llama_int4_b200.h): fused prologue / epilogue of one GEMV."""
+
+    _fields_ = [
+        ("norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float),
+        ("epilogue", ctypes.c_int),
+        ("residual", ctypes.c_void_p),
+        ("stride_rm", ctypes.c_int64),
+        ("q_rows", ctypes.c_int64),
+        ("k_rows", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("pos", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("rope_stride", ctypes.c_int64),
+        ("q_out", ctypes.c_void_p),
+        ("stride_qm", ctypes.c_int64),
+        ("cache_k", ctypes.c_void_p),
+        ("cache_v", ctypes.c_void_p),
+        ("cache_stride_b", ctypes.c_int64),
+        ("cache_stride_s", ctypes.c_int64),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/llama_int4_b200.h
 SIGNATURES = {
     "li4_version": (_INT, []),
@@ -40,6 +68,9 @@ SIGNATURES = {
     "li4_int4_linear_ex": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
                                   _INT, _INT, _INT, _INT]),
     "li4_int4_linear_noalloc": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "li4_int4_linear_fused": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                     ctypes.POINTER(Fusion), _P, _SZ, _P]),
+    "li4_decode_attention": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "li4_dequantize": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_quantize": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
 }

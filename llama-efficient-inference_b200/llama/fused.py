@@ -1,0 +1,220 @@
+"""Fused INT4 decode step: five kernel launches per transformer block.
+
+The reference's decode step runs every block as ~45 ATen kernels around its
+seven INT4 linears (llama/model.py:222-277, 310-315, 358-362): two RMSNorms of
+five or six kernels each, RoPE through complex views, the cache writes,
+repeat_kv copies, two matmuls, the softmax, SiLU, the product and two residual
+adds.  Here a block is:
+
+  1. QKV GEMV   RMSNorm(attention_norm) while staging x; RoPE on q and k; q to a
+                buffer, k and v into the KV cache at row *pos  (li4_int4_linear_fused)
+  2. attention  grouped-query decode attention over cache rows 0..*pos
+                                                                (li4_decode_attention)
+  3. wo GEMV    h1 = h + wo(attn)                               (residual epilogue)
+  4. w1/w3 GEMV RMSNorm(ffn_norm) while staging h1; fp16(silu(g)) * u
+                                                                (SwiGLU epilogue)
+  5. w2 GEMV    h = h1 + w2(ffn)                                (residual epilogue)
+
+and the step ends with lm_head with the final RMSNorm fused into its staging.
+Under tensor parallelism the wo / w2 outputs are partial sums: they are stored
+plain, all-reduced, and added to the residual by torch.
+
+The fused epilogues pair two GEMV outputs in one thread.  They take weights
+whose rows are rearranged once, at construction (pair_permutation,
+swiglu_rows): the INT4 bytes, scales and zero points are the model's own,
+only their row order changes.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _native as native
+
+
+def pair_permutation(n: int) -> torch.Tensor:
+    """Row order that puts rows (2p, 2p + 1) at tile rows (16t + j, 16t + 8 + j), p = 8t + j.
+
+    new_rows = old_rows[pair_permutation(n)]; n must be a multiple of 16."""
+    if n % 16:
+        raise ValueError(f"paired rows need a multiple of 16 rows, got {n}")
+    return torch.arange(n).view(n // 16, 8, 2).permute(0, 2, 1).reshape(n)
+
+
+def swiglu_rows(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Interleave the rows of w1 (a) and w3 (b) in blocks of 8: tile t holds a[8t:8t+8] then b[8t:8t+8]."""
+    n = a.shape[0]
+    if b.shape != a.shape or n % 8:
+        raise ValueError(f"w1 / w3 rows must match and be a multiple of 8, got {tuple(a.shape)} {tuple(b.shape)}")
+    return torch.stack([a.reshape(n // 8, 8, -1), b.reshape(n // 8, 8, -1)], dim=1).reshape(2 * n, *a.shape[1:])
+
+
+def _qparams(lin):
+    return lin.packed_weight, lin.scale, lin.zero_point
+
+
+def fuse_qkv(wq, wk, wv):
+    """Packed / scale / zero of [wq; wk; wv] in paired-row order (LI4_EPI_QKV_ROPE)."""
+    parts = [_qparams(w) for w in (wq, wk, wv)]
+    perm = pair_permutation(sum(p[0].shape[0] for p in parts)).to(parts[0][0].device)
+    return tuple(torch.cat([p[i] for p in parts]).index_select(0, perm).contiguous() for i in range(3))
+
+
+def fuse_gate_up(w1, w3):
+    """Packed / scale / zero of w1 and w3 interleaved for the SwiGLU epilogue."""
+    a, b = _qparams(w1), _qparams(w3)
+    return tuple(swiglu_rows(a[i], b[i]).contiguous() for i in range(3))
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def int4_linear_fused(x: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, zp: torch.Tensor,
+                      y: Optional[torch.Tensor], fusion: native.Fusion, group_size: int = 128) -> None:
+    """One li4_int4_linear_fused launch on the current stream: x [M, K] fp16 (row-contiguous)."""
+    M, K = x.shape
+    N = packed.shape[0]
+    lib = native.lib()
+    dev = x.device
+    nbytes = lib.li4_int4_linear_workspace_bytes(M, N, K, group_size, 0)
+    ws = native.workspace(dev, nbytes) if nbytes else None
+    rc = lib.li4_int4_linear_fused(x.data_ptr(), packed.data_ptr(), scale.data_ptr(), zp.data_ptr(), _ptr(y),
+                                   M, N, K, group_size, x.stride(0), packed.stride(0), scale.stride(0),
+                                   y.stride(0) if y is not None else 0, ctypes.byref(fusion),
+                                   _ptr(ws), ws.numel() if ws is not None else 0, native.stream_ptr(dev))
+    native.check(rc, "int4_linear_fused")
+
+
+def decode_attention(q: torch.Tensor, cache_k: torch.Tensor, cache_v: torch.Tensor, pos: torch.Tensor,
+                     out: torch.Tensor, n_heads: int, n_kv_heads: int, max_seq: Optional[int] = None) -> None:
+    """out[b] = attention of q[b] (fp16 [B, n_heads * 64]) over cache rows 0..pos (cache [B', S, n_kv_heads, 64])."""
+    B = q.shape[0]
+    S = cache_k.shape[1]
+    if cache_k.stride(3) != 1 or cache_k.stride(2) != cache_k.shape[3] or cache_v.stride() != cache_k.stride():
+        raise RuntimeError("decode_attention: cache rows [n_kv_heads, head_dim] must be contiguous, K and V alike")
+    rc = native.lib().li4_decode_attention(q.data_ptr(), q.stride(0), cache_k.data_ptr(), cache_v.data_ptr(),
+                                           cache_k.stride(0), cache_k.stride(1), out.data_ptr(), out.stride(0),
+                                           B, n_heads, n_kv_heads, cache_k.shape[3], pos.data_ptr(),
+                                           S if max_seq is None else max_seq, native.stream_ptr(q.device))
+    native.check(rc, "decode_attention")
+
+
+class _Block:
+    """Fused weights and fusion descriptors of one transformer block."""
+
+    def __init__(self, layer, cos: torch.Tensor, sin: torch.Tensor):
+        att, ff = layer.attention, layer.feed_forward
+        for lin in (att.wq, att.wk, att.wv, att.wo, ff.w1, ff.w2, ff.w3):
+            if not hasattr(lin, "packed_weight") or lin.group_size != 128 or lin.bias is not None:
+                raise TypeError("the fused decode step needs INT4 group-128 QuantizedLinear layers without bias "
+                                "(run quantize_model first)")
+        self.att, self.ff = att, ff
+        self.qkv = fuse_qkv(att.wq, att.wk, att.wv)
+        self.gate_up = fuse_gate_up(ff.w1, ff.w3)
+        self.wo = _qparams(att.wo)
+        self.w2 = _qparams(ff.w2)
+        self.attn_norm = layer.attention_norm.weight.detach().contiguous()
+        self.attn_eps = float(layer.attention_norm.eps)
+        self.ffn_norm = layer.ffn_norm.weight.detach().contiguous()
+        self.ffn_eps = float(layer.ffn_norm.eps)
+        self.q_rows = att.wq.out_features
+        self.k_rows = att.wk.out_features
+        self.cos, self.sin = cos, sin
+
+
+class FusedDecoder:
+    """The decode step of a quantized Llama (llama.model.Llama) as fused kernels.
+
+    decode_step(tokens [bs, 1], pos int64 [1]) has the semantics of
+    Llama.decode_step and shares the model's KV caches, so a prefill through
+    Llama.forward followed by fused decode steps is the reference's generation
+    loop.  Every launch reads the position from `pos`: one CUDA graph of the
+    step serves every position.
+    """
+
+    def __init__(self, model):
+        self.model = model
+        p = model.params
+        emb = model.tok_embeddings.weight
+        self.device = emb.device
+        if emb.dtype != torch.float16:
+            raise TypeError("the fused decode step runs an fp16 model")
+        freqs = model.freqs_cis.to(self.device)
+        self.cos = freqs.real.float().contiguous()
+        self.sin = freqs.imag.float().contiguous()
+        self.blocks = [_Block(layer, self.cos, self.sin) for layer in model.layers]
+        self.out = _qparams(model.output)
+        self.final_norm = model.norm.weight.detach().contiguous()
+        self.final_eps = float(model.norm.eps)
+        self.dim = p.dim
+        self.head_dim = p.dim // p.n_heads
+        att0 = model.layers[0].attention
+        self.n_heads = att0.n_local_heads
+        self.n_kv_heads = att0.n_local_kv_heads
+        self.ffn = model.layers[0].feed_forward.w1.out_features
+        self.vocab_local = model.output.out_features
+        self._bufs = {}
+
+    def _buffers(self, bs: int):
+        b = self._bufs.get(bs)
+        if b is None:
+            f16 = dict(dtype=torch.float16, device=self.device)
+            b = {"h": torch.empty(bs, self.dim, **f16), "h1": torch.empty(bs, self.dim, **f16),
+                 "q": torch.empty(bs, self.n_heads * self.head_dim, **f16),
+                 "attn": torch.empty(bs, self.n_heads * self.head_dim, **f16),
+                 "ffn": torch.empty(bs, self.ffn, **f16), "part": torch.empty(bs, self.dim, **f16),
+                 "logits": torch.empty(bs, self.vocab_local, **f16)}
+            self._bufs[bs] = b
+        return b
+
+    def _allreduce_add(self, part: torch.Tensor, residual: torch.Tensor, out: torch.Tensor, group) -> None:
+        import torch.distributed as dist
+
+        dist.all_reduce(part, group=group)
+        torch.add(residual, part, out=out)
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        bs = tokens.shape[0]
+        buf = self._buffers(bs)
+        h, h1, q, attn, ffn, part = buf["h"], buf["h1"], buf["q"], buf["attn"], buf["ffn"], buf["part"]
+        torch.index_select(self.model.tok_embeddings.weight, 0, tokens.view(-1), out=h)
+        E = native
+        for blk in self.blocks:
+            att = blk.att
+            att._ensure_cache(h)
+            ck, cv = att.cache_k, att.cache_v
+            f = E.Fusion(norm_weight=blk.attn_norm.data_ptr(), norm_eps=blk.attn_eps, epilogue=E.LI4_EPI_QKV_ROPE,
+                         q_rows=blk.q_rows, k_rows=blk.k_rows, head_dim=self.head_dim, pos=pos.data_ptr(),
+                         rope_cos=blk.cos.data_ptr(), rope_sin=blk.sin.data_ptr(), rope_stride=blk.cos.stride(0),
+                         q_out=q.data_ptr(), stride_qm=q.stride(0), cache_k=ck.data_ptr(), cache_v=cv.data_ptr(),
+                         cache_stride_b=ck.stride(0), cache_stride_s=ck.stride(1))
+            int4_linear_fused(h, *blk.qkv, None, f)
+            decode_attention(q, ck, cv, pos, attn, self.n_heads, self.n_kv_heads)
+            if att.tp_group is None:
+                f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h.data_ptr(), stride_rm=h.stride(0))
+                int4_linear_fused(attn, *blk.wo, h1, f)
+            else:
+                int4_linear_fused(attn, *blk.wo, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
+                self._allreduce_add(part, h, h1, att.tp_group)
+            f = E.Fusion(norm_weight=blk.ffn_norm.data_ptr(), norm_eps=blk.ffn_eps, epilogue=E.LI4_EPI_SWIGLU)
+            int4_linear_fused(h1, *blk.gate_up, ffn, f)
+            if blk.ff.tp_group is None:
+                f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h1.data_ptr(), stride_rm=h1.stride(0))
+                int4_linear_fused(ffn, *blk.w2, h, f)
+            else:
+                int4_linear_fused(ffn, *blk.w2, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
+                self._allreduce_add(part, h1, h, blk.ff.tp_group)
+        logits = buf["logits"]
+        f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE)
+        int4_linear_fused(h, *self.out, logits, f)
+        if self.model.tp_group is not None:
+            import torch.distributed as dist
+
+            parts = [torch.empty_like(logits) for _ in range(self.model.tp_world)]
+            dist.all_gather(parts, logits, group=self.model.tp_group)
+            logits = torch.cat(parts, dim=-1)
+        return logits.float().view(bs, 1, -1)

@@ -26,6 +26,9 @@ Additions:
   * Tensor parallelism (llama/tp.py) sets n_local_heads / n_local_kv_heads and
     a process group; row-parallel outputs are all-reduced, vocab shards of the
     logits all-gathered.
+  * Llama.enable_fused_decode(): decode_step through llama.fused (RMSNorm, RoPE,
+    KV-cache writes, SwiGLU and residual adds folded into the INT4 GEMVs, one
+    attention kernel per block).
 """
 from __future__ import annotations
 
@@ -298,7 +301,10 @@ class Llama(Generation):
         """Logits [b, 1, vocab] fp32 for tokens [b, 1] at the device position pos (int64 [1]).
 
         Every operation is a device operation with static shapes, so the step can be
-        captured once in a CUDA graph and replayed for any position."""
+        captured once in a CUDA graph and replayed for any position.  After
+        enable_fused_decode() the step runs as fused kernels (llama.fused)."""
+        if getattr(self, "_fused", None) is not None:
+            return self._fused.decode_step(tokens, pos)
         h = self.tok_embeddings(tokens)
         self.freqs_cis = self.freqs_cis.to(h.device)
         freqs_row = self.freqs_cis.index_select(0, pos)  # [1, head_dim/2]
@@ -309,6 +315,17 @@ class Llama(Generation):
             h = layer.decode(h, pos, freqs_row, bias)
         h = self.norm(h)
         return self._logits(h)
+
+    def enable_fused_decode(self, enabled: bool = True):
+        """Run decode_step as the fused INT4 kernels of llama.fused (five launches per block).
+        Needs a quantized fp16 model on a CUDA device; shares this model's KV caches."""
+        if enabled:
+            from .fused import FusedDecoder
+
+            self._fused = FusedDecoder(self)
+        else:
+            self._fused = None
+        return self
 
     def reset_cache(self):
         for layer in self.layers:
