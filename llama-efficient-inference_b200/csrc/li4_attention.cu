@@ -211,7 +211,7 @@ static size_t attn_smem_bytes(int rep, int head_dim, int max_seq) {
 template <int REP, int HD>
 static int launch_attention(const AttnArgs& a, int batch, size_t smem, cudaStream_t stream) {
   auto kernel = decode_attention_kernel<REP, HD>;
-  if (smem > 48 * 1024) {
+  if (smem + 4096 > 48 * 1024) {  // dynamic + the static softmax partials past the 48 KiB default
     static std::mutex mu;
     static std::vector<std::pair<int, size_t>> raised;  // (device, bytes) of this instantiation
     int dev = 0;

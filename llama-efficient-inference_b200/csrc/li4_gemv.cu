@@ -1291,7 +1291,9 @@ static int ctas_per_sm(KernelT kernel, size_t smem) {
 // example inside CUDA-graph capture) make no attribute call.
 template <typename KernelT>
 static int ensure_smem_limit(KernelT kernel, size_t smem) {
-  if (smem <= 48 * 1024) return LI4_OK;
+  // the kernels also hold a little static shared memory (RMSNorm partials): raise the limit well
+  // before dynamic + static reaches the 48 KiB default
+  if (smem + 4096 <= 48 * 1024) return LI4_OK;
   struct Entry { const void* fn; int dev; size_t limit; };
   static std::mutex mu;
   static std::vector<Entry> cache;
