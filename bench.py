@@ -548,6 +548,17 @@ def run_gpu(a):
     world, rank, local = dist_setup(a.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if a.only_decode:
+        rows = []
+        for bs in a.decode_bs:
+            log(f"decode: Llama-3.2-1B INT4, bs={bs}, {a.decode_prompt}-token prefill, {a.decode_gen} steps, tp={world}")
+            rows.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world))
+            if a.decode_unfused:
+                rows.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
+        if rank == 0:
+            print(json.dumps({"metric": "Llama-3.2-1B INT4 decode tokens/s", "n_gpus": world, "decode": rows}),
+                  flush=True)
+        return
     log("building the quantized weights of the 113-GEMV stream")
     stream = Stream(dev, a.m)
     log("capturing the step graph")
@@ -647,6 +658,8 @@ def main():
     ap.add_argument("--profile-shape", default=None, choices=[n for n, _, _ in LAYER_SHAPES] + [LM_HEAD[0]],
                     help="only run --launches launches of one shape (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--only-decode", action="store_true",
+                    help="only the full-model decode measurement (one JSON line with the decode rows)")
     a = ap.parse_args()
     if a.profile_shape:
         profile_shape(a)

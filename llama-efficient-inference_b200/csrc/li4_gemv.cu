@@ -121,10 +121,42 @@ __device__ __noinline__ void emit_pair(const GemvArgs& a, int m, int pair, float
 
 // The reduced outputs of one 16-row tile, value(r, m) for local row r, emitted
 // by threads tid = 0 .. nthr-1 of the caller's group.
-template <typename F>
+// value(r, m) of a tile reduced over the split-K partial sums (fixed order).
+struct PartialSum {
+  const float* base;  // partial + first row of the tile
+  int M;
+  long long N;
+  int split;
+  __device__ __forceinline__ float operator()(int r, int m) const {
+    float v = 0.f;
+    for (int sp = 0; sp < split; ++sp) v += __ldcg(&base[((long long)sp * M + m) * N + r]);
+    return v;
+  }
+};
+
+// value(r, m) of a tile reduced over the warps' partial tiles in shared memory.
+template <int COLS, int WARPS>
+struct WarpTileSum {
+  const float* rb;  // [warps][16][COLS]
+  __device__ __forceinline__ float operator()(int r, int m) const {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) v += rb[(w * 16 + r) * COLS + m];
+    return v;
+  }
+};
+
+// One output through the epilogue (FUSED) or as a plain fp16 store.
+template <bool FUSED>
+__device__ __forceinline__ void emit_value(const GemvArgs& a, int m, int row, float v) {
+  if constexpr (FUSED) emit_one(a, m, row, v);
+  else a.y[(long long)m * a.sym + row] = __float2half_rn(v);
+}
+
+template <bool FUSED, typename F>
 __device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, int nthr, F value) {
   const int row0 = tile * 16;
-  if (epi_paired(a)) {  // N is a multiple of 16: full tiles
+  if (FUSED && epi_paired(a)) {  // N is a multiple of 16: full tiles
     for (int idx = tid; idx < 8 * a.M; idx += nthr) {
       const int j = idx / a.M, m = idx - j * a.M;
       emit_pair(a, m, tile * 8 + j, value(j, m), value(j + 8, m));
@@ -133,7 +165,7 @@ __device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, 
     const int rows = min(16, a.N - row0);
     for (int idx = tid; idx < rows * a.M; idx += nthr) {
       const int r = idx / a.M, m = idx - r * a.M;
-      emit_one(a, m, row0 + r, value(r, m));
+      emit_value<FUSED>(a, m, row0 + r, value(r, m));
     }
   }
 }
@@ -203,7 +235,7 @@ __device__ __forceinline__ uint4 lds128_ordered(const uint8_t* p) {
 }
 
 // s_rstd: per-row RMSNorm factors (compute_rstd) when a.norm_w is set, else unused.
-template <int NT, int THREADS = kThreads>
+template <int NT, int THREADS = kThreads, bool NORM = false>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
                                         const float* s_rstd = nullptr) {
   const int total = nks * NT * M8 * 16;
@@ -231,7 +263,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int
         for (int e = 0; e < 4; ++e)
           u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
       }
-      if (a.norm_w != nullptr) {  // 16-byte aligned weight (checked by the host)
+      if (NORM && a.norm_w != nullptr) {  // 16-byte aligned weight (checked by the host)
         const uint4 w = *reinterpret_cast<const uint4*>(a.norm_w + k);
         const float r = s_rstd[m];
         u[0] = norm_pair(u[0], w.x, r);
@@ -730,7 +762,7 @@ __device__ __forceinline__ void stream_compute(const StreamUnit& u, const uint8_
   }
 }
 
-template <int NT, bool KSPLIT>
+template <int NT, bool KSPLIT, bool FUSED>
 __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int D = kStreamDepth;
@@ -763,8 +795,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
   }
   pdl_wait_primary();  // x is written by the preceding kernel
   __shared__ float s_rstd[LI4_MAX_M];
-  if (a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
-  stage_x<NT, kStreamThreads>(a, ks0, nks, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
+  stage_x<NT, kStreamThreads, FUSED>(a, ks0, nks, M8, xs, s_rstd);
   __syncthreads();
 
   // this thread's B-fragment offsets inside one (kstep, n-tile) group
@@ -804,7 +836,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
         if (!KSPLIT) {
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if (a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
+            if (FUSED && a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
                 const int m = nt * 8 + 2 * quad + e;
@@ -815,7 +847,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               for (int e = 0; e < 4; ++e) {
                 const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
                 if (r < rows && m < a.M) {
-                  if (a.split == 1) emit_one(a, m, row0 + r, acc[nt][e]);
+                  if (a.split == 1) emit_value<FUSED>(a, m, row0 + r, acc[nt][e]);
                   else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
                 }
               }
@@ -831,11 +863,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
               __threadfence();
-              emit_tile(a, tile, lane, 32, [&](int r, int m) {
-                float v = 0.f;
-                for (int sp = 0; sp < a.split; ++sp) v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
-                return v;
-              });
+              emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
               __syncwarp();
               if (lane == 0) a.counters[tile] = 0u;
             }
@@ -850,14 +878,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               acc[nt][e] = 0.f;
             }
           __syncthreads();
-          auto tile_sum = [&](int r, int m) {
-            float v = 0.f;
-#pragma unroll
-            for (int w = 0; w < kStreamWarps; ++w) v += rb[(w * 16 + r) * COLS + m];
-            return v;
-          };
+          const WarpTileSum<COLS, kStreamWarps> tile_sum{rb};
           if (a.split == 1) {
-            emit_tile(a, tile, threadIdx.x, kStreamThreads, tile_sum);
+            emit_tile<FUSED>(a, tile, threadIdx.x, kStreamThreads, tile_sum);
           } else {
             for (int idx = threadIdx.x; idx < rows * a.M; idx += kStreamThreads) {
               const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
@@ -873,12 +896,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               last = __shfl_sync(0xffffffffu, last, 0);
               if (last) {
                 __threadfence();
-                emit_tile(a, tile, lane, 32, [&](int r, int m) {
-                  float v = 0.f;
-                  for (int sp = 0; sp < a.split; ++sp)
-                    v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + row0 + r]);
-                  return v;
-                });
+                emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
                 __syncwarp();
                 if (lane == 0) a.counters[tile] = 0u;
               }
@@ -1003,7 +1021,7 @@ __device__ __forceinline__ void tile_compute(const TileUnit<RT>& u, const uint8_
   }
 }
 
-template <int NT, int RT>
+template <int NT, int RT, bool FUSED>
 __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NKS = kTileKs;
@@ -1026,8 +1044,8 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
   }
   pdl_wait_primary();  // x is written by the preceding kernel
   __shared__ float s_rstd[LI4_MAX_M];
-  if (a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
-  stage_x<NT, kStreamThreads>(a, ks0, NKS, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
+  stage_x<NT, kStreamThreads, FUSED>(a, ks0, NKS, M8, xs, s_rstd);
   __syncthreads();
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
@@ -1063,7 +1081,7 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
     for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        if (a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of each 16-row subtile are a pair
+        if (FUSED && a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of each 16-row subtile are a pair
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int m = nt * 8 + 2 * quad + e;
@@ -1076,7 +1094,7 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
         for (int e = 0; e < 4; ++e) {
           const int r = row0 + rt * 16 + grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
           if (r < a.N && m < a.M) {
-            if (a.split == 1) emit_one(a, m, r, acc[rt][nt][e]);
+            if (a.split == 1) emit_value<FUSED>(a, m, r, acc[rt][nt][e]);
             else a.partial[((long long)blockIdx.y * a.M + m) * a.N + r] = acc[rt][nt][e];
           }
         }
@@ -1093,12 +1111,7 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
         for (int rt = 0; rt < RT; ++rt) {
           const int sub = tile * RT + rt;
           if (sub * 16 >= a.N) break;
-          emit_tile(a, sub, lane, 32, [&](int r, int m) {
-            float v = 0.f;
-            for (int sp = 0; sp < a.split; ++sp)
-              v += __ldcg(&a.partial[((long long)sp * a.M + m) * a.N + sub * 16 + r]);
-            return v;
-          });
+          emit_tile<FUSED>(a, sub, lane, 32, PartialSum{a.partial + sub * 16, a.M, a.N, a.split});
         }
         __syncwarp();
         if (lane == 0) a.counters[tile] = 0u;
@@ -1380,19 +1393,32 @@ static int launch_stream_kernel(KernelT kernel, const Plan& p, const GemvArgs& a
 }
 
 static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
+  const bool fused = args.norm_w != nullptr || args.epi != LI4_EPI_STORE;
   if (p.kernel == LI4_KERNEL_TILE) {
-    if (p.nt == 1)
-      return p.rt == 1 ? launch_stream_kernel(gemv_tile_kernel<1, 1>, p, args, s)
-                       : launch_stream_kernel(gemv_tile_kernel<1, 2>, p, args, s);
-    return p.rt == 1 ? launch_stream_kernel(gemv_tile_kernel<2, 1>, p, args, s)
-                     : launch_stream_kernel(gemv_tile_kernel<2, 2>, p, args, s);
+    const int sel = (p.nt - 1) * 4 + (p.rt - 1) * 2 + (fused ? 1 : 0);
+    switch (sel) {
+      case 0: return launch_stream_kernel(gemv_tile_kernel<1, 1, false>, p, args, s);
+      case 1: return launch_stream_kernel(gemv_tile_kernel<1, 1, true>, p, args, s);
+      case 2: return launch_stream_kernel(gemv_tile_kernel<1, 2, false>, p, args, s);
+      case 3: return launch_stream_kernel(gemv_tile_kernel<1, 2, true>, p, args, s);
+      case 4: return launch_stream_kernel(gemv_tile_kernel<2, 1, false>, p, args, s);
+      case 5: return launch_stream_kernel(gemv_tile_kernel<2, 1, true>, p, args, s);
+      case 6: return launch_stream_kernel(gemv_tile_kernel<2, 2, false>, p, args, s);
+      default: return launch_stream_kernel(gemv_tile_kernel<2, 2, true>, p, args, s);
+    }
   }
   if (p.kernel == LI4_KERNEL_STREAM) {
-    if (p.nt == 1)
-      return p.stream_ksplit ? launch_stream_kernel(gemv_stream_kernel<1, true>, p, args, s)
-                             : launch_stream_kernel(gemv_stream_kernel<1, false>, p, args, s);
-    return p.stream_ksplit ? launch_stream_kernel(gemv_stream_kernel<2, true>, p, args, s)
-                           : launch_stream_kernel(gemv_stream_kernel<2, false>, p, args, s);
+    const int sel = (p.nt - 1) * 4 + (p.stream_ksplit ? 2 : 0) + (fused ? 1 : 0);
+    switch (sel) {
+      case 0: return launch_stream_kernel(gemv_stream_kernel<1, false, false>, p, args, s);
+      case 1: return launch_stream_kernel(gemv_stream_kernel<1, false, true>, p, args, s);
+      case 2: return launch_stream_kernel(gemv_stream_kernel<1, true, false>, p, args, s);
+      case 3: return launch_stream_kernel(gemv_stream_kernel<1, true, true>, p, args, s);
+      case 4: return launch_stream_kernel(gemv_stream_kernel<2, false, false>, p, args, s);
+      case 5: return launch_stream_kernel(gemv_stream_kernel<2, false, true>, p, args, s);
+      case 6: return launch_stream_kernel(gemv_stream_kernel<2, true, false>, p, args, s);
+      default: return launch_stream_kernel(gemv_stream_kernel<2, true, true>, p, args, s);
+    }
   }
   if (p.kernel == LI4_KERNEL_CUDA_CORE) {
     switch (args.M) {
