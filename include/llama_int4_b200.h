@@ -204,6 +204,14 @@ int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, 
                          int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
                          const int64_t* pos, int64_t max_seq, void* stream);
 
+/* out[r * out_stride] = argmax of row r of logits [rows, cols] (dtype LI4_F16 or
+ * LI4_F32, row stride `stride` elements): the first index of the row's maximum,
+ * a NaN counting as the maximum, as torch.argmax.  One CTA per row.
+ * Replaces: the greedy logits[:, -1].argmax(-1) of the decode loop
+ * (bench.py:154-161, llama/generation.py:59-60). */
+int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
+                    int64_t* out, int64_t out_stride, void* stream);
+
 /* w16[N, K] (fp16, row stride stride_wn elements) = dequantized weights,
  * bit-identical to the reference's fp32 (q - zero) * scale rounded to fp16.
  * Replaces: QuantizedLinear.dequantize_packed (llama/quantize.py:78-104) and

@@ -1,8 +1,12 @@
 // li4_attention.cu -- decode attention (one new token per sequence), sm_100a.
 //
-// One CTA per (KV head, sequence): it reads that head's cached keys and values
-// once for all `REP` query heads that share them (grouped-query attention
-// without the reference's repeat_kv copies, llama/model.py:155-164, 265-266).
+// A cluster of 1..8 CTAs per (KV head, sequence) splits the cached keys and
+// values between its CTAs, and reads them once for all `REP` query heads that
+// share them (grouped-query attention without the reference's repeat_kv
+// copies, llama/model.py:155-164, 265-266).  The CTAs exchange the softmax max
+// and sum and their partial P.V through distributed shared memory, so the
+// probabilities are normalised by the global sum before their fp16 rounding,
+// as in the reference.
 // The arithmetic follows the reference's fp16 decode step
 // (llama/model.py:266-275):
 //   s = fp16(q . k)             fp16 matmul, fp32 accumulation
@@ -15,8 +19,12 @@
 #include "li4_common.cuh"
 #include "li4_internal.h"
 
+#include <cooperative_groups.h>
+
 #include <mutex>
 #include <vector>
+
+namespace cg = cooperative_groups;
 
 namespace li4 {
 
@@ -54,18 +62,23 @@ struct AttnArgs {
   int n_kv_heads;
   const long long* pos;
   int max_seq;
+  int chunk_max;  // keys per CTA at most: ceil(max_seq / cluster size)
 };
 
 template <int REP, int HD>
 __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __grid_constant__ AttnArgs a) {
-  constexpr int kHeadDim = HD;
   constexpr int DPL = HD / 32;  // dims per lane in P.V
   extern __shared__ __align__(16) float smem[];
-  float* q_s = smem;                              // [REP][HD]
-  float* red = q_s + REP * kHeadDim;              // [warps][REP][HD]
-  float* scores = red + kAttnWarps * REP * kHeadDim;  // [REP][max_seq]
-  __shared__ float s_max[kAttnWarps][REP], s_sum[kAttnWarps][REP];
+  float* q_s = smem;                         // [REP][HD]
+  float* red = q_s + REP * HD;               // [warps][REP][HD]
+  float* part = red + kAttnWarps * REP * HD; // [REP][HD] this CTA's P.V over its keys
+  float* scores = part + REP * HD;           // [REP][chunk_max]
+  __shared__ float s_wmax[kAttnWarps][REP], s_wsum[kAttnWarps][REP];
+  __shared__ float s_lmax[REP], s_lsum[REP], s_gmax[REP], s_gsum[REP];
 
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();   // CTAs sharing this (KV head, sequence)
+  const int c = (int)cluster.block_rank();
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_launch_dependents();
@@ -74,68 +87,77 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   long long p = *a.pos;
   p = p < 0 ? 0 : (p >= a.max_seq ? a.max_seq - 1 : p);
   const int L = (int)p + 1;
-  const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * kHeadDim;
-  const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * kHeadDim;
+  const int chunk = (L + S - 1) / S;
+  const int j0 = c * chunk, j1 = min(L, j0 + chunk);
+  const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * HD;
+  const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * HD;
 
-  for (int t = tid; t < REP * kHeadDim; t += kAttnThreads)
-    q_s[t] = __half2float(a.q[(long long)b * a.sqb + (long long)kvh * REP * kHeadDim + t]);
+  for (int t = tid; t < REP * HD; t += kAttnThreads)
+    q_s[t] = __half2float(a.q[(long long)b * a.sqb + (long long)kvh * REP * HD + t]);
   __syncthreads();
 
-  // scores: one key per thread, REP dot products over its HD dims
-  const float inv_scale = 1.0f / sqrtf((float)kHeadDim);
+  // scores of this CTA's keys: one key per thread, REP dot products over HD dims
+  const float inv_scale = 1.0f / sqrtf((float)HD);
   float mx[REP];
 #pragma unroll
   for (int r = 0; r < REP; ++r) mx[r] = -INFINITY;
-  for (int j = tid; j < L; j += kAttnThreads) {
+  for (int j = j0 + tid; j < j1; j += kAttnThreads) {
     const uint4* kr = reinterpret_cast<const uint4*>(kbase + (long long)j * a.css);
     float dot[REP];
 #pragma unroll
     for (int r = 0; r < REP; ++r) dot[r] = 0.f;
 #pragma unroll
-    for (int c = 0; c < kHeadDim / 8; ++c) {
-      const uint4 kv = kr[c];
+    for (int cc = 0; cc < HD / 8; ++cc) {
+      const uint4 kv = kr[cc];
       const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
 #pragma unroll
         for (int r = 0; r < REP; ++r) {
-          dot[r] = fmaf(q_s[r * kHeadDim + c * 8 + 2 * e], kf.x, dot[r]);
-          dot[r] = fmaf(q_s[r * kHeadDim + c * 8 + 2 * e + 1], kf.y, dot[r]);
+          dot[r] = fmaf(q_s[r * HD + cc * 8 + 2 * e], kf.x, dot[r]);
+          dot[r] = fmaf(q_s[r * HD + cc * 8 + 2 * e + 1], kf.y, dot[r]);
         }
       }
     }
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       const float s16 = __half2float(__float2half_rn(dot[r]));
-      const float s = __half2float(__float2half_rn(s16 * inv_scale));  // torch divides by a scalar as a product with its reciprocal
-      scores[r * a.max_seq + j] = s;
-      mx[r] = fmaxf(mx[r], s);
+      const float sc = __half2float(__float2half_rn(s16 * inv_scale));  // torch divides by a scalar as a product with its reciprocal
+      scores[r * a.chunk_max + (j - j0)] = sc;
+      mx[r] = fmaxf(mx[r], sc);
     }
   }
-  // softmax over j < L per head, fp32
+  // softmax over all L keys of the cluster, fp32: max and sum exchanged through distributed shared memory
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
     float v = mx[r];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) s_max[warp][r] = v;
+    if (lane == 0) s_wmax[warp][r] = v;
   }
   __syncthreads();
-  float gmax[REP], sum[REP];
+  if (tid < REP) {
+    float v = s_wmax[0][tid];
 #pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    float v = s_max[0][r];
-#pragma unroll
-    for (int w = 1; w < kAttnWarps; ++w) v = fmaxf(v, s_max[w][r]);
-    gmax[r] = v;
-    sum[r] = 0.f;
+    for (int w = 1; w < kAttnWarps; ++w) v = fmaxf(v, s_wmax[w][tid]);
+    s_lmax[tid] = v;
   }
-  for (int j = tid; j < L; j += kAttnThreads) {
+  cluster.sync();
+  if (tid < REP) {
+    float v = -INFINITY;
+    for (int rk = 0; rk < S; ++rk) v = fmaxf(v, *cluster.map_shared_rank(&s_lmax[tid], rk));
+    s_gmax[tid] = v;
+  }
+  __syncthreads();
+  float sum[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) sum[r] = 0.f;
+  for (int j = tid; j < j1 - j0; j += kAttnThreads) {
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
-      const float e = expf(scores[r * a.max_seq + j] - gmax[r]);
-      scores[r * a.max_seq + j] = e;
+      const float e = expf(scores[r * a.chunk_max + j] - s_gmax[r]);
+      scores[r * a.chunk_max + j] = e;
       sum[r] += e;
     }
   }
@@ -144,49 +166,57 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
     float v = sum[r];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) s_sum[warp][r] = v;
+    if (lane == 0) s_wsum[warp][r] = v;
   }
   __syncthreads();
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
+  if (tid < REP) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) v += s_sum[w][r];
-    sum[r] = v;
+    for (int w = 0; w < kAttnWarps; ++w) v += s_wsum[w][tid];
+    s_lsum[tid] = v;
   }
-  for (int j = tid; j < L; j += kAttnThreads) {
+  cluster.sync();
+  if (tid < REP) {
+    float v = 0.f;
+    for (int rk = 0; rk < S; ++rk) v += *cluster.map_shared_rank(&s_lsum[tid], rk);
+    s_gsum[tid] = v;
+  }
+  __syncthreads();
+  for (int j = tid; j < j1 - j0; j += kAttnThreads) {
 #pragma unroll
     for (int r = 0; r < REP; ++r)
-      scores[r * a.max_seq + j] = __half2float(__float2half_rn(scores[r * a.max_seq + j] / sum[r]));
+      scores[r * a.chunk_max + j] = __half2float(__float2half_rn(scores[r * a.chunk_max + j] / s_gsum[r]));
   }
   __syncthreads();
 
-  // P.V: warp w takes keys w, w + 8, ...; lane holds dims DPL lane .. DPL lane + DPL - 1
+  // P.V over this CTA's keys: warp w takes keys j0 + w, j0 + w + 8, ...; lane holds DPL dims
   float acc[REP][DPL];
 #pragma unroll
   for (int r = 0; r < REP; ++r)
 #pragma unroll
     for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
+  const int nloc = j1 - j0;
   int j = warp;
-  for (; j + 3 * kAttnWarps < L; j += 4 * kAttnWarps) {
+  for (; j + 3 * kAttnWarps < nloc; j += 4 * kAttnWarps) {
     float v4[4][DPL];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) load_lane_dims<DPL>(vbase + (long long)(j + u * kAttnWarps) * a.css + DPL * lane, v4[u]);
+    for (int u = 0; u < 4; ++u)
+      load_lane_dims<DPL>(vbase + (long long)(j0 + j + u * kAttnWarps) * a.css + DPL * lane, v4[u]);
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
       for (int r = 0; r < REP; ++r) {
-        const float pj = scores[r * a.max_seq + j + u * kAttnWarps];
+        const float pj = scores[r * a.chunk_max + j + u * kAttnWarps];
 #pragma unroll
         for (int e = 0; e < DPL; ++e) acc[r][e] = fmaf(pj, v4[u][e], acc[r][e]);
       }
   }
-  for (; j < L; j += kAttnWarps) {
+  for (; j < nloc; j += kAttnWarps) {
     float vv[DPL];
-    load_lane_dims<DPL>(vbase + (long long)j * a.css + DPL * lane, vv);
+    load_lane_dims<DPL>(vbase + (long long)(j0 + j) * a.css + DPL * lane, vv);
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
-      const float pj = scores[r * a.max_seq + j];
+      const float pj = scores[r * a.chunk_max + j];
 #pragma unroll
       for (int e = 0; e < DPL; ++e) acc[r][e] = fmaf(pj, vv[e], acc[r][e]);
     }
@@ -194,22 +224,39 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
 #pragma unroll
   for (int r = 0; r < REP; ++r)
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) red[(warp * REP + r) * kHeadDim + DPL * lane + e] = acc[r][e];
+    for (int e = 0; e < DPL; ++e) red[(warp * REP + r) * HD + DPL * lane + e] = acc[r][e];
   __syncthreads();
-  for (int t = tid; t < REP * kHeadDim; t += kAttnThreads) {
+  for (int t = tid; t < REP * HD; t += kAttnThreads) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) v += red[w * REP * kHeadDim + t];
-    a.out[(long long)b * a.sob + (long long)kvh * REP * kHeadDim + t] = __float2half_rn(v);
+    for (int w = 0; w < kAttnWarps; ++w) v += red[w * REP * HD + t];
+    part[t] = v;
   }
+  cluster.sync();
+  if (c == 0) {  // the cluster's first CTA sums the partial P.V of all its CTAs (rank order)
+    for (int t = tid; t < REP * HD; t += kAttnThreads) {
+      float v = 0.f;
+      for (int rk = 0; rk < S; ++rk) v += *cluster.map_shared_rank(&part[t], rk);
+      a.out[(long long)b * a.sob + (long long)kvh * REP * HD + t] = __float2half_rn(v);
+    }
+  }
+  cluster.sync();  // every CTA's shared memory stays in place until the first CTA has read it
 }
 
-static size_t attn_smem_bytes(int rep, int head_dim, int max_seq) {
-  return sizeof(float) * ((size_t)rep * head_dim * (1 + kAttnWarps) + (size_t)rep * max_seq);
+static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max) {
+  return sizeof(float) * ((size_t)rep * head_dim * (2 + kAttnWarps) + (size_t)rep * chunk_max);
+}
+
+// CTAs per (KV head, sequence): a cluster of up to 8 when the (KV head, sequence)
+// pairs alone leave SMs idle, keeping >= 32 keys per CTA at max_seq.
+static int attn_cluster_size(int64_t pairs, int64_t max_seq, int sm) {
+  int S = 1;
+  while (S < 8 && pairs * S < 2LL * sm && max_seq / (2 * S) >= 32) S *= 2;
+  return S;
 }
 
 template <int REP, int HD>
-static int launch_attention(const AttnArgs& a, int batch, size_t smem, cudaStream_t stream) {
+static int launch_attention(const AttnArgs& a, int batch, int cluster, size_t smem, cudaStream_t stream) {
   auto kernel = decode_attention_kernel<REP, HD>;
   if (smem + 4096 > 48 * 1024) {  // dynamic + the static softmax partials past the 48 KiB default
     static std::mutex mu;
@@ -228,15 +275,19 @@ static int launch_attention(const AttnArgs& a, int batch, size_t smem, cudaStrea
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)a.n_kv_heads, (unsigned)batch, 1);
+  cfg.gridDim = dim3((unsigned)a.n_kv_heads, (unsigned)batch, (unsigned)cluster);
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = (unsigned)cluster;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, a), "decode_attention: kernel launch");
 }
 
@@ -264,9 +315,16 @@ extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void
   if (!aligned16(cache_k) || !aligned16(cache_v) || cache_stride_s % 8 != 0 || cache_stride_b % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(q) & 1u) || (reinterpret_cast<uintptr_t>(out) & 1u))
     return set_error(LI4_ERR_ALIGNMENT, "decode_attention: cache rows must be 16-byte aligned");
-  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, (int)max_seq);
-  if (max_seq > (1 << 20) || smem > 200 * 1024)
-    return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld needs %zu bytes of shared memory",
+  if (max_seq > (1 << 20))
+    return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld above 2^20", (long long)max_seq);
+  int cluster = attn_cluster_size(batch * n_kv_heads, max_seq, current_sm_count());
+  while (cluster < 8 && attn_smem_bytes((int)rep, (int)head_dim, (int)((max_seq + cluster - 1) / cluster)) >
+                            200 * 1024)
+    cluster *= 2;
+  const int chunk_max = (int)((max_seq + cluster - 1) / cluster);
+  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, chunk_max);
+  if (smem > 200 * 1024)
+    return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld needs %zu bytes of shared memory per CTA",
                      (long long)max_seq, smem);
   if (batch == 0) return LI4_OK;
   AttnArgs a;
@@ -281,12 +339,13 @@ extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void
   a.n_kv_heads = (int)n_kv_heads;
   a.pos = reinterpret_cast<const long long*>(pos);
   a.max_seq = (int)max_seq;
+  a.chunk_max = chunk_max;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc;
   const int sel = (int)rep * 1000 + (int)head_dim;
   switch (sel) {
 #define LI4_ATTN_CASE(R, H) \
-  case R * 1000 + H: rc = launch_attention<R, H>(a, (int)batch, smem, s); break;
+  case R * 1000 + H: rc = launch_attention<R, H>(a, (int)batch, cluster, smem, s); break;
     LI4_ATTN_CASE(1, 32) LI4_ATTN_CASE(2, 32) LI4_ATTN_CASE(4, 32) LI4_ATTN_CASE(8, 32)
     LI4_ATTN_CASE(1, 64) LI4_ATTN_CASE(2, 64) LI4_ATTN_CASE(4, 64) LI4_ATTN_CASE(8, 64)
     LI4_ATTN_CASE(1, 128) LI4_ATTN_CASE(2, 128) LI4_ATTN_CASE(4, 128) LI4_ATTN_CASE(8, 128)

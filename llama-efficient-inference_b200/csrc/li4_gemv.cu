@@ -1223,7 +1223,7 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     }
     p->stream_ksplit = (int64_t)p->n_tiles < 4LL * sm && p->n_ks / split >= kStreamWarps;
     if (split_req <= 0 && p->stream_ksplit)
-      while ((int64_t)p->n_tiles * split * 2 <= sm && p->n_ks % (2 * split) == 0 &&
+      while ((int64_t)p->n_tiles * split * 2 <= 2LL * sm && p->n_ks % (2 * split) == 0 &&
              p->n_ks / (2 * split) >= kStreamWarps)
         split *= 2;
   }

@@ -71,6 +71,7 @@ SIGNATURES = {
     "li4_int4_linear_fused": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                      ctypes.POINTER(Fusion), _P, _SZ, _P]),
     "li4_decode_attention": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "li4_argmax_rows": (_INT, [_P, _INT, _I64, _I64, _I64, _P, _I64, _P]),
     "li4_dequantize": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_quantize": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
 }

@@ -102,6 +102,17 @@ def decode_attention(q: torch.Tensor, cache_k: torch.Tensor, cache_v: torch.Tens
     native.check(rc, "decode_attention")
 
 
+def argmax_rows(logits: torch.Tensor, out: torch.Tensor) -> None:
+    """out[r, 0] = torch.argmax(logits[r]) for fp16 / fp32 logits [rows, cols] (li4_argmax_rows)."""
+    codes = {torch.float16: native.LI4_F16, torch.float32: native.LI4_F32}
+    if logits.dtype not in codes or logits.stride(-1) != 1 or out.dtype != torch.long:
+        raise RuntimeError("argmax_rows: fp16 / fp32 logits with contiguous rows and an int64 output")
+    rows, cols = logits.shape
+    rc = native.lib().li4_argmax_rows(logits.data_ptr(), codes[logits.dtype], rows, cols, logits.stride(0),
+                                      out.data_ptr(), out.stride(0), native.stream_ptr(logits.device))
+    native.check(rc, "argmax_rows")
+
+
 class _Block:
     """Fused weights and fusion descriptors of one transformer block."""
 
@@ -177,7 +188,10 @@ class FusedDecoder:
         torch.add(residual, part, out=out)
 
     @torch.no_grad()
-    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor,
+                    next_tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """fp32 logits [bs, 1, vocab]; with next_tokens (int64 [bs, 1], may be `tokens`) also
+        the greedy argmax of each row, written on the GPU."""
         bs = tokens.shape[0]
         buf = self._buffers(bs)
         h, h1, q, attn, ffn, part = buf["h"], buf["h1"], buf["q"], buf["attn"], buf["ffn"], buf["part"]
@@ -217,4 +231,6 @@ class FusedDecoder:
             parts = [torch.empty_like(logits) for _ in range(self.model.tp_world)]
             dist.all_gather(parts, logits, group=self.model.tp_group)
             logits = torch.cat(parts, dim=-1)
+        if next_tokens is not None:
+            argmax_rows(logits, next_tokens.view(bs, 1))
         return logits.float().view(bs, 1, -1)

@@ -295,3 +295,34 @@ def test_fused_step_matches_unfused_llama_block(bs, cuda_device):
         assert err <= 1e-2 * ref.abs().max().item(), f"max|d logits| = {err:.3e}, max|ref| = {ref.abs().max():.3e}"
     finally:
         quantize.set_dequant_impl("v1")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(1, 128256), (16, 128256), (3, 1000), (2, 7)])
+def test_argmax_rows_matches_torch(dtype, rows, cols, fz, cuda_device):
+    fused, _ = fz
+    gen = torch.Generator(device=cuda_device).manual_seed(rows * cols)
+    x = torch.randn(rows, cols, generator=gen, device=cuda_device).to(dtype)
+    if cols > 10:
+        x[0, 5] = x[0, cols - 3] = x[0].max() + 1  # a tie: the first index wins
+    out = torch.full((rows, 1), -1, dtype=torch.long, device=cuda_device)
+    fused.argmax_rows(x, out)
+    assert torch.equal(out.view(-1), x.argmax(-1))
+    if rows > 1:
+        x[1, cols // 2] = float("nan")  # NaN counts as the maximum
+        fused.argmax_rows(x, out)
+        assert out[1, 0].item() == cols // 2 == x[1].argmax().item()
+
+
+@pytest.mark.parametrize("B,max_seq,pos", [(2, 8192, 8191), (16, 640, 600), (1, 640, 1)])
+def test_decode_attention_cluster_shapes(B, max_seq, pos, fz, cuda_device):
+    """Long caches (several CTAs per head, shared memory above 48 KiB) and batch 16 (one CTA per head)."""
+    fused, _ = fz
+    n_heads, n_kv_heads, head_dim = 32, 8, 64
+    q = randn((B, n_heads * head_dim), cuda_device, 61 + B)
+    ck = randn((B, max_seq, n_kv_heads, head_dim), cuda_device, 62)
+    cv = randn((B, max_seq, n_kv_heads, head_dim), cuda_device, 63)
+    out = torch.empty_like(q)
+    pos_t = torch.tensor([pos], dtype=torch.long, device=cuda_device)
+    fused.decode_attention(q, ck, cv, pos_t, out, n_heads, n_kv_heads)
+    close(out, attention_ref(q, ck, cv, pos, n_heads, n_kv_heads, head_dim), what="attention")
