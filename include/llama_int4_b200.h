@@ -51,7 +51,9 @@ typedef enum li4_kernel {
   LI4_KERNEL_CUDA_CORE = 1,  /* fp32 FMA on CUDA cores, M <= 8                      */
   LI4_KERNEL_MMA = 2,        /* m16n8k16 tensor-core tiles (weights as the A side)  */
   LI4_KERNEL_STREAM = 3,     /* streaming warps, m16n8k16 tiles, groups >= 128      */
-  LI4_KERNEL_TILE = 4        /* tile-streaming warps: group 128, K ranges of 2048  */
+  LI4_KERNEL_TILE = 4,       /* tile-streaming warps: group 128, K ranges of 2048  */
+  LI4_KERNEL_BULK = 5        /* bulk-copy ring in shared memory: group 128,
+                                K % 1024 == 0, 16-byte aligned scale / zero rows   */
 } li4_kernel;
 
 /* Library version, (major << 16) | (minor << 8) | patch. */
@@ -211,6 +213,12 @@ int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, 
  * (bench.py:154-161, llama/generation.py:59-60). */
 int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
                     int64_t* out, int64_t out_stride, void* stream);
+
+/* Device-side error flags of the current device (bit 0: a bounded pipeline wait
+ * inside a kernel ran out -- the kernel returned early and its outputs are not
+ * valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
+ * A diagnostic for tests and health checks, not for the decode loop. */
+int li4_device_errors(unsigned* flags, int reset);
 
 /* w16[N, K] (fp16, row stride stride_wn elements) = dequantized weights,
  * bit-identical to the reference's fp32 (q - zero) * scale rounded to fp16.

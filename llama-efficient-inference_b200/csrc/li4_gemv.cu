@@ -1122,6 +1122,243 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
 }
 
 // ---------------------------------------------------------------------------
+// Bulk-copy pipeline kernel.  A producer warp moves whole 16-row tiles of one K
+// range (packed rows, scale and zero rows) from HBM into a ring of shared-memory
+// stages with cp.async.bulk (the TMA engine's 1-D bulk copy), completing on
+// per-stage mbarriers; eight consumer warps split each stage's ksteps between
+// them, reduce the tile in shared memory and run the epilogue.  The ring holds
+// up to kBulkMaxStages x 18 KiB per SM in flight (against 4-5 KiB per warp for
+// the register rings), and the first stages are requested before
+// griddepcontrol.wait, so the weight stream of a launch overlaps the tail of the
+// preceding kernel.  Every mbarrier wait is bounded; a wait that runs out sets
+// g_li4_device_error and the kernel drains its own copies and returns.
+// ---------------------------------------------------------------------------
+constexpr int kBulkConsumerWarps = 8;
+constexpr int kBulkThreads = (kBulkConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kBulkMaxStages = 8;
+constexpr unsigned kBulkWaitLimit = 1u << 22;  // try_wait rounds: well under a second of polling, never forever
+
+__device__ unsigned g_li4_device_error;  // bit 0: a bounded pipeline wait ran out
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, at most kBulkWaitLimit rounds.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
+  for (unsigned i = 0; i < kBulkWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicOr(&g_li4_device_error, 1u);
+  return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Shared-memory layout of one stage: 16 packed rows of K-range/2 bytes at a
+// pitch of K-range/2 + 64 (the 64 keeps the 16-byte reads of the eight row
+// pairs of a quarter warp on distinct banks), then 16 scale rows and 16 zero
+// rows of KS fp16 values.
+struct BulkLayout {
+  int ks;       // ksteps per K range (8 or 16)
+  int pitch;    // bytes between packed rows
+  int sz_off;   // scale rows, then zero rows at + 16 * ks * 2
+  int stage;    // bytes per stage (multiple of 128)
+};
+
+__host__ __device__ inline BulkLayout bulk_layout(int ks) {
+  BulkLayout L;
+  L.ks = ks;
+  L.pitch = ks * 64 + 64;
+  L.sz_off = 16 * L.pitch;
+  L.stage = (L.sz_off + 2 * 16 * ks * 2 + 127) & ~127;
+  return L;
+}
+
+template <int NT, bool FUSED>
+__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs a, int stages) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int M8 = 8;           // x rows padded to 8 per n-tile (as the tile kernel)
+  constexpr int COLS = 8 * NT;
+  const int ks_n = a.ks_per_split;
+  const BulkLayout L = bulk_layout(ks_n);
+  uint8_t* ring = smem;
+  uint8_t* xs = ring + (size_t)stages * L.stage;
+  float* red = reinterpret_cast<float*>(xs + (size_t)ks_n * NT * M8 * 256);  // [2][warps][16][COLS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kBulkConsumerWarps * 16 * COLS);
+  uint64_t* empty = full + kBulkMaxStages;
+  __shared__ float s_rstd[LI4_MAX_M];
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks0 = blockIdx.y * ks_n;
+  // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int my_tiles = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kBulkConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kBulkConsumerWarps) {
+    // ---------------- producer warp ----------------
+    const unsigned stage_bytes = 16u * (unsigned)(ks_n * 64) + 2u * 16u * (unsigned)(ks_n * 2);
+    bool ok = true;
+    for (int it = 0; it < my_tiles && ok; ++it) {
+      const int s = it % stages;
+      if (it >= stages) ok = mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1);
+      if (!ok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_bytes);
+      __syncwarp();
+      const int tile = (int)blockIdx.x + it * (int)gridDim.x;
+      uint8_t* st = ring + (size_t)s * L.stage;
+      if (lane < 16) {
+        int r = tile * 16 + lane;
+        r = r < a.N ? r : a.N - 1;
+        bulk_g2s(st + lane * L.pitch, a.packed + (long long)r * a.spn + (long long)ks0 * 64, ks_n * 64, &full[s]);
+        bulk_g2s(st + L.sz_off + lane * ks_n * 2, a.scale + (long long)r * a.ssn + ks0, ks_n * 2, &full[s]);
+      } else {
+        int r = tile * 16 + (lane - 16);
+        r = r < a.N ? r : a.N - 1;
+        bulk_g2s(st + L.sz_off + 16 * ks_n * 2 + (lane - 16) * ks_n * 2, a.zero + (long long)r * a.ssn + ks0,
+                 ks_n * 2, &full[s]);
+      }
+    }
+    if (!ok) {  // drain: the copies already issued land before the CTA exits
+      for (int it = (my_tiles > stages ? my_tiles - stages : 0); it < my_tiles; ++it)
+        mbar_wait_bounded(&full[it % stages], (it / stages) & 1);
+    }
+    pdl_wait_primary();  // every thread of the grid passes the dependency wait
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int grp = lane >> 2, quad = lane & 3;
+  pdl_wait_primary();  // x (and the residual) come from the preceding kernel
+  if (FUSED && a.norm_w != nullptr) {
+    // compute_rstd over the consumer warps only (named barrier 1)
+    __shared__ float part[kBulkConsumerWarps][LI4_MAX_M];
+    for (int m = 0; m < a.M; ++m) {
+      const __half* row = a.x + (long long)m * a.sxm;
+      float ss = 0.f;
+      for (int k = threadIdx.x; k < a.K; k += kBulkConsumerWarps * 32) {
+        const float v = __half2float(row[k]);
+        ss = fmaf(v, v, ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) part[warp][m] = ss;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+    if (threadIdx.x < a.M) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kBulkConsumerWarps; ++w) t += part[w][threadIdx.x];
+      s_rstd[threadIdx.x] = rsqrtf(t / (float)a.K + a.norm_eps);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+  }
+  stage_x<NT, kBulkConsumerWarps * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
+  asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+
+  const bool bvalid = grp < ((NT == 1) ? a.M : 8);
+  int boff[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) boff[w] = (grp * 4 + quad) * 64 + ((w ^ xs_key(grp, quad)) << 4);
+  constexpr int nt_stride = M8 * 256;
+  constexpr int ks_stride = NT * nt_stride;
+
+  bool ok = true;
+  for (int it = 0; it < my_tiles; ++it) {
+    const int s = it % stages;
+    const int tile = (int)blockIdx.x + it * (int)gridDim.x;
+    if (ok) ok = mbar_wait_bounded(&full[s], (it / stages) & 1);
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+    if (ok) {
+      const uint8_t* st = ring + (size_t)s * L.stage;
+      const unsigned short* sc = reinterpret_cast<const unsigned short*>(st + L.sz_off);
+      const unsigned short* ze = sc + 16 * ks_n;
+      for (int ks = warp; ks < ks_n; ks += kBulkConsumerWarps) {
+        StreamUnit u;
+        u.lo = *reinterpret_cast<const uint4*>(st + grp * L.pitch + ks * 64 + quad * 16);
+        u.hi = *reinterpret_cast<const uint4*>(st + (grp + 8) * L.pitch + ks * 64 + quad * 16);
+        u.sz_lo = (uint32_t)sc[grp * ks_n + ks] | ((uint32_t)ze[grp * ks_n + ks] << 16);
+        u.sz_hi = (uint32_t)sc[(grp + 8) * ks_n + ks] | ((uint32_t)ze[(grp + 8) * ks_n + ks] << 16);
+        stream_compute<NT>(u, xs + ks * ks_stride, nt_stride, boff, bvalid, acc);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done reading the stage
+    // cross-warp reduction of the tile (double-buffered by tile parity)
+    float* rb = red + (it & 1) * (kBulkConsumerWarps * 16 * COLS);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        rb[(warp * 16 + grp + 8 * (e >> 1)) * COLS + nt * 8 + 2 * quad + (e & 1)] = acc[nt][e];
+    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+    const int row0 = tile * 16;
+    const int rows = min(16, a.N - row0);
+    const WarpTileSum<COLS, kBulkConsumerWarps> tile_sum{rb};
+    if (a.split == 1) {
+      emit_tile<FUSED>(a, tile, threadIdx.x, kBulkConsumerWarps * 32, tile_sum);
+    } else {
+      for (int idx = threadIdx.x; idx < rows * a.M; idx += kBulkConsumerWarps * 32) {
+        const int r = idx / a.M, m = idx - r * a.M;
+        a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = tile_sum(r, m);
+      }
+      __threadfence();  // every writer publishes its partials before the arrival count
+      asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+      if (threadIdx.x == 0)
+        s_last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1 : 0;
+      asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+      if (s_last) {  // last K range to arrive: fixed-order sum, epilogue, counter reset
+        __threadfence();
+        emit_tile<FUSED>(a, tile, threadIdx.x, kBulkConsumerWarps * 32,
+                         PartialSum{a.partial + row0, a.M, a.N, a.split});
+        asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+        if (threadIdx.x == 0) a.counters[tile] = 0u;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: planning and launch.
 // ---------------------------------------------------------------------------
 struct Plan {
@@ -1140,6 +1377,7 @@ struct Plan {
   size_t ws_counters;  // bytes
   size_t ws_bytes;     // total
   bool stream_ksplit;  // LI4_KERNEL_STREAM: K-split mode
+  int stages;          // LI4_KERNEL_BULK: shared-memory ring stages
 };
 
 static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -1169,12 +1407,12 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
   }
-  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE)
-    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp "
-                     "and tile kernels (group_size >= 128)");
-  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE)
-    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp "
-                     "and tile kernels (group_size >= 128)");
+  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK)
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp, "
+                     "tile and bulk-copy kernels (group_size >= 128)");
+  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK)
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp, "
+                     "tile and bulk-copy kernels (group_size >= 128)");
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel takes M <= 8 (M=%lld)", (long long)M);
   if (kernel == LI4_KERNEL_STREAM && (group < 128 || K == 0))
@@ -1182,7 +1420,10 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (kernel == LI4_KERNEL_TILE && (group != 128 || K == 0 || (K / 128) % kTileKs != 0))
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the tile kernel needs group_size 128 and K a multiple of %d",
                      kTileKs * 128);
-  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_TILE)
+  if (kernel == LI4_KERNEL_BULK && (group != 128 || K == 0 || (K / 128) % 8 != 0))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the bulk-copy kernel needs group_size 128 and K a multiple "
+                     "of 1024");
+  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_BULK)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: unknown kernel %d", kernel);
   p->stream_ksplit = false;
   p->kernel = kernel;
@@ -1235,6 +1476,20 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     p->rt = (rows_req == 32) ? 2 : 1;
     p->n_tiles = (int)((N + 16 * p->rt - 1) / (16 * p->rt));
   }
+  if (kernel == LI4_KERNEL_BULK) {  // 16-row tiles of K ranges of 16 (or 8) ksteps through a shared-memory ring
+    p->rt = 1;
+    p->n_tiles = (int)((N + 15) / 16);
+    int ks = (p->n_ks % 16 == 0) ? 16 : 8;
+    if (split_req > 0) {
+      if (p->n_ks % split_req != 0 || (p->n_ks / split_req != 16 && p->n_ks / split_req != 8))
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the bulk-copy kernel takes K ranges of 8 or 16 ksteps "
+                         "(split=%d, K/128=%d)", split_req, p->n_ks);
+      ks = p->n_ks / split_req;
+    } else if (ks == 16 && (int64_t)p->n_tiles * (p->n_ks / 16) * 2 <= sm) {
+      ks = 8;  // few tiles: shorter K ranges put more CTAs to work
+    }
+    split = p->n_ks / ks;
+  }
   p->split = split;
   p->ks_per_split = (p->n_ks == 0) ? 0 : p->n_ks / split;
 
@@ -1256,6 +1511,18 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     int gx = p->stream_ksplit ? p->n_tiles : (p->n_tiles + kStreamWarps - 1) / kStreamWarps;
     if (max_ctas > 0 && gx > max_ctas / split) gx = max_ctas / split > 0 ? max_ctas / split : 1;
     p->grid_x = gx;  // capped by occupancy at launch
+  }
+  if (kernel == LI4_KERNEL_BULK) {
+    const int max_stages = (p->nt == 1) ? kBulkMaxStages : 6;
+    int gx = std::max(1, sm / split);
+    if (max_ctas > 0) gx = std::max(1, std::min(gx, max_ctas / split));
+    gx = std::min(gx, p->n_tiles);
+    const int per_cta = (p->n_tiles + gx - 1) / gx;
+    p->stages = std::min(max_stages, per_cta);
+    p->grid_x = gx;
+    const BulkLayout L = bulk_layout(p->ks_per_split);
+    p->smem = (size_t)p->stages * L.stage + (size_t)p->ks_per_split * p->nt * 8 * 256 +
+              (size_t)2 * kBulkConsumerWarps * 16 * 8 * p->nt * sizeof(float) + 2 * kBulkMaxStages * sizeof(uint64_t);
   }
   if (kernel == LI4_KERNEL_TILE) {
     p->smem = (size_t)kTileKs * p->nt * 8 * 256;
@@ -1392,8 +1659,34 @@ static int launch_stream_kernel(KernelT kernel, const Plan& p, const GemvArgs& a
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args), "int4_linear: streaming kernel launch");
 }
 
+template <typename KernelT>
+static int launch_bulk_kernel(KernelT kernel, const Plan& p, const GemvArgs& args, cudaStream_t stream) {
+  int rc = ensure_smem_limit(kernel, p.smem);
+  if (rc != LI4_OK) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.grid_x, (unsigned)p.split, 1);
+  cfg.blockDim = dim3(kBulkThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args, p.stages), "int4_linear: bulk-copy kernel launch");
+}
+
 static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
   const bool fused = args.norm_w != nullptr || args.epi != LI4_EPI_STORE;
+  if (p.kernel == LI4_KERNEL_BULK) {
+    const int sel = (p.nt - 1) * 2 + (fused ? 1 : 0);
+    switch (sel) {
+      case 0: return launch_bulk_kernel(gemv_bulk_kernel<1, false>, p, args, s);
+      case 1: return launch_bulk_kernel(gemv_bulk_kernel<1, true>, p, args, s);
+      case 2: return launch_bulk_kernel(gemv_bulk_kernel<2, false>, p, args, s);
+      default: return launch_bulk_kernel(gemv_bulk_kernel<2, true>, p, args, s);
+    }
+  }
   if (p.kernel == LI4_KERNEL_TILE) {
     const int sel = (p.nt - 1) * 4 + (p.rt - 1) * 2 + (fused ? 1 : 0);
     switch (sel) {
@@ -1529,6 +1822,14 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
     if (rc != LI4_OK) return rc;
   }
+  if (p.kernel == LI4_KERNEL_BULK && (!aligned16(scale) || !aligned16(zero) || ssn % 8 != 0)) {
+    // the scale / zero rows move as 16-byte-aligned bulk copies
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_ALIGNMENT, "int4_linear: the bulk-copy kernel needs 16-byte aligned scale / zero "
+                       "rows (row stride %% 8 == 0)");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
   if (p.ws_bytes > 0) {
     if (!workspace || workspace_bytes < p.ws_bytes)
       return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "
@@ -1587,7 +1888,7 @@ extern "C" size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t 
   if (li4::make_plan(M, N, K, group_size, sm, LI4_KERNEL_AUTO, 0, 0, 0, &p) != LI4_OK) return 0;
   // Enough for every kernel family and launch shape the dispatcher may pick.
   size_t best = p.ws_bytes;
-  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_TILE; ++kernel) {
+  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_BULK; ++kernel) {
     if (kernel == LI4_KERNEL_CUDA_CORE && M > 8) continue;
     if (li4::make_plan(M, N, K, group_size, sm, kernel, 0, 0, 0, &p) == LI4_OK && p.ws_bytes > best) best = p.ws_bytes;
   }
@@ -1609,6 +1910,19 @@ extern "C" int li4_int4_linear_ex(const void* x, const void* packed, const void*
                                   int max_ctas) {
   return li4::int4_linear_impl(x, packed, scale, zero, y, M, N, K, group_size, stride_xm, stride_pn, stride_sn,
                                stride_ym, workspace, workspace_bytes, stream, kernel, rows_per_cta, split, max_ctas);
+}
+
+extern "C" int li4_device_errors(unsigned* flags, int reset) {
+  if (!flags) return li4::set_error(LI4_ERR_INVALID_ARG, "device_errors: null output");
+  int rc = li4::check_cuda(cudaMemcpyFromSymbol(flags, li4::g_li4_device_error, sizeof(unsigned)),
+                           "device_errors: reading the flags");
+  if (rc == LI4_OK && reset) {
+    const unsigned zero = 0;
+    rc = li4::check_cuda(cudaMemcpyToSymbol(li4::g_li4_device_error, &zero, sizeof(unsigned)),
+                         "device_errors: clearing the flags");
+  }
+  if (rc == LI4_OK) li4::clear_error();
+  return rc;
 }
 
 extern "C" int li4_int4_linear_fused(const void* x, const void* packed, const void* scale, const void* zero, void* y,

@@ -24,7 +24,7 @@ LI4_ERR_CUDA = 5
 
 LI4_F16, LI4_BF16, LI4_F32 = 0, 1, 2
 WORKSPACE_COUNTER_BYTES = 65536  # LI4_WORKSPACE_COUNTER_BYTES
-KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA = 0, 1, 2
+KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA, KERNEL_STREAM, KERNEL_TILE, KERNEL_BULK = 0, 1, 2, 3, 4, 5
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -72,6 +72,7 @@ SIGNATURES = {
                                      ctypes.POINTER(Fusion), _P, _SZ, _P]),
     "li4_decode_attention": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "li4_argmax_rows": (_INT, [_P, _INT, _I64, _I64, _I64, _P, _I64, _P]),
+    "li4_device_errors": (_INT, [ctypes.POINTER(ctypes.c_uint), _INT]),
     "li4_dequantize": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_quantize": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
 }
@@ -115,6 +116,13 @@ def check(status: int, what: str = "") -> None:
     if status != LI4_OK:
         msg = last_error()
         raise Li4Error(status, f"{what}: {msg}" if what else msg)
+
+
+def device_errors(reset: bool = True) -> int:
+    """Device-side error flags (li4_device_errors); synchronises the device."""
+    flags = ctypes.c_uint(0)
+    check(lib().li4_device_errors(ctypes.byref(flags), int(reset)), "device_errors")
+    return flags.value
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -21,7 +21,7 @@ LLAMA_SHAPES = [  # (name, N = out_features, K = in_features)
     ("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
     ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192), ("lm_head", 128256, 2048),
 ]
-KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4}
+KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5}
 
 
 def supported(kernel: str, M: int, group: int = 128, K: int = 2048) -> bool:
@@ -32,6 +32,8 @@ def supported(kernel: str, M: int, group: int = 128, K: int = 2048) -> bool:
         return group >= 128 and K > 0
     if kernel == "tile":
         return group == 128 and K > 0 and K % 2048 == 0
+    if kernel == "bulk":
+        return group == 128 and K > 0 and K % 1024 == 0
     return True
 
 
@@ -207,6 +209,28 @@ def test_tile_launch_shapes(M, rows, max_ctas, N, K, g, cuda_device):
     y2 = torch.empty_like(y)
     int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["tile"], rows_per_cta=rows, max_ctas=max_ctas)
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+@pytest.mark.parametrize("M", [1, 5, 9, 16])
+@pytest.mark.parametrize("split", [0, 1, 2, 4, 8])
+@pytest.mark.parametrize("max_ctas", [0, 1, 7])
+@pytest.mark.parametrize("N,K", [(17, 2048), (300, 4096), (4100, 2048), (20000, 2048), (2049, 8192), (512, 1024)])
+def test_bulk_launch_shapes(M, split, max_ctas, N, K, g, cuda_device):
+    """Bulk-copy ring kernel: K ranges of 8 and 16 ksteps (split-K above), one to many tiles per CTA (the
+    ring wraps around its stages), partial last tiles; deterministic, and no device-side wait ran out."""
+    int4_gemv, native = g
+    n_ks = K // 128
+    if split and (n_ks % split or n_ks // split not in (8, 16)):
+        pytest.skip("the bulk kernel takes K ranges of 8 or 16 ksteps")
+    x, p, s, z, host = make_problem(N, K, M, seed=N + K + M + split + max_ctas)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["bulk"], split=split, max_ctas=max_ctas)
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["bulk"], split=split, max_ctas=max_ctas)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+    assert native.device_errors() == 0
 
 
 def test_split_counters_reset_across_launches(g, cuda_device):
