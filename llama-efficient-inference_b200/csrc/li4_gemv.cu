@@ -1125,17 +1125,18 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
 // Bulk-copy pipeline kernel.  A producer warp moves whole 16-row tiles of one K
 // range (packed rows, scale and zero rows) from HBM into a ring of shared-memory
 // stages with cp.async.bulk (the TMA engine's 1-D bulk copy), completing on
-// per-stage mbarriers; eight consumer warps split each stage's ksteps between
-// them, reduce the tile in shared memory and run the epilogue.  The ring holds
-// up to kBulkMaxStages x 18 KiB per SM in flight (against 4-5 KiB per warp for
-// the register rings), and the first stages are requested before
+// per-stage mbarriers; each of eight consumer warps takes every eighth tile
+// whole (all its ksteps, no cross-warp reduction) and runs the epilogue from
+// its registers.  The ring holds up to kBulkMaxStages x 18 KiB per SM in
+// flight (against 4-5 KiB per warp for the register rings), and the first
+// stages are requested before
 // griddepcontrol.wait, so the weight stream of a launch overlaps the tail of the
 // preceding kernel.  Every mbarrier wait is bounded; a wait that runs out sets
 // g_li4_device_error and the kernel drains its own copies and returns.
 // ---------------------------------------------------------------------------
 constexpr int kBulkConsumerWarps = 8;
 constexpr int kBulkThreads = (kBulkConsumerWarps + 1) * 32;  // + one producer warp
-constexpr int kBulkMaxStages = 8;
+constexpr int kBulkMaxStages = 10;
 constexpr unsigned kBulkWaitLimit = 1u << 22;  // try_wait rounds: well under a second of polling, never forever
 
 __device__ unsigned g_li4_device_error;  // bit 0: a bounded pipeline wait ran out
@@ -1181,10 +1182,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       : "memory");
 }
 
-// Shared-memory layout of one stage: 16 packed rows of K-range/2 bytes at a
-// pitch of K-range/2 + 64 (the 64 keeps the 16-byte reads of the eight row
-// pairs of a quarter warp on distinct banks), then 16 scale rows and 16 zero
-// rows of KS fp16 values.
+// Shared-memory layout of one stage: 16 packed rows of K-range/2 bytes, then
+// 16 scale rows and 16 zero rows of KS fp16 values.  When the tile's rows are
+// one contiguous block of HBM (contiguous tensors, one K range) a stage is
+// three bulk copies and the rows sit back to back; otherwise each row is its
+// own copy and the row pitch is K-range/2 + 64, which keeps the 16-byte reads
+// of the eight row pairs of a quarter warp on distinct banks.
 struct BulkLayout {
   int ks;       // ksteps per K range (8 or 16)
   int pitch;    // bytes between packed rows
@@ -1192,29 +1195,27 @@ struct BulkLayout {
   int stage;    // bytes per stage (multiple of 128)
 };
 
-__host__ __device__ inline BulkLayout bulk_layout(int ks) {
+__host__ __device__ inline BulkLayout bulk_layout(int ks, bool contig) {
   BulkLayout L;
   L.ks = ks;
-  L.pitch = ks * 64 + 64;
+  L.pitch = ks * 64 + (contig ? 0 : 64);
   L.sz_off = 16 * L.pitch;
   L.stage = (L.sz_off + 2 * 16 * ks * 2 + 127) & ~127;
   return L;
 }
 
 template <int NT, bool FUSED>
-__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs a, int stages) {
+__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs a, int stages,
+                                                                     int contig) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int M8 = 8;           // x rows padded to 8 per n-tile (as the tile kernel)
-  constexpr int COLS = 8 * NT;
   const int ks_n = a.ks_per_split;
-  const BulkLayout L = bulk_layout(ks_n);
+  const BulkLayout L = bulk_layout(ks_n, contig != 0);
   uint8_t* ring = smem;
   uint8_t* xs = ring + (size_t)stages * L.stage;
-  float* red = reinterpret_cast<float*>(xs + (size_t)ks_n * NT * M8 * 256);  // [2][warps][16][COLS]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kBulkConsumerWarps * 16 * COLS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs + (size_t)ks_n * NT * M8 * 256);
   uint64_t* empty = full + kBulkMaxStages;
   __shared__ float s_rstd[LI4_MAX_M];
-  __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks0 = blockIdx.y * ks_n;
@@ -1224,7 +1225,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kBulkConsumerWarps);
+      mbar_init(&empty[s], 1);  // the consumer warp that owns the stage's tile
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1243,7 +1244,14 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
       __syncwarp();
       const int tile = (int)blockIdx.x + it * (int)gridDim.x;
       uint8_t* st = ring + (size_t)s * L.stage;
-      if (lane < 16) {
+      if (contig) {  // rows tile*16 .. +15 are one block of packed, scale and zero (the last tile is clamped)
+        if (lane == 0) {
+          const int r0 = min(tile * 16, a.N - 16);
+          bulk_g2s(st, a.packed + (long long)r0 * a.spn, 16 * ks_n * 64, &full[s]);
+          bulk_g2s(st + L.sz_off, a.scale + (long long)r0 * a.ssn, 16 * ks_n * 2, &full[s]);
+          bulk_g2s(st + L.sz_off + 16 * ks_n * 2, a.zero + (long long)r0 * a.ssn, 16 * ks_n * 2, &full[s]);
+        }
+      } else if (lane < 16) {
         int r = tile * 16 + lane;
         r = r < a.N ? r : a.N - 1;
         bulk_g2s(st + lane * L.pitch, a.packed + (long long)r * a.spn + (long long)ks0 * 64, ks_n * 64, &full[s]);
@@ -1263,11 +1271,11 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     return;
   }
 
-  // ---------------- consumer warps ----------------
+  // ---------------- consumer warps: one whole tile per warp ----------------
   const int grp = lane >> 2, quad = lane & 3;
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
   if (FUSED && a.norm_w != nullptr) {
-    // compute_rstd over the consumer warps only (named barrier 1)
+    // RMSNorm factors over the consumer warps only (named barrier 1)
     __shared__ float part[kBulkConsumerWarps][LI4_MAX_M];
     for (int m = 0; m < a.M; ++m) {
       const __half* row = a.x + (long long)m * a.sxm;
@@ -1300,7 +1308,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
   constexpr int ks_stride = NT * nt_stride;
 
   bool ok = true;
-  for (int it = 0; it < my_tiles; ++it) {
+  for (int it = warp; it < my_tiles; it += kBulkConsumerWarps) {
     const int s = it % stages;
     const int tile = (int)blockIdx.x + it * (int)gridDim.x;
     if (ok) ok = mbar_wait_bounded(&full[s], (it / stages) & 1);
@@ -1313,46 +1321,55 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
       const uint8_t* st = ring + (size_t)s * L.stage;
       const unsigned short* sc = reinterpret_cast<const unsigned short*>(st + L.sz_off);
       const unsigned short* ze = sc + 16 * ks_n;
-      for (int ks = warp; ks < ks_n; ks += kBulkConsumerWarps) {
+      // stage row of tile row j: a clamped contiguous last tile starts `shift` rows early
+      const int shift = contig ? tile * 16 - min(tile * 16, a.N - 16) : 0;
+      const int ra = min(grp + shift, 15), rb2 = min(grp + 8 + shift, 15);
+      const uint8_t* row_lo = st + ra * L.pitch + quad * 16;
+      const uint8_t* row_hi = st + rb2 * L.pitch + quad * 16;
+#pragma unroll 4
+      for (int ks = 0; ks < ks_n; ++ks) {
         StreamUnit u;
-        u.lo = *reinterpret_cast<const uint4*>(st + grp * L.pitch + ks * 64 + quad * 16);
-        u.hi = *reinterpret_cast<const uint4*>(st + (grp + 8) * L.pitch + ks * 64 + quad * 16);
-        u.sz_lo = (uint32_t)sc[grp * ks_n + ks] | ((uint32_t)ze[grp * ks_n + ks] << 16);
-        u.sz_hi = (uint32_t)sc[(grp + 8) * ks_n + ks] | ((uint32_t)ze[(grp + 8) * ks_n + ks] << 16);
+        u.lo = *reinterpret_cast<const uint4*>(row_lo + ks * 64);
+        u.hi = *reinterpret_cast<const uint4*>(row_hi + ks * 64);
+        u.sz_lo = (uint32_t)sc[ra * ks_n + ks] | ((uint32_t)ze[ra * ks_n + ks] << 16);
+        u.sz_hi = (uint32_t)sc[rb2 * ks_n + ks] | ((uint32_t)ze[rb2 * ks_n + ks] << 16);
         stream_compute<NT>(u, xs + ks * ks_stride, nt_stride, boff, bvalid, acc);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done reading the stage
-    // cross-warp reduction of the tile (double-buffered by tile parity)
-    float* rb = red + (it & 1) * (kBulkConsumerWarps * 16 * COLS);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        rb[(warp * 16 + grp + 8 * (e >> 1)) * COLS + nt * 8 + 2 * quad + (e & 1)] = acc[nt][e];
-    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+    if (lane == 0) mbar_arrive(&empty[s]);  // the stage is free for the producer
     const int row0 = tile * 16;
     const int rows = min(16, a.N - row0);
-    const WarpTileSum<COLS, kBulkConsumerWarps> tile_sum{rb};
-    if (a.split == 1) {
-      emit_tile<FUSED>(a, tile, threadIdx.x, kBulkConsumerWarps * 32, tile_sum);
-    } else {
-      for (int idx = threadIdx.x; idx < rows * a.M; idx += kBulkConsumerWarps * 32) {
-        const int r = idx / a.M, m = idx - r * a.M;
-        a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = tile_sum(r, m);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (FUSED && a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int m = nt * 8 + 2 * quad + e;
+          if (m < a.M) emit_pair(a, m, tile * 8 + grp, acc[nt][e], acc[nt][e + 2]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
+          if (r < rows && m < a.M) {
+            if (a.split == 1) emit_value<FUSED>(a, m, row0 + r, acc[nt][e]);
+            else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
+          }
+        }
       }
-      __threadfence();  // every writer publishes its partials before the arrival count
-      asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
-      if (threadIdx.x == 0)
-        s_last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1 : 0;
-      asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
-      if (s_last) {  // last K range to arrive: fixed-order sum, epilogue, counter reset
+    }
+    if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
+      __threadfence();
+      __syncwarp();
+      unsigned last = 0;
+      if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1u : 0u;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
         __threadfence();
-        emit_tile<FUSED>(a, tile, threadIdx.x, kBulkConsumerWarps * 32,
-                         PartialSum{a.partial + row0, a.M, a.N, a.split});
-        asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
-        if (threadIdx.x == 0) a.counters[tile] = 0u;
+        emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
+        __syncwarp();
+        if (lane == 0) a.counters[tile] = 0u;
       }
     }
   }
@@ -1378,6 +1395,7 @@ struct Plan {
   size_t ws_bytes;     // total
   bool stream_ksplit;  // LI4_KERNEL_STREAM: K-split mode
   int stages;          // LI4_KERNEL_BULK: shared-memory ring stages
+  bool bulk_contig;    // LI4_KERNEL_BULK: tiles move as three contiguous copies (set at launch from the strides)
 };
 
 static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -1513,16 +1531,16 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     p->grid_x = gx;  // capped by occupancy at launch
   }
   if (kernel == LI4_KERNEL_BULK) {
-    const int max_stages = (p->nt == 1) ? kBulkMaxStages : 6;
+    const int max_stages = (p->nt == 1) ? kBulkMaxStages : 8;
     int gx = std::max(1, sm / split);
     if (max_ctas > 0) gx = std::max(1, std::min(gx, max_ctas / split));
     gx = std::min(gx, p->n_tiles);
     const int per_cta = (p->n_tiles + gx - 1) / gx;
     p->stages = std::min(max_stages, per_cta);
     p->grid_x = gx;
-    const BulkLayout L = bulk_layout(p->ks_per_split);
+    const BulkLayout L = bulk_layout(p->ks_per_split, false);  // the padded layout: an upper bound
     p->smem = (size_t)p->stages * L.stage + (size_t)p->ks_per_split * p->nt * 8 * 256 +
-              (size_t)2 * kBulkConsumerWarps * 16 * 8 * p->nt * sizeof(float) + 2 * kBulkMaxStages * sizeof(uint64_t);
+              2 * kBulkMaxStages * sizeof(uint64_t);
   }
   if (kernel == LI4_KERNEL_TILE) {
     p->smem = (size_t)kTileKs * p->nt * 8 * 256;
@@ -1673,7 +1691,9 @@ static int launch_bulk_kernel(KernelT kernel, const Plan& p, const GemvArgs& arg
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args, p.stages), "int4_linear: bulk-copy kernel launch");
+  // contiguous tiles: one K range, rows back to back in packed / scale / zero, and N >= 16
+  const int contig = (p.split == 1 && args.spn == args.K / 2 && args.ssn == args.K / 128 && args.N >= 16) ? 1 : 0;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args, p.stages, contig), "int4_linear: bulk-copy kernel launch");
 }
 
 static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
