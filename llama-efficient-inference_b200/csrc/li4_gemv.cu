@@ -1134,8 +1134,10 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
 // preceding kernel.  Every mbarrier wait is bounded; a wait that runs out sets
 // g_li4_device_error and the kernel drains its own copies and returns.
 // ---------------------------------------------------------------------------
-constexpr int kBulkConsumerWarps = 8;
-constexpr int kBulkThreads = (kBulkConsumerWarps + 1) * 32;  // + one producer warp
+// Consumer warps: 15 for M <= 8 (with the producer, 16 warps = 4 per scheduler at 128 registers a
+// thread), 8 for M <= 16.
+__host__ __device__ constexpr int bulk_consumer_warps(int nt) { return nt == 1 ? 15 : 8; }
+__host__ __device__ constexpr int bulk_threads(int nt) { return (bulk_consumer_warps(nt) + 1) * 32; }  // + producer
 constexpr int kBulkMaxStages = 10;
 constexpr unsigned kBulkWaitLimit = 1u << 22;  // try_wait rounds: well under a second of polling, never forever
 
@@ -1205,8 +1207,9 @@ __host__ __device__ inline BulkLayout bulk_layout(int ks, bool contig) {
 }
 
 template <int NT, bool FUSED>
-__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs a, int stages,
-                                                                     int contig) {
+__global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs a, int stages,
+                                                                        int contig) {
+  constexpr int CW = bulk_consumer_warps(NT);
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int M8 = 8;           // x rows padded to 8 per n-tile (as the tile kernel)
   const int ks_n = a.ks_per_split;
@@ -1232,7 +1235,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == kBulkConsumerWarps) {
+  if (warp == CW) {
     // ---------------- producer warp ----------------
     const unsigned stage_bytes = 16u * (unsigned)(ks_n * 64) + 2u * 16u * (unsigned)(ks_n * 2);
     bool ok = true;
@@ -1276,11 +1279,11 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
   if (FUSED && a.norm_w != nullptr) {
     // RMSNorm factors over the consumer warps only (named barrier 1)
-    __shared__ float part[kBulkConsumerWarps][LI4_MAX_M];
+    __shared__ float part[CW][LI4_MAX_M];
     for (int m = 0; m < a.M; ++m) {
       const __half* row = a.x + (long long)m * a.sxm;
       float ss = 0.f;
-      for (int k = threadIdx.x; k < a.K; k += kBulkConsumerWarps * 32) {
+      for (int k = threadIdx.x; k < a.K; k += CW * 32) {
         const float v = __half2float(row[k]);
         ss = fmaf(v, v, ss);
       }
@@ -1288,17 +1291,17 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (lane == 0) part[warp][m] = ss;
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
     if (threadIdx.x < a.M) {
       float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < kBulkConsumerWarps; ++w) t += part[w][threadIdx.x];
+      for (int w = 0; w < CW; ++w) t += part[w][threadIdx.x];
       s_rstd[threadIdx.x] = rsqrtf(t / (float)a.K + a.norm_eps);
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
   }
-  stage_x<NT, kBulkConsumerWarps * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
-  asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumerWarps * 32) : "memory");
+  stage_x<NT, CW * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
+  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
   int boff[4];
@@ -1308,7 +1311,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
   constexpr int ks_stride = NT * nt_stride;
 
   bool ok = true;
-  for (int it = warp; it < my_tiles; it += kBulkConsumerWarps) {
+  for (int it = warp; it < my_tiles; it += CW) {
     const int s = it % stages;
     const int tile = (int)blockIdx.x + it * (int)gridDim.x;
     if (ok) ok = mbar_wait_bounded(&full[s], (it / stages) & 1);
@@ -1683,7 +1686,7 @@ static int launch_bulk_kernel(KernelT kernel, const Plan& p, const GemvArgs& arg
   if (rc != LI4_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid_x, (unsigned)p.split, 1);
-  cfg.blockDim = dim3(kBulkThreads, 1, 1);
+  cfg.blockDim = dim3(bulk_threads(p.nt), 1, 1);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
