@@ -1125,20 +1125,21 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
 // Bulk-copy pipeline kernel.  A producer warp moves whole 16-row tiles of one K
 // range (packed rows, scale and zero rows) from HBM into a ring of shared-memory
 // stages with cp.async.bulk (the TMA engine's 1-D bulk copy), completing on
-// per-stage mbarriers; each of eight consumer warps takes every eighth tile
-// whole (all its ksteps, no cross-warp reduction) and runs the epilogue from
-// its registers.  The ring holds up to kBulkMaxStages x 18 KiB per SM in
+// per-stage mbarriers; consumer warp w owns ring stage w, takes every
+// `stages`-th tile whole (all its ksteps, no cross-warp reduction) and runs the
+// epilogue from its registers.  The ring holds up to kBulkMaxStages x 18 KiB per SM in
 // flight (against 4-5 KiB per warp for the register rings), and the first
 // stages are requested before
 // griddepcontrol.wait, so the weight stream of a launch overlaps the tail of the
 // preceding kernel.  Every mbarrier wait is bounded; a wait that runs out sets
 // g_li4_device_error and the kernel drains its own copies and returns.
 // ---------------------------------------------------------------------------
-// Consumer warps: 15 for M <= 8 (with the producer, 16 warps = 4 per scheduler at 128 registers a
-// thread), 8 for M <= 16.
-__host__ __device__ constexpr int bulk_consumer_warps(int nt) { return nt == 1 ? 15 : 8; }
+// Consumer warps: one per ring stage at most (10 for M <= 8, 8 for M <= 16).  Warp w consumes
+// only stage w (tiles w, w + stages, ...), so it waits on each stage's uses in order and never
+// polls an mbarrier phase more than one ahead of the barrier (which would read as complete).
+__host__ __device__ constexpr int bulk_consumer_warps(int nt) { return nt == 1 ? 10 : 8; }
 __host__ __device__ constexpr int bulk_threads(int nt) { return (bulk_consumer_warps(nt) + 1) * 32; }  // + producer
-constexpr int kBulkMaxStages = 10;
+constexpr int kBulkMaxStages = 10;  // = bulk_consumer_warps(1)
 constexpr unsigned kBulkWaitLimit = 1u << 22;  // try_wait rounds: well under a second of polling, never forever
 
 __device__ unsigned g_li4_device_error;  // bit 0: a bounded pipeline wait ran out
@@ -1311,8 +1312,8 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
   constexpr int ks_stride = NT * nt_stride;
 
   bool ok = true;
-  for (int it = warp; it < my_tiles; it += CW) {
-    const int s = it % stages;
+  for (int it = warp; it < my_tiles; it += stages) {  // stage `warp` only; warps >= stages have none
+    const int s = warp;
     const int tile = (int)blockIdx.x + it * (int)gridDim.x;
     if (ok) ok = mbar_wait_bounded(&full[s], (it / stages) & 1);
     float acc[NT][4];
