@@ -1489,9 +1489,10 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
       while (p->n_ks % split != 0 || p->n_ks / split > max_ks) ++split;
     }
     p->stream_ksplit = (int64_t)p->n_tiles < 4LL * sm && p->n_ks / split >= kStreamWarps;
+    // more K ranges while the CTAs stay resident (two per SM) and every warp keeps >= 2 ksteps
     if (split_req <= 0 && p->stream_ksplit)
       while ((int64_t)p->n_tiles * split * 2 <= 2LL * sm && p->n_ks % (2 * split) == 0 &&
-             p->n_ks / (2 * split) >= kStreamWarps)
+             p->n_ks / (2 * split) >= 2 * kStreamWarps)
         split *= 2;
   }
   if (kernel == LI4_KERNEL_TILE) {  // K ranges of exactly kTileKs ksteps; 16 or 32 rows per warp tile
