@@ -1,6 +1,7 @@
 """Tensor-parallel INT4 decode on 2 GPUs (NCCL): the sharded tiny model matches the
 unsharded one, and decode replayed from one CUDA graph (collectives inside the graph)
-gives the same greedy tokens as eager decoding.  Runs as child processes; skipped on
+gives the same greedy tokens as eager decoding, as does the fused step (llama.fused) on the
+shards.  Runs as child processes; skipped on
 machines with fewer than 2 GPUs."""
 import json
 
@@ -21,3 +22,4 @@ def test_tp2_int4_model_matches_unsharded():
         rec = json.loads(out.strip().splitlines()[-1])
         assert rec["prefill_rel_err"] < 1e-2, rec
         assert rec["eager_tokens_equal"] and rec["graph_tokens_equal"], rec
+        assert rec["fused_graph_tokens_equal"], rec

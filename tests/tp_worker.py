@@ -90,11 +90,18 @@ def gpu_parity():
         graph = DecodeGraph(part, prompt.shape[0])
         t_graph = graph.tokens(prompt, steps)
         torch.cuda.synchronize(dev)
+        del graph
+        # the fused step (llama.fused) on the shards: row-parallel partial sums all-reduced in the graph
+        part.enable_fused_decode()
+        fgraph = DecodeGraph(part, prompt.shape[0])
+        t_fused = fgraph.tokens(prompt, steps)
+        torch.cuda.synchronize(dev)
+        del fgraph
     same_eager = bool(torch.equal(t_full, t_part))
     same_graph = bool(torch.equal(t_part, t_graph))
-    del graph
+    same_fused = bool(torch.equal(t_full, t_fused))
     print(json.dumps({"rank": rank, "world": world, "prefill_rel_err": prefill_err, "eager_tokens_equal": same_eager,
-                      "graph_tokens_equal": same_graph}), flush=True)
+                      "graph_tokens_equal": same_graph, "fused_graph_tokens_equal": same_fused}), flush=True)
 
 
 def dead_peer():
