@@ -326,6 +326,77 @@ def per_shape_isolated(stream: Stream, reps: int = 5):
     return out
 
 
+SWEEP_SHAPES = LAYER_SHAPES[:2] + LAYER_SHAPES[4:5] + LAYER_SHAPES[6:] + [LM_HEAD, ("qkv_fused", 3072, 2048),
+                                                                           ("gate_up_fused", 16384, 2048)]
+KERNEL_NAMES = {0: "auto", 1: "cuda_core", 2: "mma", 3: "stream", 4: "tile", 5: "bulk"}
+
+
+def kernel_sweep(a):
+    """--sweep: every kernel family x launch shape on the decode shapes (one JSON line per config, then the
+    best per shape).  Each config is a CUDA graph of back-to-back launches over rotating weight copies
+    totalling > 3x L2, device time per launch, median of 5 replays."""
+    from llama.int4_gemv import int4_linear_out
+    from llama.quantize import QuantizedLinear
+
+    dev = torch.device("cuda", 0)
+    Ms = [int(v) for v in a.sweep_m.split(",")]
+    kernels = [int(v) for v in a.sweep_kernels.split(",")]
+    out = []
+    for name, N, K in SWEEP_SHAPES:
+        wbytes = gemv_bytes(N, K, 0)
+        copies = max(2, (3 * L2_BYTES) // wbytes + 1)
+        gen = torch.Generator(device=dev).manual_seed(N + K)
+        w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+        p, s, z = QuantizedLinear.quantize_tensor(w, GROUP)
+        del w
+        ws = [(p, s, z)] + [(p.clone(), s.clone(), z.clone()) for _ in range(copies - 1)]
+        n_ks = K // 128
+        for M in Ms:
+            x = torch.randn(M, K, generator=gen, device=dev).half()
+            y = torch.empty(M, N, dtype=torch.float16, device=dev)
+            for kernel in kernels:
+                for rows in ((16, 32) if kernel in (1, 2, 4) else (16,)):
+                    for sp in [0] + [v for v in (1, 2, 4, 8) if n_ks % v == 0]:
+                        if kernel == 1 and M > 8:
+                            continue
+
+                        def run():
+                            for pi, si, zi in ws:
+                                int4_linear_out(x, pi, si, zi, y, GROUP, kernel=kernel, rows_per_cta=rows, split=sp)
+
+                        rec = dict(shape=name, N=N, K=K, M=M, kernel=KERNEL_NAMES[kernel], rows=rows, split=sp)
+                        try:
+                            run()
+                            torch.cuda.synchronize(dev)
+                            g = torch.cuda.CUDAGraph()
+                            with torch.cuda.graph(g):
+                                run()
+                            g.replay()
+                            ts = []
+                            for _ in range(5):
+                                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                                e0.record()
+                                g.replay()
+                                e1.record()
+                                torch.cuda.synchronize(dev)
+                                ts.append(e0.elapsed_time(e1) / copies)
+                            us = statistics.median(ts) * 1e3
+                            rec.update(us=round(us, 2), GBps=round(gemv_bytes(N, K, M) / us / 1e3, 1))
+                            del g
+                        except Exception as e:  # noqa: BLE001 -- a launch shape the family rejects
+                            rec["error"] = str(e)[:160]
+                        out.append(rec)
+                        print(json.dumps(rec), flush=True)
+        del ws
+        torch.cuda.empty_cache()
+    best = {}
+    for r in out:
+        if "us" in r and ((r["shape"], r["M"]) not in best or r["us"] < best[(r["shape"], r["M"])]["us"]):
+            best[(r["shape"], r["M"])] = r
+    for (shape, M), r in sorted(best.items()):
+        print(json.dumps({"best": shape, "M": M, **{k: r[k] for k in ("kernel", "rows", "split", "us", "GBps")}}))
+
+
 def profile_shape(a):
     """--profile-shape NAME: `--launches` eager launches of one shape (a small case for ncu captures)."""
     from llama.int4_gemv import int4_linear_out
@@ -660,9 +731,15 @@ def main():
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
+    ap.add_argument("--sweep", action="store_true", help="kernel-family x launch-shape sweep of the decode shapes")
+    ap.add_argument("--sweep-m", default="1,8,16")
+    ap.add_argument("--sweep-kernels", default="0,1,2,3,4,5", help="0 auto, 1 cuda_core, 2 mma, 3 stream, 4 tile, 5 bulk")
     a = ap.parse_args()
     if a.profile_shape:
         profile_shape(a)
+        return
+    if a.sweep:
+        kernel_sweep(a)
         return
     if a.warmup < 3:
         a.warmup = 3
