@@ -1421,14 +1421,15 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
 
   int kernel = kernel_req;
   if (kernel == LI4_KERNEL_AUTO) {
-    // By measured B200 sweeps of the Llama-3.2-1B shapes: tile streaming when
-    // every warp slot gets several 16-row x 2048-k tiles (lm_head-sized N);
-    // the bulk-copy ring when each SM gets about four tiles or more
-    // (fused gate/up, and down_proj at M > 8); streaming warps below that;
-    // CUDA-core / MMA kernels for groups below 128.
+    // By measured B200 sweeps of the Llama-3.2-1B shapes (bench.py --sweep):
+    // tile streaming when every warp slot gets several 16-row x 2048-k tiles
+    // (lm_head-sized N); the bulk-copy ring for 2 <= M <= 8, and otherwise when
+    // each SM gets about four tiles or more (fused gate/up; down_proj at M > 8);
+    // streaming warps below that; CUDA-core / MMA kernels for groups below 128.
     const int64_t tiles_2048 = ((N + 15) / 16) * std::max<int64_t>(1, K / 2048);
     if (group == 128 && K > 0 && K % 2048 == 0 && tiles_2048 >= 32LL * sm) kernel = LI4_KERNEL_TILE;
-    else if (group == 128 && K > 0 && K % 1024 == 0 && (tiles_2048 >= 4LL * sm || (M > 8 && tiles_2048 >= 2LL * sm)))
+    else if (group == 128 && K > 0 && K % 1024 == 0 &&
+             ((M >= 2 && M <= 8) || tiles_2048 >= 4LL * sm || (M > 8 && tiles_2048 >= 2LL * sm)))
       kernel = LI4_KERNEL_BULK;
     else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
