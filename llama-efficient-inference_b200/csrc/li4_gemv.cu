@@ -1240,10 +1240,12 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
     // ---------------- producer warp ----------------
     const unsigned stage_bytes = 16u * (unsigned)(ks_n * 64) + 2u * 16u * (unsigned)(ks_n * 2);
     bool ok = true;
+    int issued = 0;
     for (int it = 0; it < my_tiles && ok; ++it) {
       const int s = it % stages;
       if (it >= stages) ok = mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1);
       if (!ok) break;
+      issued = it + 1;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_bytes);
       __syncwarp();
       const int tile = (int)blockIdx.x + it * (int)gridDim.x;
@@ -1267,10 +1269,11 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
                  ks_n * 2, &full[s]);
       }
     }
-    if (!ok) {  // drain: the copies already issued land before the CTA exits
-      for (int it = (my_tiles > stages ? my_tiles - stages : 0); it < my_tiles; ++it)
-        mbar_wait_bounded(&full[it % stages], (it / stages) & 1);
-    }
+    // Drain: the last fill of every stage has landed before the producer leaves (a stage is
+    // refilled only after its previous fill was consumed, so these are the only copies that
+    // can be in flight; on the normal path they complete as the data arrives).
+    for (int it = (issued > stages ? issued - stages : 0); it < issued; ++it)
+      mbar_wait_bounded(&full[it % stages], (it / stages) & 1);
     pdl_wait_primary();  // every thread of the grid passes the dependency wait
     return;
   }
