@@ -208,7 +208,7 @@ int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, 
 
 /* out[r * out_stride] = argmax of row r of logits [rows, cols] (dtype LI4_F16 or
  * LI4_F32, row stride `stride` elements): the first index of the row's maximum,
- * a NaN counting as the maximum, as torch.argmax.  One CTA per row.
+ * a NaN counting as the maximum, as torch.argmax.  One cluster of 8 CTAs per row.
  * Replaces: the greedy logits[:, -1].argmax(-1) of the decode loop
  * (bench.py:154-161, llama/generation.py:59-60). */
 int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,

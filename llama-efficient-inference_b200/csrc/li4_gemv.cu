@@ -171,30 +171,38 @@ __device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, 
 }
 
 // Per-row 1 / rms of x for the RMSNorm prologue: s_rstd[m] = rsqrt(mean_k x[m,k]^2 + eps),
-// the mean in fp32 over all K columns (llama/model.py:61).  All THREADS threads call it.
-template <int THREADS>
-__device__ __forceinline__ void compute_rstd(const GemvArgs& a, float* s_rstd) {
-  __shared__ float part[THREADS / 32][LI4_MAX_M];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int m = 0; m < a.M; ++m) {
+// the mean in fp32 over all K columns (llama/model.py:61).  One warp per row, 16-byte loads
+// unrolled so a row's loads are in flight together; the caller synchronises before use.
+template <int WARPS>
+__device__ __forceinline__ void rms_factors(const GemvArgs& a, float* s_rstd, int warp, int lane) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
+  for (int m = warp; m < a.M; m += WARPS) {
     const __half* row = a.x + (long long)m * a.sxm;
     float ss = 0.f;
-    for (int k = threadIdx.x; k < a.K; k += THREADS) {
-      const float v = __half2float(row[k]);
-      ss = fmaf(v, v, ss);
+    if (vec) {
+      const uint4* r4 = reinterpret_cast<const uint4*>(row);
+      const int n4 = a.K >> 3;
+#pragma unroll 4
+      for (int c = lane; c < n4; c += 32) {
+        const uint4 u = r4[c];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          ss = fmaf(f.x, f.x, ss);
+          ss = fmaf(f.y, f.y, ss);
+        }
+      }
+    } else {
+      for (int k = lane; k < a.K; k += 32) {
+        const float v = __half2float(row[k]);
+        ss = fmaf(v, v, ss);
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) part[warp][m] = ss;
+    if (lane == 0) s_rstd[m] = rsqrtf(ss / (float)a.K + a.norm_eps);
   }
-  __syncthreads();
-  if (threadIdx.x < a.M) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < THREADS / 32; ++w) t += part[w][threadIdx.x];
-    s_rstd[threadIdx.x] = rsqrtf(t / (float)a.K + a.norm_eps);
-  }
-  __syncthreads();
 }
 
 // fp16(fp16(x * rstd) * w): RMSNorm's output cast (type_as) and its fp16 weight product.
@@ -234,7 +242,7 @@ __device__ __forceinline__ uint4 lds128_ordered(const uint8_t* p) {
   return r;
 }
 
-// s_rstd: per-row RMSNorm factors (compute_rstd) when a.norm_w is set, else unused.
+// s_rstd: per-row RMSNorm factors (rms_factors) when a.norm_w is set, else unused.
 template <int NT, int THREADS = kThreads, bool NORM = false>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
                                         const float* s_rstd = nullptr) {
@@ -795,7 +803,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
   }
   pdl_wait_primary();  // x is written by the preceding kernel
   __shared__ float s_rstd[LI4_MAX_M];
-  if (FUSED && a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
+  if (FUSED && a.norm_w != nullptr) {
+    rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    __syncthreads();
+  }
   stage_x<NT, kStreamThreads, FUSED>(a, ks0, nks, M8, xs, s_rstd);
   __syncthreads();
 
@@ -1044,7 +1055,10 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
   }
   pdl_wait_primary();  // x is written by the preceding kernel
   __shared__ float s_rstd[LI4_MAX_M];
-  if (FUSED && a.norm_w != nullptr) compute_rstd<kStreamThreads>(a, s_rstd);
+  if (FUSED && a.norm_w != nullptr) {
+    rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    __syncthreads();
+  }
   stage_x<NT, kStreamThreads, FUSED>(a, ks0, NKS, M8, xs, s_rstd);
   __syncthreads();
 
@@ -1281,27 +1295,8 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
   // ---------------- consumer warps: one whole tile per warp ----------------
   const int grp = lane >> 2, quad = lane & 3;
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
-  if (FUSED && a.norm_w != nullptr) {
-    // RMSNorm factors over the consumer warps only (named barrier 1)
-    __shared__ float part[CW][LI4_MAX_M];
-    for (int m = 0; m < a.M; ++m) {
-      const __half* row = a.x + (long long)m * a.sxm;
-      float ss = 0.f;
-      for (int k = threadIdx.x; k < a.K; k += CW * 32) {
-        const float v = __half2float(row[k]);
-        ss = fmaf(v, v, ss);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) part[warp][m] = ss;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
-    if (threadIdx.x < a.M) {
-      float t = 0.f;
-#pragma unroll
-      for (int w = 0; w < CW; ++w) t += part[w][threadIdx.x];
-      s_rstd[threadIdx.x] = rsqrtf(t / (float)a.K + a.norm_eps);
-    }
+  if (FUSED && a.norm_w != nullptr) {  // RMSNorm factors over the consumer warps only (named barrier 1)
+    rms_factors<CW>(a, s_rstd, warp, lane);
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
   }
   stage_x<NT, CW * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);

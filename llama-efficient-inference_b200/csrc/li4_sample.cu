@@ -1,6 +1,6 @@
 // li4_sample.cu -- greedy next-token selection on the GPU, sm_100a.
 //
-// One CTA per row of logits: the index of the row's maximum, the first one on
+// One cluster of CTAs per row of logits: the index of the row's maximum, the first one on
 // ties, a NaN counting as the maximum -- torch.argmax's answer (the
 // reference's greedy step, bench.py:154-161 / llama/generation.py:59-60).
 // Reading fp16 logits is exact: the reference's fp32 logits are the same
@@ -8,9 +8,15 @@
 #include "li4_common.cuh"
 #include "li4_internal.h"
 
+#include <algorithm>
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
+
 namespace li4 {
 
-constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxCluster = 8;
 
 struct Best {
   float v;
@@ -30,33 +36,44 @@ __device__ __forceinline__ void take(Best& best, float v, long long i) {
   if (better(c, best)) best = c;
 }
 
+// A cluster of kArgmaxCluster CTAs per row: CTA c scans columns [c*chunk, (c+1)*chunk) with
+// 16-byte loads unrolled so they are in flight together, and the cluster's first CTA picks
+// the winner among the CTAs' candidates through distributed shared memory.
 template <bool F16>
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void* logits, long long cols,
                                                                      long long stride, long long* out,
-                                                                     long long out_stride) {
+                                                                     long long out_stride, long long chunk) {
   __shared__ Best s_best[kArgmaxThreads / 32];
-  const long long row = blockIdx.x;
+  __shared__ Best s_cta;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks(), c = (int)cluster.block_rank();
+  const long long row = blockIdx.y;
   pdl_launch_dependents();
   pdl_wait_primary();  // the logits come from the preceding kernel
+  const long long c0 = (long long)c * chunk, c1 = min(cols, c0 + chunk);
   Best best{-INFINITY, (long long)cols};  // loses to every real entry
   if constexpr (F16) {
     const __half* x = static_cast<const __half*>(logits) + row * stride;
+    // chunk is a multiple of 8: each CTA's first vector starts on a 16-byte boundary when the row does
     const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0);
-    const long long nvec = vec ? cols / 8 : 0;
-    for (long long c = threadIdx.x; c < nvec; c += kArgmaxThreads) {
-      const uint4 u = reinterpret_cast<const uint4*>(x)[c];
+    const long long v0 = vec ? c0 / 8 : 0, v1 = vec ? c1 / 8 : 0;
+#pragma unroll 4
+    for (long long v = v0 + threadIdx.x; v < v1; v += kArgmaxThreads) {
+      const uint4 u = reinterpret_cast<const uint4*>(x)[v];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-        take(best, f.x, 8 * c + 2 * e);
-        take(best, f.y, 8 * c + 2 * e + 1);
+        take(best, f.x, 8 * v + 2 * e);
+        take(best, f.y, 8 * v + 2 * e + 1);
       }
     }
-    for (long long c = 8 * nvec + threadIdx.x; c < cols; c += kArgmaxThreads) take(best, __half2float(x[c]), c);
+    for (long long i = (vec ? max(c0, 8 * v1) : c0) + threadIdx.x; i < c1; i += kArgmaxThreads)
+      take(best, __half2float(x[i]), i);
   } else {
     const float* x = static_cast<const float*>(logits) + row * stride;
-    for (long long c = threadIdx.x; c < cols; c += kArgmaxThreads) take(best, x[c], c);
+#pragma unroll 4
+    for (long long i = c0 + threadIdx.x; i < c1; i += kArgmaxThreads) take(best, x[i], i);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -67,14 +84,24 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void*
   if (lane == 0) s_best[warp] = best;
   __syncthreads();
   if (warp == 0) {
-    best = s_best[lane];
+    best = lane < kArgmaxThreads / 32 ? s_best[lane] : Best{-INFINITY, (long long)cols};
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       Best other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
       if (better(other, best)) best = other;
     }
-    if (lane == 0) out[row * out_stride] = best.i;
+    if (lane == 0) s_cta = best;
   }
+  cluster.sync();
+  if (c == 0 && threadIdx.x == 0) {
+    Best win = s_cta;
+    for (int rk = 1; rk < S; ++rk) {
+      const Best other = *cluster.map_shared_rank(&s_cta, rk);
+      if (better(other, win)) win = other;
+    }
+    out[row * out_stride] = win.i;
+  }
+  cluster.sync();  // every CTA's candidate stays in place until the first CTA has read it
 }
 
 }  // namespace li4
@@ -91,22 +118,29 @@ extern "C" int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int6
     return set_error(LI4_ERR_ALIGNMENT, "argmax_rows: misaligned logits or output");
   if (rows == 0) return LI4_OK;
   if (rows > 65535) return set_error(LI4_ERR_UNSUPPORTED, "argmax_rows: rows=%lld above 65535", (long long)rows);
+  // columns per CTA of the row's cluster: a multiple of 8 (16-byte vectors), at least 8
+  const int S = kArgmaxCluster;
+  const long long chunk = std::max<long long>(8, ((cols + S - 1) / S + 7) / 8 * 8);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)rows, 1, 1);
+  cfg.gridDim = dim3((unsigned)S, (unsigned)rows, 1);
   cfg.blockDim = dim3(kArgmaxThreads, 1, 1);
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)S;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   long long* o = reinterpret_cast<long long*>(out);
   const int rc = dtype == LI4_F16
                      ? check_cuda(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<true>, logits, (long long)cols,
-                                                     (long long)stride, o, (long long)out_stride),
+                                                     (long long)stride, o, (long long)out_stride, chunk),
                                   "argmax_rows: kernel launch")
                      : check_cuda(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<false>, logits, (long long)cols,
-                                                     (long long)stride, o, (long long)out_stride),
+                                                     (long long)stride, o, (long long)out_stride, chunk),
                                   "argmax_rows: kernel launch");
   if (rc == LI4_OK) clear_error();
   return rc;
