@@ -51,6 +51,12 @@ __device__ __forceinline__ void load_lane_dims(const __half* p, float (&v)[DPL])
   }
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+
 struct AttnArgs {
   const __half* q;
   long long sqb;
@@ -65,14 +71,22 @@ struct AttnArgs {
   int chunk_max;  // keys per CTA at most: ceil(max_seq / cluster size)
 };
 
-template <int REP, int HD>
+// STAGE: the CTA's keys and values are first copied into shared memory with cp.async (all of
+// them in flight at once), the key rows with their 16-byte chunks XOR-swizzled by row so the
+// per-key reads of a warp spread over the banks.
+template <int REP, int HD, bool STAGE>
 __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __grid_constant__ AttnArgs a) {
   constexpr int DPL = HD / 32;  // dims per lane in P.V
+  constexpr int CPR = HD / 8;   // 16-byte chunks per cached row
+  constexpr int SWZ = (CPR < 8 ? CPR : 8) - 1;
   extern __shared__ __align__(16) float smem[];
   float* q_s = smem;                         // [REP][HD]
   float* red = q_s + REP * HD;               // [warps][REP][HD]
   float* part = red + kAttnWarps * REP * HD; // [REP][HD] this CTA's P.V over its keys
   float* scores = part + REP * HD;           // [REP][chunk_max]
+  // STAGE: [chunk_max][HD] keys (swizzled), then values, from the next 16-byte boundary (cp.async targets)
+  __half* k_s = reinterpret_cast<__half*>((reinterpret_cast<uintptr_t>(scores + REP * a.chunk_max) + 15) & ~uintptr_t(15));
+  __half* v_s = k_s + (size_t)a.chunk_max * HD;                         // STAGE: [chunk_max][HD]
   __shared__ float s_wmax[kAttnWarps][REP], s_wsum[kAttnWarps][REP];
   __shared__ float s_lmax[REP], s_lsum[REP], s_gmax[REP], s_gsum[REP];
 
@@ -92,8 +106,17 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * HD;
   const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * HD;
 
+  if (STAGE) {
+    for (int idx = tid; idx < (j1 - j0) * CPR; idx += kAttnThreads) {
+      const int jj = idx / CPR, cc = idx - jj * CPR;
+      cp_async16(k_s + jj * HD + ((cc ^ (jj & SWZ)) << 3), kbase + (long long)(j0 + jj) * a.css + cc * 8);
+      cp_async16(v_s + jj * HD + cc * 8, vbase + (long long)(j0 + jj) * a.css + cc * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   for (int t = tid; t < REP * HD; t += kAttnThreads)
     q_s[t] = __half2float(a.q[(long long)b * a.sqb + (long long)kvh * REP * HD + t]);
+  if (STAGE) asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
   // scores of this CTA's keys: one key per thread, REP dot products over HD dims
@@ -102,13 +125,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
 #pragma unroll
   for (int r = 0; r < REP; ++r) mx[r] = -INFINITY;
   for (int j = j0 + tid; j < j1; j += kAttnThreads) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kbase + (long long)j * a.css);
+    const uint4* kr = reinterpret_cast<const uint4*>(STAGE ? k_s + (j - j0) * HD : kbase + (long long)j * a.css);
     float dot[REP];
 #pragma unroll
     for (int r = 0; r < REP; ++r) dot[r] = 0.f;
 #pragma unroll
     for (int cc = 0; cc < HD / 8; ++cc) {
-      const uint4 kv = kr[cc];
+      const uint4 kv = kr[STAGE ? (cc ^ ((j - j0) & SWZ)) : cc];
       const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -201,7 +224,9 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
     float v4[4][DPL];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      load_lane_dims<DPL>(vbase + (long long)(j0 + j + u * kAttnWarps) * a.css + DPL * lane, v4[u]);
+      load_lane_dims<DPL>(STAGE ? v_s + (j + u * kAttnWarps) * HD + DPL * lane
+                                : vbase + (long long)(j0 + j + u * kAttnWarps) * a.css + DPL * lane,
+                          v4[u]);
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -213,7 +238,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   }
   for (; j < nloc; j += kAttnWarps) {
     float vv[DPL];
-    load_lane_dims<DPL>(vbase + (long long)(j0 + j) * a.css + DPL * lane, vv);
+    load_lane_dims<DPL>(STAGE ? v_s + j * HD + DPL * lane : vbase + (long long)(j0 + j) * a.css + DPL * lane, vv);
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       const float pj = scores[r * a.chunk_max + j];
@@ -243,9 +268,12 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   cluster.sync();  // every CTA's shared memory stays in place until the first CTA has read it
 }
 
-static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max) {
-  return sizeof(float) * ((size_t)rep * head_dim * (2 + kAttnWarps) + (size_t)rep * chunk_max);
+static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max, bool stage) {
+  return sizeof(float) * ((size_t)rep * head_dim * (2 + kAttnWarps) + (size_t)rep * chunk_max) +
+         (stage ? (size_t)2 * chunk_max * head_dim * sizeof(__half) + 16 : 0);
 }
+
+constexpr size_t kAttnStageLimit = 96 * 1024;  // K + V of a CTA's keys staged when they fit in this
 
 // CTAs per (KV head, sequence): a cluster of up to 8 when the (KV head, sequence)
 // pairs alone leave SMs idle, keeping >= 32 keys per CTA at max_seq.
@@ -255,9 +283,9 @@ static int attn_cluster_size(int64_t pairs, int64_t max_seq, int sm) {
   return S;
 }
 
-template <int REP, int HD>
+template <int REP, int HD, bool STAGE>
 static int launch_attention(const AttnArgs& a, int batch, int cluster, size_t smem, cudaStream_t stream) {
-  auto kernel = decode_attention_kernel<REP, HD>;
+  auto kernel = decode_attention_kernel<REP, HD, STAGE>;
   if (smem + 4096 > 48 * 1024) {  // dynamic + the static softmax partials past the 48 KiB default
     static std::mutex mu;
     static std::vector<std::pair<int, size_t>> raised;  // (device, bytes) of this instantiation
@@ -318,11 +346,12 @@ extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void
   if (max_seq > (1 << 20))
     return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld above 2^20", (long long)max_seq);
   int cluster = attn_cluster_size(batch * n_kv_heads, max_seq, current_sm_count());
-  while (cluster < 8 && attn_smem_bytes((int)rep, (int)head_dim, (int)((max_seq + cluster - 1) / cluster)) >
+  while (cluster < 8 && attn_smem_bytes((int)rep, (int)head_dim, (int)((max_seq + cluster - 1) / cluster), false) >
                             200 * 1024)
     cluster *= 2;
   const int chunk_max = (int)((max_seq + cluster - 1) / cluster);
-  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, chunk_max);
+  const bool stage = (size_t)2 * chunk_max * head_dim * sizeof(__half) <= kAttnStageLimit;
+  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, chunk_max, stage);
   if (smem > 200 * 1024)
     return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld needs %zu bytes of shared memory per CTA",
                      (long long)max_seq, smem);
@@ -344,8 +373,11 @@ extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void
   int rc;
   const int sel = (int)rep * 1000 + (int)head_dim;
   switch (sel) {
-#define LI4_ATTN_CASE(R, H) \
-  case R * 1000 + H: rc = launch_attention<R, H>(a, (int)batch, cluster, smem, s); break;
+#define LI4_ATTN_CASE(R, H)                                                                  \
+  case R * 1000 + H:                                                                           \
+    rc = stage ? launch_attention<R, H, true>(a, (int)batch, cluster, smem, s)                 \
+               : launch_attention<R, H, false>(a, (int)batch, cluster, smem, s);               \
+    break;
     LI4_ATTN_CASE(1, 32) LI4_ATTN_CASE(2, 32) LI4_ATTN_CASE(4, 32) LI4_ATTN_CASE(8, 32)
     LI4_ATTN_CASE(1, 64) LI4_ATTN_CASE(2, 64) LI4_ATTN_CASE(4, 64) LI4_ATTN_CASE(8, 64)
     LI4_ATTN_CASE(1, 128) LI4_ATTN_CASE(2, 128) LI4_ATTN_CASE(4, 128) LI4_ATTN_CASE(8, 128)
