@@ -215,10 +215,42 @@ int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, i
                     int64_t* out, int64_t out_stride, void* stream);
 
 /* Device-side error flags of the current device (bit 0: a bounded pipeline wait
- * inside a kernel ran out -- the kernel returned early and its outputs are not
+ * inside a GEMV kernel ran out; bit 1: a bounded wait for a peer's flag in
+ * li4_allreduce_add ran out -- the kernel carried on and its outputs are not
  * valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel all-reduce over NVLink peer memory (one GPU per process).
+ * Every rank allocates one communication buffer (li4_comm_alloc), exports it
+ * (li4_ipc_get_handle), exchanges the handles with the other ranks through the
+ * host, and maps the peers' buffers (li4_ipc_open_handle).  Each buffer holds
+ * two partial-sum slots and a flag array of ctas x world uint32, zeroed at
+ * allocation; each rank also keeps ctas uint32 call counts, zeroed.
+ * --------------------------------------------------------------------------- */
+#define LI4_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc + zero fill of a buffer that other processes can map. */
+int li4_comm_alloc(size_t bytes, void** dev_ptr);
+int li4_comm_free(void* dev_ptr);
+/* The IPC handle (LI4_IPC_HANDLE_BYTES bytes, host memory) of a li4_comm_alloc buffer. */
+int li4_ipc_get_handle(void* dev_ptr, void* handle);
+/* Map a peer's buffer from its handle (peer access enabled on first use). */
+int li4_ipc_open_handle(const void* handle, void** dev_ptr);
+int li4_ipc_close(void* dev_ptr);
+
+/* out[0..n) = fp16(residual + fp16(sum over ranks of slots[r][0..n))), the sum in
+ * fp32 in rank order; slots[r] is this call's slot (fp16, 16-byte aligned) in rank
+ * r's buffer, written by this rank's preceding kernel for r == rank.  flags[r]
+ * is rank r's flag array, counts this rank's call counts.  Every rank must make
+ * the same sequence of calls, alternating the two slots, with the same ctas.
+ * The kernel waits for all peers' flags (bounded); ranks run on separate GPUs.
+ * slots and flags are host arrays of device pointers (world entries, <= 8).
+ * Replaces: the NCCL all-reduce after each row-parallel linear and the residual
+ * add that follows it (llama/model.py:276-277, 358-362 under tensor parallelism). */
+int li4_allreduce_add(const void* const* slots, void* const* flags, void* counts, int ctas, int world, int rank,
+                      int64_t n, const void* residual, void* out, void* stream);
 
 /* w16[N, K] (fp16, row stride stride_wn elements) = dequantized weights,
  * bit-identical to the reference's fp32 (q - zero) * scale rounded to fp16.

@@ -1949,6 +1949,9 @@ extern "C" int li4_device_errors(unsigned* flags, int reset) {
     rc = li4::check_cuda(cudaMemcpyToSymbol(li4::g_li4_device_error, &zero, sizeof(unsigned)),
                          "device_errors: clearing the flags");
   }
+  unsigned comm = 0;
+  if (rc == LI4_OK) rc = li4::comm_device_errors(&comm, reset != 0);
+  if (rc == LI4_OK) *flags |= comm;
   if (rc == LI4_OK) li4::clear_error();
   return rc;
 }

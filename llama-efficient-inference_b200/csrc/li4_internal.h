@@ -17,6 +17,8 @@ void clear_error();
 int check_cuda(cudaError_t err, const char* what);
 // SM count of the current device (cached per device ordinal).
 int current_sm_count();
+// Device error word of the communication kernels (li4_comm.cu); reset clears it.
+int comm_device_errors(unsigned* flags, bool reset);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }

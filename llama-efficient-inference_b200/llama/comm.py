@@ -1,0 +1,88 @@
+"""Tensor-parallel all-reduce + residual add over NVLink peer memory (li4_allreduce_add).
+
+Replaces, for the decode step's small row-parallel outputs, the NCCL all-reduce
+after wo / w2 and the residual add that follows it (the reference's
+TransformerBlock.forward, llama/model.py:358-362, under tensor parallelism).
+Each rank allocates one buffer with the kernel library (two partial slots and
+a flag array), exports it with a CUDA IPC handle, gathers the other ranks'
+handles through the process group, and maps their buffers.  A row-parallel
+GEMV writes its fp16 partial straight into this rank's slot (`slot_ptr`), then
+`all_reduce_add` sums the slots of all ranks over NVLink and adds the residual
+in one launch.  Calls alternate the two slots; every rank must make the same
+sequence of calls.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _native as native
+
+_ALIGN = 256
+
+
+def _round_up(v: int, a: int = _ALIGN) -> int:
+    return (v + a - 1) // a * a
+
+
+class NvlinkAllReduce:
+    """One communication buffer per rank of `group`, mapped by every other rank."""
+
+    def __init__(self, group, max_elems: int, device: torch.device, ctas: int = 16):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 1 <= self.world <= 8:
+            raise ValueError(f"NvlinkAllReduce takes 1..8 ranks, got {self.world}")
+        self.device, self.ctas, self.max_elems = device, ctas, max_elems
+        lib = native.lib()
+        self.slot_bytes = _round_up(2 * max_elems)
+        total = 2 * self.slot_bytes + _round_up(4 * ctas * self.world)
+        with torch.cuda.device(device):
+            base = ctypes.c_void_p()
+            native.check(lib.li4_comm_alloc(total, ctypes.byref(base)), "comm_alloc")
+            self._own = base.value
+            handle = (ctypes.c_char * 64)()
+            native.check(lib.li4_ipc_get_handle(base, ctypes.cast(handle, ctypes.c_void_p)), "ipc_get_handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            bases, self._opened = [], []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                ptr = ctypes.c_void_p()
+                buf = (ctypes.c_char * 64).from_buffer_copy(h)
+                native.check(lib.li4_ipc_open_handle(ctypes.cast(buf, ctypes.c_void_p), ctypes.byref(ptr)),
+                             "ipc_open_handle")
+                bases.append(ptr.value)
+                self._opened.append(ptr.value)
+        arr = ctypes.c_void_p * self.world
+        self._slots = [arr(*[b + s * self.slot_bytes for b in bases]) for s in (0, 1)]
+        self._flags = arr(*[b + 2 * self.slot_bytes for b in bases])
+        self.counts = torch.zeros(ctas, dtype=torch.int32, device=device)
+
+    def slot_ptr(self, slot: int) -> int:
+        """Device address of this rank's partial slot `slot` (0 or 1), fp16, max_elems values."""
+        return self._own + slot * self.slot_bytes
+
+    def all_reduce_add(self, slot: int, residual: torch.Tensor, out: torch.Tensor) -> None:
+        """out = fp16(residual + sum over ranks of slot `slot`) on the current stream."""
+        n = residual.numel()
+        if n > self.max_elems or out.numel() != n or not (residual.is_contiguous() and out.is_contiguous()):
+            raise RuntimeError(f"all_reduce_add: {n} contiguous values (at most {self.max_elems})")
+        rc = native.lib().li4_allreduce_add(self._slots[slot], self._flags, self.counts.data_ptr(), self.ctas,
+                                           self.world, self.rank, n, residual.data_ptr(), out.data_ptr(),
+                                           native.stream_ptr(out.device))
+        native.check(rc, "allreduce_add")
+
+    def close(self) -> None:
+        lib = native.lib()
+        for p in self._opened:
+            lib.li4_ipc_close(p)
+        self._opened = []
+        if self._own:
+            lib.li4_comm_free(self._own)
+            self._own = None

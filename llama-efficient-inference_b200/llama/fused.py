@@ -16,8 +16,10 @@ adds.  Here a block is:
   5. w2 GEMV    h = h1 + w2(ffn)                                (residual epilogue)
 
 and the step ends with lm_head with the final RMSNorm fused into its staging.
-Under tensor parallelism the wo / w2 outputs are partial sums: they are stored
-plain, all-reduced, and added to the residual by torch.
+Under tensor parallelism the wo / w2 outputs are partial sums: each rank's GEMV
+writes its partial into a buffer every rank has mapped, and one kernel sums the
+ranks' partials over NVLink and adds the residual (llama.comm; NCCL plus a torch
+add with nvlink_allreduce=False).
 
 The fused epilogues pair two GEMV outputs in one thread.  They take weights
 whose rows are rearranged once, at construction (pair_permutation,
@@ -73,18 +75,22 @@ def _ptr(t: Optional[torch.Tensor]):
 
 
 def int4_linear_fused(x: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, zp: torch.Tensor,
-                      y: Optional[torch.Tensor], fusion: native.Fusion, group_size: int = 128) -> None:
-    """One li4_int4_linear_fused launch on the current stream: x [M, K] fp16 (row-contiguous)."""
+                      y: Optional[torch.Tensor], fusion: native.Fusion, group_size: int = 128,
+                      y_ptr: Optional[int] = None, y_stride: int = 0) -> None:
+    """One li4_int4_linear_fused launch on the current stream: x [M, K] fp16 (row-contiguous).
+    y_ptr / y_stride give the output as a raw device address instead of a tensor (a communication slot)."""
     M, K = x.shape
     N = packed.shape[0]
     lib = native.lib()
     dev = x.device
     nbytes = lib.li4_int4_linear_workspace_bytes(M, N, K, group_size, 0)
     ws = native.workspace(dev, nbytes) if nbytes else None
-    rc = lib.li4_int4_linear_fused(x.data_ptr(), packed.data_ptr(), scale.data_ptr(), zp.data_ptr(), _ptr(y),
-                                   M, N, K, group_size, x.stride(0), packed.stride(0), scale.stride(0),
-                                   y.stride(0) if y is not None else 0, ctypes.byref(fusion),
-                                   _ptr(ws), ws.numel() if ws is not None else 0, native.stream_ptr(dev))
+    if y_ptr is None:
+        y_ptr, y_stride = _ptr(y), (y.stride(0) if y is not None else 0)
+    rc = lib.li4_int4_linear_fused(x.data_ptr(), packed.data_ptr(), scale.data_ptr(), zp.data_ptr(), y_ptr,
+                                   M, N, K, group_size, x.stride(0), packed.stride(0), scale.stride(0), y_stride,
+                                   ctypes.byref(fusion), _ptr(ws), ws.numel() if ws is not None else 0,
+                                   native.stream_ptr(dev))
     native.check(rc, "int4_linear_fused")
 
 
@@ -146,8 +152,10 @@ class FusedDecoder:
     step serves every position.
     """
 
-    def __init__(self, model):
+    def __init__(self, model, nvlink_allreduce: bool = True):
         self.model = model
+        self.nvlink_allreduce = nvlink_allreduce
+        self._ar = None  # NvlinkAllReduce of the model's TP group, built on first use
         p = model.params
         emb = model.tok_embeddings.weight
         self.device = emb.device
@@ -187,6 +195,24 @@ class FusedDecoder:
         dist.all_reduce(part, group=group)
         torch.add(residual, part, out=out)
 
+    def _row_parallel(self, x: torch.Tensor, w, residual: torch.Tensor, out: torch.Tensor, part: torch.Tensor,
+                      group, slot: int) -> None:
+        """out = residual + allreduce(x @ w^T) for a row-parallel INT4 linear: the partial goes straight
+        into this rank's NVLink communication slot and one kernel sums the ranks' slots (or NCCL)."""
+        E = native
+        if self.nvlink_allreduce:
+            if self._ar is None:
+                from .comm import NvlinkAllReduce
+
+                self._ar = NvlinkAllReduce(group, max_elems=self.model.params.max_batch_size * self.dim,
+                                           device=self.device)
+            int4_linear_fused(x, *w, None, E.Fusion(epilogue=E.LI4_EPI_STORE),
+                              y_ptr=self._ar.slot_ptr(slot), y_stride=out.stride(0))
+            self._ar.all_reduce_add(slot, residual, out)
+        else:
+            int4_linear_fused(x, *w, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
+            self._allreduce_add(part, residual, out, group)
+
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor,
                     next_tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -212,16 +238,14 @@ class FusedDecoder:
                 f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h.data_ptr(), stride_rm=h.stride(0))
                 int4_linear_fused(attn, *blk.wo, h1, f)
             else:
-                int4_linear_fused(attn, *blk.wo, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
-                self._allreduce_add(part, h, h1, att.tp_group)
+                self._row_parallel(attn, blk.wo, h, h1, part, att.tp_group, slot=0)
             f = E.Fusion(norm_weight=blk.ffn_norm.data_ptr(), norm_eps=blk.ffn_eps, epilogue=E.LI4_EPI_SWIGLU)
             int4_linear_fused(h1, *blk.gate_up, ffn, f)
             if blk.ff.tp_group is None:
                 f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h1.data_ptr(), stride_rm=h1.stride(0))
                 int4_linear_fused(ffn, *blk.w2, h, f)
             else:
-                int4_linear_fused(ffn, *blk.w2, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
-                self._allreduce_add(part, h1, h, blk.ff.tp_group)
+                self._row_parallel(ffn, blk.w2, h1, h, part, blk.ff.tp_group, slot=1)
         logits = buf["logits"]
         f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE)
         int4_linear_fused(h, *self.out, logits, f)

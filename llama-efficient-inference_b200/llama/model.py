@@ -316,13 +316,14 @@ class Llama(Generation):
         h = self.norm(h)
         return self._logits(h)
 
-    def enable_fused_decode(self, enabled: bool = True):
+    def enable_fused_decode(self, enabled: bool = True, nvlink_allreduce: bool = True):
         """Run decode_step as the fused INT4 kernels of llama.fused (five launches per block).
-        Needs a quantized fp16 model on a CUDA device; shares this model's KV caches."""
+        Needs a quantized fp16 model on a CUDA device; shares this model's KV caches.  Under tensor
+        parallelism the row-parallel sums go over NVLink peer memory (llama.comm), or NCCL."""
         if enabled:
             from .fused import FusedDecoder
 
-            self._fused = FusedDecoder(self)
+            self._fused = FusedDecoder(self, nvlink_allreduce=nvlink_allreduce)
         else:
             self._fused = None
         return self

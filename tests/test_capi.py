@@ -82,12 +82,12 @@ def test_rejects_unaligned_packed(native):
 
 
 def test_rejects_missing_workspace(native):
-    # N=512, K=2048 on 148 SMs needs split-K (32 row tiles of 16 rows)
+    # down_proj (N=2048, K=8192) at M=1 on 148 SMs: 128 row tiles, so the dispatcher splits K in two
     lib = native.lib()
-    need = lib.li4_int4_linear_workspace_bytes(1, 512, 2048, 128, 148)
+    need = lib.li4_int4_linear_workspace_bytes(1, 2048, 8192, 128, 148)
     assert need > 0
     assert lib.li4_int4_linear_workspace_bytes(1, 128256, 2048, 128, 148) == 0  # enough row tiles, no split
-    rc = call_linear(native, M=1, N=512, K=2048)
+    rc = call_linear(native, M=1, N=2048, K=8192)
     # the SM count of a machine without a GPU falls back to 148, so split-K is chosen
     assert rc == native.LI4_ERR_WORKSPACE
 

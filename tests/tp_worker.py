@@ -5,6 +5,7 @@ modes:
              logits with the unsharded model on every rank; prints one JSON line
   dead_peer  rank 1 leaves right after joining; rank 0's next collective must fail
              with an error (not hang); prints one JSON line from rank 0
+  gpu_parity / gpu_allreduce  the NCCL-backed GPU checks of tests/test_tp_gpu.py
 """
 import datetime
 import json
@@ -104,6 +105,68 @@ def gpu_parity():
                       "graph_tokens_equal": same_graph, "fused_graph_tokens_equal": same_fused}), flush=True)
 
 
+def gpu_allreduce():
+    """li4_allreduce_add over NVLink peer memory against NCCL: each rank's INT4 GEMV writes its
+    partial into its communication slot; sum over ranks + residual, eager and replayed in a graph."""
+    from llama import _native, fused
+    from llama.comm import NvlinkAllReduce
+    from llama.quantize import QuantizedLinear
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", rank)
+    M, N, K = 16, 2048, 1024  # a row-parallel down_proj shard at batch 16
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+    p, s, z = QuantizedLinear.quantize_tensor(w, 128)
+    ar = NvlinkAllReduce(dist.group.WORLD, max_elems=M * N, device=dev)
+    xs = [torch.randn(M, K, generator=gen, device=dev).half() for _ in range(4)]
+    res = torch.randn(M, N, generator=torch.Generator(device=dev).manual_seed(7), device=dev).half()
+    outs = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(4)]
+    E = _native
+
+    def run():
+        for i, x in enumerate(xs):  # alternate the two slots as the decode step does
+            fused.int4_linear_fused(x, p, s, z, None, E.Fusion(epilogue=E.LI4_EPI_STORE),
+                                    y_ptr=ar.slot_ptr(i % 2), y_stride=N)
+            ar.all_reduce_add(i % 2, res, outs[i])
+
+    worst = 0.0
+    with torch.no_grad():
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize(dev)
+        refs = []
+        for x in xs:
+            part = torch.empty(M, N, dtype=torch.float16, device=dev)
+            fused.int4_linear_fused(x, p, s, z, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
+            tot = part.float()
+            dist.all_reduce(tot)
+            refs.append((res.float() + tot.half().float()).half())
+        for o, r in zip(outs, refs):
+            worst = max(worst, float((o.float() - r.float()).abs().max() / r.float().abs().max()))
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            run()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g):
+            run()
+        for o in outs:
+            o.zero_()
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        for o, r in zip(outs, refs):
+            worst = max(worst, float((o.float() - r.float()).abs().max() / r.float().abs().max()))
+        del g
+    errors = _native.device_errors()
+    dist.barrier()
+    ar.close()
+    print(json.dumps({"rank": rank, "world": world, "max_rel_err": worst, "device_errors": errors}), flush=True)
+
+
 def dead_peer():
     rank = dist.get_rank()
     if rank == 1:
@@ -122,14 +185,14 @@ def dead_peer():
 if __name__ == "__main__":
     mode = sys.argv[1]
     timeout = datetime.timedelta(seconds=float(os.environ.get("TP_TEST_TIMEOUT", "60")))
-    if mode == "gpu_parity":
+    if mode in ("gpu_parity", "gpu_allreduce"):
         torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
         dist.init_process_group("nccl", timeout=timeout,
                                 device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
     else:
         dist.init_process_group("gloo", timeout=timeout)
-    {"parity": parity, "dead_peer": dead_peer, "gpu_parity": gpu_parity}[mode]()
-    if mode in ("parity", "gpu_parity"):
+    {"parity": parity, "dead_peer": dead_peer, "gpu_parity": gpu_parity, "gpu_allreduce": gpu_allreduce}[mode]()
+    if mode in ("parity", "gpu_parity", "gpu_allreduce"):
         dist.barrier()
         dist.destroy_process_group()
     os._exit(0)
