@@ -402,7 +402,7 @@ def profile_shape(a):
     from llama.int4_gemv import int4_linear_out
     from llama.quantize import QuantizedLinear
 
-    shapes = {n: (N, K) for n, N, K in LAYER_SHAPES + [LM_HEAD]}
+    shapes = {n: (N, K) for n, N, K in LAYER_SHAPES + SWEEP_SHAPES + [LM_HEAD]}
     N, K = shapes[a.profile_shape]
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(0)
@@ -726,7 +726,8 @@ def main():
     ap.add_argument("--decode-reps", type=int, default=3)
     ap.add_argument("--decode-unfused", action="store_true",
                     help="also time the module-by-module decode step (ATen ops around the INT4 GEMVs)")
-    ap.add_argument("--profile-shape", default=None, choices=[n for n, _, _ in LAYER_SHAPES] + [LM_HEAD[0]],
+    ap.add_argument("--profile-shape", default=None,
+                    choices=[n for n, _, _ in LAYER_SHAPES] + [LM_HEAD[0], "qkv_fused", "gate_up_fused"],
                     help="only run --launches launches of one shape (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--only-decode", action="store_true",
