@@ -3,10 +3,10 @@
 // A cluster of 1..8 CTAs per (KV head, sequence) splits the cached keys and
 // values between its CTAs, and reads them once for all `REP` query heads that
 // share them (grouped-query attention without the reference's repeat_kv
-// copies, llama/model.py:155-164, 265-266).  The CTAs exchange the softmax max
-// and sum and their partial P.V through distributed shared memory, so the
-// probabilities are normalised by the global sum before their fp16 rounding,
-// as in the reference.
+// copies, llama/model.py:155-164, 265-266).  The CTAs push their softmax max
+// and sum, and then their partial P.V, into each other's shared memory (two
+// cluster barriers), so the probabilities are normalised by the global sum
+// before their fp16 rounding, as in the reference.
 // The arithmetic follows the reference's fp16 decode step
 // (llama/model.py:266-275):
 //   s = fp16(q . k)             fp16 matmul, fp32 accumulation
@@ -82,19 +82,23 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   extern __shared__ __align__(16) float smem[];
   float* q_s = smem;                         // [REP][HD]
   float* red = q_s + REP * HD;               // [warps][REP][HD]
-  float* part = red + kAttnWarps * REP * HD; // [REP][HD] this CTA's P.V over its keys
-  float* scores = part + REP * HD;           // [REP][chunk_max]
+  float* part = red + kAttnWarps * REP * HD; // [cluster][REP][HD] partial P.V (collected in the first CTA)
+  float* scores = part + 8 * REP * HD;       // [REP][chunk_max]
   // STAGE: [chunk_max][HD] keys (swizzled), then values, from the next 16-byte boundary (cp.async targets)
   __half* k_s = reinterpret_cast<__half*>((reinterpret_cast<uintptr_t>(scores + REP * a.chunk_max) + 15) & ~uintptr_t(15));
   __half* v_s = k_s + (size_t)a.chunk_max * HD;                         // STAGE: [chunk_max][HD]
   __shared__ float s_wmax[kAttnWarps][REP], s_wsum[kAttnWarps][REP];
-  __shared__ float s_lmax[REP], s_lsum[REP], s_gmax[REP], s_gsum[REP];
+  __shared__ float s_lmax[REP], s_gmax[REP], s_gsum[REP];
+  __shared__ float s_cm[8][REP], s_cl[8][REP];  // (max, sum) of every CTA of the cluster, pushed by each
 
   cg::cluster_group cluster = cg::this_cluster();
   const int S = (int)cluster.num_blocks();   // CTAs sharing this (KV head, sequence)
   const int c = (int)cluster.block_rank();
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Every CTA of the cluster must have started before a peer writes into its shared memory:
+  // arrive now, wait just before the first remote store (by then the barrier is long complete).
+  cluster.barrier_arrive();
   pdl_launch_dependents();
   pdl_wait_primary();  // q and the cache row of this step come from the preceding kernel
 
@@ -151,7 +155,9 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
       mx[r] = fmaxf(mx[r], sc);
     }
   }
-  // softmax over all L keys of the cluster, fp32: max and sum exchanged through distributed shared memory
+  // softmax over all L keys of the cluster, fp32.  Each CTA reduces its keys to (max m_c, sum of
+  // exp(s - m_c)) and pushes both into every CTA's shared memory; after one cluster barrier every
+  // CTA has the global max M and sum L = sum_c l_c exp(m_c - M), and rounds p = exp(s - M) / L.
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
     float v = mx[r];
@@ -166,23 +172,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
     for (int w = 1; w < kAttnWarps; ++w) v = fmaxf(v, s_wmax[w][tid]);
     s_lmax[tid] = v;
   }
-  cluster.sync();
-  if (tid < REP) {
-    float v = -INFINITY;
-    for (int rk = 0; rk < S; ++rk) v = fmaxf(v, *cluster.map_shared_rank(&s_lmax[tid], rk));
-    s_gmax[tid] = v;
-  }
   __syncthreads();
   float sum[REP];
 #pragma unroll
   for (int r = 0; r < REP; ++r) sum[r] = 0.f;
   for (int j = tid; j < j1 - j0; j += kAttnThreads) {
 #pragma unroll
-    for (int r = 0; r < REP; ++r) {
-      const float e = expf(scores[r * a.chunk_max + j] - s_gmax[r]);
-      scores[r * a.chunk_max + j] = e;
-      sum[r] += e;
-    }
+    for (int r = 0; r < REP; ++r) sum[r] += expf(scores[r * a.chunk_max + j] - s_lmax[r]);
   }
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
@@ -192,23 +188,33 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
     if (lane == 0) s_wsum[warp][r] = v;
   }
   __syncthreads();
+  cluster.barrier_wait();
   if (tid < REP) {
     float v = 0.f;
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) v += s_wsum[w][tid];
-    s_lsum[tid] = v;
+    const float m = s_lmax[tid];
+    for (int rk = 0; rk < S; ++rk) {  // push (m_c, l_c) into every CTA of the cluster
+      *cluster.map_shared_rank(&s_cm[c][tid], rk) = m;
+      *cluster.map_shared_rank(&s_cl[c][tid], rk) = v;
+    }
   }
   cluster.sync();
   if (tid < REP) {
-    float v = 0.f;
-    for (int rk = 0; rk < S; ++rk) v += *cluster.map_shared_rank(&s_lsum[tid], rk);
-    s_gsum[tid] = v;
+    float M = -INFINITY;
+    for (int rk = 0; rk < S; ++rk) M = fmaxf(M, s_cm[rk][tid]);
+    float Lsum = 0.f;
+    for (int rk = 0; rk < S; ++rk)
+      if (s_cm[rk][tid] != -INFINITY) Lsum += s_cl[rk][tid] * expf(s_cm[rk][tid] - M);
+    s_gmax[tid] = M;
+    s_gsum[tid] = Lsum;
   }
   __syncthreads();
   for (int j = tid; j < j1 - j0; j += kAttnThreads) {
 #pragma unroll
     for (int r = 0; r < REP; ++r)
-      scores[r * a.chunk_max + j] = __half2float(__float2half_rn(scores[r * a.chunk_max + j] / s_gsum[r]));
+      scores[r * a.chunk_max + j] =
+          __half2float(__float2half_rn(expf(scores[r * a.chunk_max + j] - s_gmax[r]) / s_gsum[r]));
   }
   __syncthreads();
 
@@ -251,25 +257,25 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
 #pragma unroll
     for (int e = 0; e < DPL; ++e) red[(warp * REP + r) * HD + DPL * lane + e] = acc[r][e];
   __syncthreads();
+  float* part0 = cluster.map_shared_rank(part, 0);  // the first CTA collects [S][REP * HD] partials
   for (int t = tid; t < REP * HD; t += kAttnThreads) {
     float v = 0.f;
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) v += red[w * REP * HD + t];
-    part[t] = v;
+    part0[c * REP * HD + t] = v;
   }
-  cluster.sync();
-  if (c == 0) {  // the cluster's first CTA sums the partial P.V of all its CTAs (rank order)
+  cluster.sync();  // the last cluster barrier: after it only the first CTA reads shared memory, its own
+  if (c == 0) {
     for (int t = tid; t < REP * HD; t += kAttnThreads) {
       float v = 0.f;
-      for (int rk = 0; rk < S; ++rk) v += *cluster.map_shared_rank(&part[t], rk);
+      for (int rk = 0; rk < S; ++rk) v += part[rk * REP * HD + t];
       a.out[(long long)b * a.sob + (long long)kvh * REP * HD + t] = __float2half_rn(v);
     }
   }
-  cluster.sync();  // every CTA's shared memory stays in place until the first CTA has read it
 }
 
 static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max, bool stage) {
-  return sizeof(float) * ((size_t)rep * head_dim * (2 + kAttnWarps) + (size_t)rep * chunk_max) +
+  return sizeof(float) * ((size_t)rep * head_dim * (1 + kAttnWarps + 8) + (size_t)rep * chunk_max) +
          (stage ? (size_t)2 * chunk_max * head_dim * sizeof(__half) + 16 : 0);
 }
 
