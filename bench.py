@@ -397,6 +397,42 @@ def kernel_sweep(a):
         print(json.dumps({"best": shape, "M": M, **{k: r[k] for k in ("kernel", "rows", "split", "us", "GBps")}}))
 
 
+def size_floor(a):
+    """--size-floor: the time a plain HBM read of each decode-GEMV byte count takes as one launch among
+    back-to-back launches (torch's sum of fp16 buffers in a CUDA graph over rotating copies > 3x L2):
+    the per-launch floor a GEMV of that size competes with, beside the 6550 GB/s of a long copy."""
+    dev = torch.device("cuda", 0)
+    sizes = [("k_proj", gemv_bytes(512, 2048, 0)), ("q_proj", gemv_bytes(2048, 2048, 0)),
+             ("gate_proj", gemv_bytes(8192, 2048, 0)), ("gate_up_fused", gemv_bytes(16384, 2048, 0)),
+             ("lm_head", gemv_bytes(128256, 2048, 0))]
+    for name, nbytes in sizes:
+        copies = max(2, (3 * L2_BYTES) // nbytes + 1)
+        bufs = [torch.ones(nbytes // 2, dtype=torch.float16, device=dev) for _ in range(copies)]
+        out = torch.empty((), dtype=torch.float32, device=dev)
+
+        def run():
+            for b in bufs:
+                torch.sum(b, dtype=torch.float32, out=out)
+
+        run()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run()
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ts.append(e0.elapsed_time(e1) / copies)
+        us = statistics.median(ts) * 1e3
+        print(json.dumps({"size_floor": name, "bytes": nbytes, "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}))
+        del g, bufs
+        torch.cuda.empty_cache()
+
+
 def profile_shape(a):
     """--profile-shape NAME: `--launches` eager launches of one shape (a small case for ncu captures)."""
     from llama.int4_gemv import int4_linear_out
@@ -733,6 +769,8 @@ def main():
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
     ap.add_argument("--sweep", action="store_true", help="kernel-family x launch-shape sweep of the decode shapes")
+    ap.add_argument("--size-floor", action="store_true",
+                    help="time a plain HBM read of each decode-GEMV byte count as back-to-back launches")
     ap.add_argument("--sweep-m", default="1,8,16")
     ap.add_argument("--sweep-kernels", default="0,1,2,3,4,5", help="0 auto, 1 cuda_core, 2 mma, 3 stream, 4 tile, 5 bulk")
     a = ap.parse_args()
@@ -741,6 +779,9 @@ def main():
         return
     if a.sweep:
         kernel_sweep(a)
+        return
+    if a.size_floor:
+        size_floor(a)
         return
     if a.warmup < 3:
         a.warmup = 3
