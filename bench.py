@@ -408,11 +408,11 @@ def size_floor(a):
     for name, nbytes in sizes:
         copies = max(2, (3 * L2_BYTES) // nbytes + 1)
         bufs = [torch.ones(nbytes // 2, dtype=torch.float16, device=dev) for _ in range(copies)]
-        out = torch.empty((), dtype=torch.float32, device=dev)
+        out = torch.empty(1, dtype=torch.float32, device=dev)
 
         def run():
             for b in bufs:
-                torch.sum(b, dtype=torch.float32, out=out)
+                torch.sum(b.view(1, -1), dim=1, dtype=torch.float32, out=out)
 
         run()
         torch.cuda.synchronize(dev)
