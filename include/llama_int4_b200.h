@@ -152,8 +152,10 @@ typedef enum li4_epilogue_kind {
   LI4_EPI_STORE = 0,     /* y = fp16(x W^T)                                          */
   LI4_EPI_RESIDUAL = 1,  /* y = fp16(residual + fp16(x W^T))                         */
   LI4_EPI_SWIGLU = 2,    /* y = fp16(fp16(silu(g)) * u), g, u = fp16 outputs of pair  */
-  LI4_EPI_QKV_ROPE = 3   /* RoPE on q, k pairs at position *pos; q -> q_out,
+  LI4_EPI_QKV_ROPE = 3,  /* RoPE on q, k pairs at position *pos; q -> q_out,
                             k and v -> cache_k / cache_v at row *pos (y unused)       */
+  LI4_EPI_STORE_F32 = 4  /* y is fp32 [M, N] (row stride in fp32 elements):
+                            y = (float)fp16(x W^T), the reference's output(h).float() */
 } li4_epilogue_kind;
 
 typedef struct li4_fusion {

@@ -82,11 +82,17 @@ struct GemvArgs {
 // reference's fp16 Linear output is, and each later fp16 intermediate of the
 // reference is rounded again at the same point.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ bool epi_paired(const GemvArgs& a) { return a.epi >= LI4_EPI_SWIGLU; }
+__device__ __forceinline__ bool epi_paired(const GemvArgs& a) {
+  return a.epi == LI4_EPI_SWIGLU || a.epi == LI4_EPI_QKV_ROPE;
+}
 
 // One output y[m, row] (LI4_EPI_STORE / LI4_EPI_RESIDUAL).
 __device__ __noinline__ void emit_one(const GemvArgs& a, int m, int row, float v) {
   __half h = __float2half_rn(v);
+  if (a.epi == LI4_EPI_STORE_F32) {  // fp16 Linear output widened: logits = output(h).float() (llama/model.py:455)
+    reinterpret_cast<float*>(a.y)[(long long)m * a.sym + row] = __half2float(h);
+    return;
+  }
   if (a.epi == LI4_EPI_RESIDUAL)  // h = x + wo(...): fp16 + fp16 (llama/model.py:358-362)
     h = __float2half_rn(__half2float(h) + __half2float(a.res[(long long)m * a.srm + row]));
   a.y[(long long)m * a.sym + row] = h;
@@ -1778,6 +1784,7 @@ static int check_fusion(const li4_fusion& f, int64_t M, int64_t N, int64_t K) {
   }
   switch (f.epilogue) {
     case LI4_EPI_STORE:
+    case LI4_EPI_STORE_F32:
       return LI4_OK;
     case LI4_EPI_RESIDUAL:
       if (!f.residual || f.stride_rm < N || (reinterpret_cast<uintptr_t>(f.residual) & 1u))
@@ -1842,6 +1849,8 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(scale) |
        reinterpret_cast<uintptr_t>(zero)) & 1u)
     return set_error(LI4_ERR_ALIGNMENT, "int4_linear: fp16 tensors must be 2-byte aligned");
+  if (epi == LI4_EPI_STORE_F32 && (reinterpret_cast<uintptr_t>(y) & 3u))
+    return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: an fp32 output must be 4-byte aligned");
   if (p.kernel == LI4_KERNEL_TILE && ((N - 1) * spn + K / 2 > (int64_t)UINT32_MAX ||
                                       (N - 1) * ssn + K / group > (int64_t)UINT32_MAX)) {
     // the tile kernel addresses rows with 32-bit offsets

@@ -31,7 +31,7 @@ _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
 _INT = ctypes.c_int
 
-LI4_EPI_STORE, LI4_EPI_RESIDUAL, LI4_EPI_SWIGLU, LI4_EPI_QKV_ROPE = 0, 1, 2, 3
+LI4_EPI_STORE, LI4_EPI_RESIDUAL, LI4_EPI_SWIGLU, LI4_EPI_QKV_ROPE, LI4_EPI_STORE_F32 = 0, 1, 2, 3, 4
 
 
 class Fusion(ctypes.Structure):

@@ -185,7 +185,7 @@ class FusedDecoder:
                  "q": torch.empty(bs, self.n_heads * self.head_dim, **f16),
                  "attn": torch.empty(bs, self.n_heads * self.head_dim, **f16),
                  "ffn": torch.empty(bs, self.ffn, **f16), "part": torch.empty(bs, self.dim, **f16),
-                 "logits": torch.empty(bs, self.vocab_local, **f16)}
+                 "logits": torch.empty(bs, self.vocab_local, dtype=torch.float32, device=self.device)}
             self._bufs[bs] = b
         return b
 
@@ -246,9 +246,9 @@ class FusedDecoder:
                 int4_linear_fused(ffn, *blk.w2, h, f)
             else:
                 self._row_parallel(ffn, blk.w2, h1, h, part, blk.ff.tp_group, slot=1)
-        logits = buf["logits"]
-        f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE)
-        int4_linear_fused(h, *self.out, logits, f)
+        logits = buf["logits"]  # fp32: the lm_head writes its fp16 outputs widened (output(h).float())
+        f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE_F32)
+        int4_linear_fused(h, *self.out, None, f, y_ptr=logits.data_ptr(), y_stride=logits.stride(0))
         if self.model.tp_group is not None:
             import torch.distributed as dist
 
@@ -257,4 +257,4 @@ class FusedDecoder:
             logits = torch.cat(parts, dim=-1)
         if next_tokens is not None:
             argmax_rows(logits, next_tokens.view(bs, 1))
-        return logits.float().view(bs, 1, -1)
+        return logits.view(bs, 1, -1)

@@ -326,3 +326,18 @@ def test_decode_attention_cluster_shapes(B, max_seq, pos, fz, cuda_device):
     pos_t = torch.tensor([pos], dtype=torch.long, device=cuda_device)
     fused.decode_attention(q, ck, cv, pos_t, out, n_heads, n_kv_heads)
     close(out, attention_ref(q, ck, cv, pos, n_heads, n_kv_heads, head_dim), what="attention")
+
+
+@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("N,K", [(128256, 2048), (1000, 256), (2048, 8192)])
+def test_store_f32_epilogue(M, N, K, fz, cuda_device):
+    """fp32 output of the fp16-rounded GEMV (the lm_head's output(h).float()), with the final RMSNorm."""
+    fused, nat = fz
+    p, s, z, w16 = quantized(N, K, cuda_device, N + 3 * K)
+    x = randn((M, K), cuda_device, 5 + M, 2.0)
+    nw = (1 + 0.1 * randn((K,), cuda_device, 6).float()).half()
+    y = torch.empty(M, N, dtype=torch.float32, device=cuda_device)
+    f = nat.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5, epilogue=nat.LI4_EPI_STORE_F32)
+    fused.int4_linear_fused(x, p, s, z, None, f, y_ptr=y.data_ptr(), y_stride=y.stride(0))
+    assert torch.equal(y, y.half().float()), "fp32 outputs are not widened fp16 values"
+    close(y, F.linear(rmsnorm_ref(x, nw, 1e-5), w16).float(), what="store_f32")
