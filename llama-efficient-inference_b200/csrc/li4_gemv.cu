@@ -294,83 +294,6 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int
   }
 }
 
-// stage_x with the RMSNorm prologue, for a CTA whose K range is the whole row (ks0 == 0,
-// nks * 128 == K): the sum of squares comes from the x values being staged, so x is read from
-// global memory once.  Pass 1 stages raw x and leaves one partial sum per 16-chunk group (the 16
-// lanes that share a row) in s_part; threads < M turn them into s_rstd; pass 2 normalises the
-// staged chunks in place with the weight permuted the same way.  `sync` is the caller's barrier
-// over its THREADS threads.
-template <int NT, int THREADS, typename Sync>
-__device__ __forceinline__ void stage_x_norm(const GemvArgs& a, int nks, int M8, uint8_t* xs, float* s_part,
-                                             float* s_rstd, Sync sync) {
-  const int total = nks * NT * M8 * 16;
-  const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
-  // the loop bound is uniform over the block so that every lane reaches the shuffles
-  for (int base = 0; base < total; base += THREADS) {
-    const int idx = base + threadIdx.x;
-    const bool live = idx < total;
-    const int w = idx & 3, block = idx >> 2, quad = block & 3, t = block >> 2;
-    const int m8 = t % M8, nt = (t / M8) % NT, ks = t / (M8 * NT);
-    const int m = nt * 8 + m8;
-    uint4 out = make_uint4(0u, 0u, 0u, 0u);
-    float ss = 0.f;
-    if (live && m < a.M) {
-      const long long k = (long long)ks * 128 + 32 * quad + 8 * w;
-      const __half* src = a.x + (long long)m * a.sxm + k;
-      uint32_t u[4];
-      if (vec_ok) {
-        const uint4 v = *reinterpret_cast<const uint4*>(src);
-        u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
-        ss = fmaf(f.x, f.x, ss);
-        ss = fmaf(f.y, f.y, ss);
-      }
-      out.x = __byte_perm(u[0], u[2], 0x5410);
-      out.y = __byte_perm(u[0], u[2], 0x7632);
-      out.z = __byte_perm(u[1], u[3], 0x5410);
-      out.w = __byte_perm(u[1], u[3], 0x7632);
-    }
-    // the 16 lanes of a half warp hold the 16 chunks of one (kstep, row) group
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (live) {
-      if ((idx & 15) == 0) s_part[t] = ss;
-      *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8)) = out;
-    }
-  }
-  sync();
-  if (threadIdx.x < a.M) {
-    const int m = threadIdx.x, nt = m >> 3, m8 = m & 7;
-    float tot = 0.f;
-    for (int ks = 0; ks < nks; ++ks) tot += s_part[(ks * NT + nt) * M8 + m8];
-    s_rstd[m] = rsqrtf(tot / (float)a.K + a.norm_eps);
-  }
-  sync();
-  for (int idx = threadIdx.x; idx < total; idx += THREADS) {
-    const int w = idx & 3, block = idx >> 2, quad = block & 3, t = block >> 2;
-    const int m8 = t % M8, nt = (t / M8) % NT, ks = t / (M8 * NT);
-    const int m = nt * 8 + m8;
-    if (m >= a.M) continue;
-    uint4* dst = reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8));
-    const uint4 xv = *dst;
-    const uint4 wr = *reinterpret_cast<const uint4*>(a.norm_w + (long long)ks * 128 + 32 * quad + 8 * w);
-    const float r = s_rstd[m];
-    uint4 o;
-    o.x = norm_pair(xv.x, __byte_perm(wr.x, wr.z, 0x5410), r);
-    o.y = norm_pair(xv.y, __byte_perm(wr.x, wr.z, 0x7632), r);
-    o.z = norm_pair(xv.z, __byte_perm(wr.y, wr.w, 0x5410), r);
-    o.w = norm_pair(xv.w, __byte_perm(wr.y, wr.w, 0x7632), r);
-    *dst = o;
-  }
-}
-
 // Start pulling the first row tile's weight bytes into L2 (TMA bulk prefetch)
 // before waiting on the preceding kernel.
 template <int ROWS>
@@ -886,16 +809,11 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
   }
   pdl_wait_primary();  // x is written by the preceding kernel
   __shared__ float s_rstd[LI4_MAX_M];
-  __shared__ float s_part[kMaxKsPerCta * 16];  // stage_x_norm: per (kstep, row) partial sums of squares
-  if (FUSED && a.norm_w != nullptr && ks0 == 0 && nks * 128 == a.K && nks <= kMaxKsPerCta) {
-    stage_x_norm<NT, kStreamThreads>(a, nks, M8, xs, s_part, s_rstd, [] { __syncthreads(); });
-  } else {
-    if (FUSED && a.norm_w != nullptr) {
-      rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
-      __syncthreads();
-    }
-    stage_x<NT, kStreamThreads, FUSED>(a, ks0, nks, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) {
+    rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    __syncthreads();
   }
+  stage_x<NT, kStreamThreads, FUSED>(a, ks0, nks, M8, xs, s_rstd);
   __syncthreads();
 
   // this thread's B-fragment offsets inside one (kstep, n-tile) group
@@ -1143,16 +1061,11 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
   }
   pdl_wait_primary();  // x is written by the preceding kernel
   __shared__ float s_rstd[LI4_MAX_M];
-  __shared__ float s_part[NKS * NT * M8];  // stage_x_norm: per (kstep, row) partial sums of squares
-  if (FUSED && a.norm_w != nullptr && ks0 == 0 && NKS * 128 == a.K) {
-    stage_x_norm<NT, kStreamThreads>(a, NKS, M8, xs, s_part, s_rstd, [] { __syncthreads(); });
-  } else {
-    if (FUSED && a.norm_w != nullptr) {
-      rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
-      __syncthreads();
-    }
-    stage_x<NT, kStreamThreads, FUSED>(a, ks0, NKS, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) {
+    rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    __syncthreads();
   }
+  stage_x<NT, kStreamThreads, FUSED>(a, ks0, NKS, M8, xs, s_rstd);
   __syncthreads();
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
@@ -1388,17 +1301,11 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
   // ---------------- consumer warps: one whole tile per warp ----------------
   const int grp = lane >> 2, quad = lane & 3;
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
-  __shared__ float s_part[16 * NT * M8];  // stage_x_norm: per (kstep, row) partial sums of squares
-  auto consumers_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); };
-  if (FUSED && a.norm_w != nullptr && ks0 == 0 && ks_n * 128 == a.K) {  // named barrier 1: consumers only
-    stage_x_norm<NT, CW * 32>(a, ks_n, M8, xs, s_part, s_rstd, consumers_sync);
-  } else {
-    if (FUSED && a.norm_w != nullptr) {
-      rms_factors<CW>(a, s_rstd, warp, lane);
-      consumers_sync();
-    }
-    stage_x<NT, CW * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) {  // RMSNorm factors over the consumer warps only (named barrier 1)
+    rms_factors<CW>(a, s_rstd, warp, lane);
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
   }
+  stage_x<NT, CW * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
   asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
