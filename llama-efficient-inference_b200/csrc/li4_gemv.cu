@@ -152,6 +152,15 @@ struct WarpTileSum {
   }
 };
 
+// Pull the residual rows a tile's epilogue will read into L1 while x is being staged, so the
+// epilogue's loads do not add an L2 round trip to the end of the launch.  Threads tid < M of
+// the group prefetch one 32-byte segment each (rows tile*16 .. +16 of row m).
+template <bool FUSED>
+__device__ __forceinline__ void prefetch_residual(const GemvArgs& a, int tile16, int tid) {
+  if (FUSED && a.epi == LI4_EPI_RESIDUAL && tid < a.M && tile16 >= 0 && tile16 * 16 < a.N)
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(a.res + (long long)tid * a.srm + tile16 * 16));
+}
+
 // One output through the epilogue (FUSED) or as a plain fp16 store.
 template <bool FUSED>
 __device__ __forceinline__ void emit_value(const GemvArgs& a, int m, int row, float v) {
@@ -808,6 +817,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
     stream_advance<KSPLIT>(lc, units_per_tile, tile_step);
   }
   pdl_wait_primary();  // x is written by the preceding kernel
+  if (KSPLIT) prefetch_residual<FUSED>(a, blockIdx.x, threadIdx.x);
+  else prefetch_residual<FUSED>(a, blockIdx.x * kStreamWarps + warp, lane);
   __shared__ float s_rstd[LI4_MAX_M];
   if (FUSED && a.norm_w != nullptr) {
     rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
@@ -1060,6 +1071,8 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
     for (int d = 0; d < D; ++d) tile_load<RT>(buf[d], a, cur, d);
   }
   pdl_wait_primary();  // x is written by the preceding kernel
+  prefetch_residual<FUSED>(a, tile * RT, lane);
+  if (RT == 2) prefetch_residual<FUSED>(a, tile * RT + 1, lane);
   __shared__ float s_rstd[LI4_MAX_M];
   if (FUSED && a.norm_w != nullptr) {
     rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
@@ -1301,6 +1314,7 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
   // ---------------- consumer warps: one whole tile per warp ----------------
   const int grp = lane >> 2, quad = lane & 3;
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
+  if (warp < my_tiles) prefetch_residual<FUSED>(a, (int)blockIdx.x + warp * (int)gridDim.x, lane);
   if (FUSED && a.norm_w != nullptr) {  // RMSNorm factors over the consumer warps only (named barrier 1)
     rms_factors<CW>(a, s_rstd, warp, lane);
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
