@@ -102,3 +102,48 @@ def test_quantize_dequantize_validate(native):
     assert lib.li4_quantize(16, 9, 16, 16, 16, 4, 256, 128, 256, None) == native.LI4_ERR_INVALID_ARG
     assert lib.li4_dequantize(0, 16, 16, 16, 4, 256, 128, 128, 2, 256, None) == native.LI4_ERR_INVALID_ARG
     assert lib.li4_quantize(16, 0, 16, 16, 16, 0, 256, 128, 256, None) == native.LI4_OK  # empty: no launch
+
+
+def test_fused_rejects_bad_epilogues(native):
+    """li4_int4_linear_fused validates its fusion descriptor before any launch."""
+    import ctypes
+
+    lib = native.lib()
+
+    def call(f, N=64, K=256, y=16, sym=None):
+        return lib.li4_int4_linear_fused(16, 16, 16, 16, y, 1, N, K, 128, K, K // 2, K // 128,
+                                         N if sym is None else sym, ctypes.byref(f), None, 0, None)
+
+    assert call(native.Fusion(epilogue=99)) == native.LI4_ERR_INVALID_ARG
+    assert call(native.Fusion(epilogue=native.LI4_EPI_RESIDUAL)) == native.LI4_ERR_INVALID_ARG  # no residual
+    assert call(native.Fusion(epilogue=native.LI4_EPI_SWIGLU), N=40) == native.LI4_ERR_INVALID_ARG  # N % 16
+    assert call(native.Fusion(epilogue=native.LI4_EPI_QKV_ROPE, q_rows=32, k_rows=16, head_dim=16), N=80) == \
+        native.LI4_ERR_INVALID_ARG  # N != q + 2k
+    assert call(native.Fusion(epilogue=native.LI4_EPI_QKV_ROPE, q_rows=32, k_rows=16, head_dim=16), N=64) == \
+        native.LI4_ERR_INVALID_ARG  # no position, tables, q output or cache
+    assert call(native.Fusion(norm_weight=24, epilogue=native.LI4_EPI_STORE)) == native.LI4_ERR_ALIGNMENT
+    assert call(native.Fusion(epilogue=native.LI4_EPI_STORE_F32), y=18) == native.LI4_ERR_ALIGNMENT
+
+
+def test_attention_and_argmax_validate(native):
+    lib = native.lib()
+    # head_dim 48 unsupported; GQA ratio 3 unsupported; misaligned cache
+    assert lib.li4_decode_attention(16, 256, 16, 16, 64 * 4 * 48, 4 * 48, 16, 256, 1, 4, 4, 48, 16, 64, None) == \
+        native.LI4_ERR_UNSUPPORTED
+    assert lib.li4_decode_attention(16, 384, 16, 16, 64 * 2 * 64, 2 * 64, 16, 384, 1, 6, 2, 64, 16, 64, None) == \
+        native.LI4_ERR_UNSUPPORTED
+    assert lib.li4_decode_attention(16, 256, 24, 16, 64 * 64, 64, 16, 256, 1, 4, 1, 64, 16, 64, None) == \
+        native.LI4_ERR_ALIGNMENT
+    assert lib.li4_argmax_rows(16, 7, 1, 10, 10, 16, 1, None) == native.LI4_ERR_UNSUPPORTED
+    assert lib.li4_argmax_rows(16, native.LI4_F16, 1, 10, 5, 16, 1, None) == native.LI4_ERR_INVALID_ARG
+
+
+def test_allreduce_validates(native):
+    import ctypes
+
+    lib = native.lib()
+    arr = (ctypes.c_void_p * 9)(*([16] * 9))
+    assert lib.li4_allreduce_add(arr, arr, 16, 16, 9, 0, 64, 16, 16, None) == native.LI4_ERR_INVALID_ARG  # > 8 ranks
+    assert lib.li4_allreduce_add(arr, arr, 16, 16, 2, 2, 64, 16, 16, None) == native.LI4_ERR_INVALID_ARG  # rank
+    odd = (ctypes.c_void_p * 2)(18, 16)
+    assert lib.li4_allreduce_add(odd, arr, 16, 16, 2, 0, 64, 16, 16, None) == native.LI4_ERR_ALIGNMENT
