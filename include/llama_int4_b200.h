@@ -178,6 +178,14 @@ typedef struct li4_fusion {
   void* cache_k;                            /* fp16 [batch, seq, k_rows] with strides */
   void* cache_v;                            /* (elements) cache_stride_b / _s         */
   int64_t cache_stride_b, cache_stride_s;
+  /* Sums of squares handed from a residual epilogue to the next RMSNorm prologue, so the
+   * norm needs no pass over x: with LI4_EPI_RESIDUAL, sumsq_out (fp32 [ceil(N/16)][M])
+   * receives, per 16-row tile and row m, the sum of the written fp16 values squared; a
+   * launch with norm_weight and sumsq_in = that array (sumsq_tiles = ceil(K/16)) takes its
+   * mean of squares from it.  NULL = not used. */
+  float* sumsq_out;
+  const float* sumsq_in;
+  int64_t sumsq_tiles;
 } li4_fusion;
 
 /* li4_int4_linear with a fused prologue / epilogue (`fusion` NULL = plain).

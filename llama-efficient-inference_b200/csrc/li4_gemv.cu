@@ -75,6 +75,9 @@ struct GemvArgs {
   __half* cache_k;
   __half* cache_v;
   long long cache_sb, cache_ss;
+  float* ssq_out;                // LI4_EPI_RESIDUAL: per 16-row tile, per row m, sum of the written values squared
+  const float* ssq_in;           // RMSNorm prologue: the producer's ssq_out, [ssq_tiles][M]
+  int ssq_tiles;
 };
 
 // ---------------------------------------------------------------------------
@@ -86,16 +89,17 @@ __device__ __forceinline__ bool epi_paired(const GemvArgs& a) {
   return a.epi == LI4_EPI_SWIGLU || a.epi == LI4_EPI_QKV_ROPE;
 }
 
-// One output y[m, row] (LI4_EPI_STORE / LI4_EPI_RESIDUAL).
-__device__ __noinline__ void emit_one(const GemvArgs& a, int m, int row, float v) {
+// One output y[m, row] (LI4_EPI_STORE / LI4_EPI_RESIDUAL / LI4_EPI_STORE_F32); returns the value written.
+__device__ __noinline__ float emit_one(const GemvArgs& a, int m, int row, float v) {
   __half h = __float2half_rn(v);
   if (a.epi == LI4_EPI_STORE_F32) {  // fp16 Linear output widened: logits = output(h).float() (llama/model.py:455)
     reinterpret_cast<float*>(a.y)[(long long)m * a.sym + row] = __half2float(h);
-    return;
+    return __half2float(h);
   }
   if (a.epi == LI4_EPI_RESIDUAL)  // h = x + wo(...): fp16 + fp16 (llama/model.py:358-362)
     h = __float2half_rn(__half2float(h) + __half2float(a.res[(long long)m * a.srm + row]));
   a.y[(long long)m * a.sym + row] = h;
+  return __half2float(h);
 }
 
 // Pair `pair` of a paired-row weight: v0 from tile row j, v1 from tile row j + 8.
@@ -171,6 +175,25 @@ __device__ __forceinline__ void emit_value(const GemvArgs& a, int m, int row, fl
 template <bool FUSED, typename F>
 __device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, int nthr, F value) {
   const int row0 = tile * 16;
+  if (FUSED && a.ssq_out != nullptr) {
+    // (row m, tile row r) in half-warp groups of 16 rows: each group also leaves the sum of its
+    // written values squared for the next kernel's RMSNorm.  nthr is a multiple of 32 and the
+    // loop bound is uniform, so every lane reaches the shuffles.
+    const int rows = min(16, a.N - row0);
+    for (int base = 0; base < 16 * a.M; base += nthr) {
+      const int idx = base + tid, m = idx >> 4, r = idx & 15;
+      const bool live = idx < 16 * a.M;
+      float sq = 0.f;
+      if (live && r < rows) {
+        const float h = emit_one(a, m, row0 + r, value(r, m));
+        sq = h * h;
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      if (live && r == 0) a.ssq_out[(long long)tile * a.M + m] = sq;
+    }
+    return;
+  }
   if (FUSED && epi_paired(a)) {  // N is a multiple of 16: full tiles
     for (int idx = tid; idx < 8 * a.M; idx += nthr) {
       const int j = idx / a.M, m = idx - j * a.M;
@@ -182,6 +205,63 @@ __device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, 
       const int r = idx / a.M, m = idx - r * a.M;
       emit_value<FUSED>(a, m, row0 + r, value(r, m));
     }
+  }
+}
+
+// Rows mode: a warp's 16-row tile `tile16` straight from its lanes' accumulators (lane (grp, quad)
+// holds rows grp and grp + 8, columns nt*8 + 2*quad + {0, 1}); split == 1.
+template <bool FUSED, int NT>
+__device__ __forceinline__ void emit_warp_tile(const GemvArgs& a, int tile16, const float (&acc)[NT][4], int grp,
+                                               int quad) {
+  const int row0 = tile16 * 16;
+  const int rows = min(16, a.N - row0);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    if (FUSED && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = nt * 8 + 2 * quad + e;
+        if (m < a.M && row0 < a.N) emit_pair(a, m, tile16 * 8 + grp, acc[nt][e], acc[nt][e + 2]);
+      }
+      continue;
+    }
+    float sq[2] = {0.f, 0.f};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
+      if (r < rows && m < a.M) {
+        if constexpr (FUSED) {
+          const float h = emit_one(a, m, row0 + r, acc[nt][e]);
+          sq[e & 1] += h * h;
+        } else {
+          a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(acc[nt][e]);
+        }
+      }
+    }
+    if (FUSED && a.ssq_out != nullptr) {  // sum over the tile's rows: the 8 lanes of a quad column
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        sq[0] += __shfl_xor_sync(0xffffffffu, sq[0], o);
+        sq[1] += __shfl_xor_sync(0xffffffffu, sq[1], o);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = nt * 8 + 2 * quad + e;
+        if (grp == 0 && m < a.M && row0 < a.N) a.ssq_out[(long long)tile16 * a.M + m] = sq[e];
+      }
+    }
+  }
+}
+
+// 1 / rms from the producer's per-tile sums of squares (fusion.sumsq_in): one warp per row.
+template <int WARPS>
+__device__ __forceinline__ void rms_from_ssq(const GemvArgs& a, float* s_rstd, int warp, int lane) {
+  for (int m = warp; m < a.M; m += WARPS) {
+    float ss = 0.f;
+    for (int t = lane; t < a.ssq_tiles; t += 32) ss += a.ssq_in[(long long)t * a.M + m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) s_rstd[m] = rsqrtf(ss / (float)a.K + a.norm_eps);
   }
 }
 
@@ -821,7 +901,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
   else prefetch_residual<FUSED>(a, blockIdx.x * kStreamWarps + warp, lane);
   __shared__ float s_rstd[LI4_MAX_M];
   if (FUSED && a.norm_w != nullptr) {
-    rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    if (a.ssq_in != nullptr) rms_from_ssq<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    else rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
     __syncthreads();
   }
   stage_x<NT, kStreamThreads, FUSED>(a, ks0, nks, M8, xs, s_rstd);
@@ -862,27 +943,21 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
         const int row0 = tile * 16;
         const int rows = min(16, a.N - row0);
         if (!KSPLIT) {
+          if (a.split == 1) {
+            emit_warp_tile<FUSED, NT>(a, tile, acc, grp, quad);
+          } else {
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            if (FUSED && a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int m = nt * 8 + 2 * quad + e;
-                if (m < a.M) emit_pair(a, m, tile * 8 + grp, acc[nt][e], acc[nt][e + 2]);
-              }
-            } else {
+            for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
-                if (r < rows && m < a.M) {
-                  if (a.split == 1) emit_value<FUSED>(a, m, row0 + r, acc[nt][e]);
-                  else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
-                }
+                if (r < rows && m < a.M) a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
               }
-            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-          }
           if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
             __threadfence();
             __syncwarp();
@@ -1075,7 +1150,8 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
   if (RT == 2) prefetch_residual<FUSED>(a, tile * RT + 1, lane);
   __shared__ float s_rstd[LI4_MAX_M];
   if (FUSED && a.norm_w != nullptr) {
-    rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    if (a.ssq_in != nullptr) rms_from_ssq<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
+    else rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
     __syncthreads();
   }
   stage_x<NT, kStreamThreads, FUSED>(a, ks0, NKS, M8, xs, s_rstd);
@@ -1111,27 +1187,19 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
     }
     const int row0 = tile * ROWS;
 #pragma unroll
-    for (int rt = 0; rt < RT; ++rt)
+    for (int rt = 0; rt < RT; ++rt) {
+      if (a.split == 1) {
+        if (row0 + rt * 16 < a.N) emit_warp_tile<FUSED, NT>(a, tile * RT + rt, acc[rt], grp, quad);
+        continue;
+      }
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        if (FUSED && a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of each 16-row subtile are a pair
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int m = nt * 8 + 2 * quad + e;
-            if (m < a.M && row0 + rt * 16 < a.N)
-              emit_pair(a, m, (tile * RT + rt) * 8 + grp, acc[rt][nt][e], acc[rt][nt][e + 2]);
-          }
-          continue;
-        }
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = row0 + rt * 16 + grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
-          if (r < a.N && m < a.M) {
-            if (a.split == 1) emit_value<FUSED>(a, m, r, acc[rt][nt][e]);
-            else a.partial[((long long)blockIdx.y * a.M + m) * a.N + r] = acc[rt][nt][e];
-          }
+          if (r < a.N && m < a.M) a.partial[((long long)blockIdx.y * a.M + m) * a.N + r] = acc[rt][nt][e];
         }
-      }
+    }
     if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
       __threadfence();
       __syncwarp();
@@ -1316,7 +1384,8 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
   if (warp < my_tiles) prefetch_residual<FUSED>(a, (int)blockIdx.x + warp * (int)gridDim.x, lane);
   if (FUSED && a.norm_w != nullptr) {  // RMSNorm factors over the consumer warps only (named barrier 1)
-    rms_factors<CW>(a, s_rstd, warp, lane);
+    if (a.ssq_in != nullptr) rms_from_ssq<CW>(a, s_rstd, warp, lane);
+    else rms_factors<CW>(a, s_rstd, warp, lane);
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
   }
   stage_x<NT, CW * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
@@ -1362,24 +1431,16 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
     if (lane == 0) mbar_arrive(&empty[s]);  // the stage is free for the producer
     const int row0 = tile * 16;
     const int rows = min(16, a.N - row0);
+    if (a.split == 1) {
+      emit_warp_tile<FUSED, NT>(a, tile, acc, grp, quad);
+    } else {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      if (FUSED && a.split == 1 && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int m = nt * 8 + 2 * quad + e;
-          if (m < a.M) emit_pair(a, m, tile * 8 + grp, acc[nt][e], acc[nt][e + 2]);
-        }
-      } else {
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
-          if (r < rows && m < a.M) {
-            if (a.split == 1) emit_value<FUSED>(a, m, row0 + r, acc[nt][e]);
-            else a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
-          }
+          if (r < rows && m < a.M) a.partial[((long long)blockIdx.y * a.M + m) * a.N + row0 + r] = acc[nt][e];
         }
-      }
     }
     if (a.split > 1) {  // last K range to arrive sums the partials (fixed order) and resets the counter
       __threadfence();
@@ -1791,6 +1852,14 @@ static bool aligned4(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr)
 
 // Preconditions of the fused prologue / epilogues (li4_fusion).
 static int check_fusion(const li4_fusion& f, int64_t M, int64_t N, int64_t K) {
+  if (f.sumsq_out != nullptr && (f.epilogue != LI4_EPI_RESIDUAL || !aligned4(f.sumsq_out)))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: sumsq_out goes with the residual epilogue (4-byte "
+                     "aligned, [ceil(N/16)][M] floats)");
+  if (f.sumsq_in != nullptr &&
+      (f.norm_weight == nullptr || !aligned4(f.sumsq_in) || f.sumsq_tiles != (K + 15) / 16))
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: sumsq_in needs the RMSNorm prologue and "
+                     "sumsq_tiles = ceil(K/16) = %lld (got %lld)", (long long)((K + 15) / 16),
+                     (long long)f.sumsq_tiles);
   if (f.norm_weight != nullptr) {
     if (!aligned16(f.norm_weight))
       return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: norm_weight must be 16-byte aligned");
@@ -1907,6 +1976,9 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     args.cache_v = static_cast<__half*>(f->cache_v);
     args.cache_sb = f->cache_stride_b;
     args.cache_ss = f->cache_stride_s;
+    args.ssq_out = f->sumsq_out;
+    args.ssq_in = f->sumsq_in;
+    args.ssq_tiles = (int)f->sumsq_tiles;
   }
   args.x = static_cast<const __half*>(x);
   args.packed = static_cast<const uint8_t*>(packed);

@@ -56,6 +56,9 @@ class Fusion(ctypes.Structure):
         ("cache_v", ctypes.c_void_p),
         ("cache_stride_b", ctypes.c_int64),
         ("cache_stride_s", ctypes.c_int64),
+        ("sumsq_out", ctypes.c_void_p),
+        ("sumsq_in", ctypes.c_void_p),
+        ("sumsq_tiles", ctypes.c_int64),
     ]
 
 

@@ -8,6 +8,8 @@ adds.  Here a block is:
 
   1. QKV GEMV   RMSNorm(attention_norm) while staging x; RoPE on q and k; q to a
                 buffer, k and v into the KV cache at row *pos  (li4_int4_linear_fused)
+                (the mean of squares comes from the previous block's w2 epilogue, which
+                leaves per-tile sums of squares of h beside h: no extra pass over x)
   2. attention  grouped-query decode attention over cache rows 0..*pos
                                                                 (li4_decode_attention)
   3. wo GEMV    h1 = h + wo(attn)                               (residual epilogue)
@@ -185,6 +187,9 @@ class FusedDecoder:
                  "q": torch.empty(bs, self.n_heads * self.head_dim, **f16),
                  "attn": torch.empty(bs, self.n_heads * self.head_dim, **f16),
                  "ffn": torch.empty(bs, self.ffn, **f16), "part": torch.empty(bs, self.dim, **f16),
+                 # sums of squares of h / h1 per 16-row tile, from the residual epilogues to the next RMSNorm
+                 "ssq_h": torch.zeros((self.dim + 15) // 16, bs, dtype=torch.float32, device=self.device),
+                 "ssq_h1": torch.zeros((self.dim + 15) // 16, bs, dtype=torch.float32, device=self.device),
                  "logits": torch.empty(bs, self.vocab_local, dtype=torch.float32, device=self.device)}
             self._bufs[bs] = b
         return b
@@ -223,11 +228,15 @@ class FusedDecoder:
         h, h1, q, attn, ffn, part = buf["h"], buf["h1"], buf["q"], buf["attn"], buf["ffn"], buf["part"]
         torch.index_select(self.model.tok_embeddings.weight, 0, tokens.view(-1), out=h)
         E = native
+        ssq_h, ssq_h1 = buf["ssq_h"], buf["ssq_h1"]
+        tiles = ssq_h.shape[0]
+        h_ssq = None  # the embedding rows carry no sums of squares: the first block's norm reads x
         for blk in self.blocks:
             att = blk.att
             att._ensure_cache(h)
             ck, cv = att.cache_k, att.cache_v
             f = E.Fusion(norm_weight=blk.attn_norm.data_ptr(), norm_eps=blk.attn_eps, epilogue=E.LI4_EPI_QKV_ROPE,
+                         sumsq_in=h_ssq, sumsq_tiles=tiles if h_ssq else 0,
                          q_rows=blk.q_rows, k_rows=blk.k_rows, head_dim=self.head_dim, pos=pos.data_ptr(),
                          rope_cos=blk.cos.data_ptr(), rope_sin=blk.sin.data_ptr(), rope_stride=blk.cos.stride(0),
                          q_out=q.data_ptr(), stride_qm=q.stride(0), cache_k=ck.data_ptr(), cache_v=cv.data_ptr(),
@@ -235,19 +244,27 @@ class FusedDecoder:
             int4_linear_fused(h, *blk.qkv, None, f)
             decode_attention(q, ck, cv, pos, attn, self.n_heads, self.n_kv_heads)
             if att.tp_group is None:
-                f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h.data_ptr(), stride_rm=h.stride(0))
+                f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h.data_ptr(), stride_rm=h.stride(0),
+                             sumsq_out=ssq_h1.data_ptr())
                 int4_linear_fused(attn, *blk.wo, h1, f)
+                h1_ssq = ssq_h1.data_ptr()
             else:
                 self._row_parallel(attn, blk.wo, h, h1, part, att.tp_group, slot=0)
-            f = E.Fusion(norm_weight=blk.ffn_norm.data_ptr(), norm_eps=blk.ffn_eps, epilogue=E.LI4_EPI_SWIGLU)
+                h1_ssq = None
+            f = E.Fusion(norm_weight=blk.ffn_norm.data_ptr(), norm_eps=blk.ffn_eps, epilogue=E.LI4_EPI_SWIGLU,
+                         sumsq_in=h1_ssq, sumsq_tiles=tiles if h1_ssq else 0)
             int4_linear_fused(h1, *blk.gate_up, ffn, f)
             if blk.ff.tp_group is None:
-                f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h1.data_ptr(), stride_rm=h1.stride(0))
+                f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h1.data_ptr(), stride_rm=h1.stride(0),
+                             sumsq_out=ssq_h.data_ptr())
                 int4_linear_fused(ffn, *blk.w2, h, f)
+                h_ssq = ssq_h.data_ptr()
             else:
                 self._row_parallel(ffn, blk.w2, h1, h, part, blk.ff.tp_group, slot=1)
+                h_ssq = None
         logits = buf["logits"]  # fp32: the lm_head writes its fp16 outputs widened (output(h).float())
-        f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE_F32)
+        f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE_F32,
+                     sumsq_in=h_ssq, sumsq_tiles=tiles if h_ssq else 0)
         int4_linear_fused(h, *self.out, None, f, y_ptr=logits.data_ptr(), y_stride=logits.stride(0))
         if self.model.tp_group is not None:
             import torch.distributed as dist

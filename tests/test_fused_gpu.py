@@ -341,3 +341,31 @@ def test_store_f32_epilogue(M, N, K, fz, cuda_device):
     fused.int4_linear_fused(x, p, s, z, None, f, y_ptr=y.data_ptr(), y_stride=y.stride(0))
     assert torch.equal(y, y.half().float()), "fp32 outputs are not widened fp16 values"
     close(y, F.linear(rmsnorm_ref(x, nw, 1e-5), w16).float(), what="store_f32")
+
+
+@pytest.mark.parametrize("M", [1, 3, 16])
+@pytest.mark.parametrize("N,K", [(2048, 2048), (2048, 8192), (2048, 256)])
+def test_sumsq_handoff(M, N, K, fz, cuda_device):
+    """A residual epilogue leaves per-16-row-tile sums of squares of what it wrote; an RMSNorm
+    prologue reading them gives the same result as the prologue that reads x itself."""
+    fused, nat = fz
+    p, s, z, w16 = quantized(N, K, cuda_device, 9 * N + K)
+    x = randn((M, K), cuda_device, 70 + M)
+    res = randn((M, N), cuda_device, 71 + M)
+    h = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    ssq = torch.full(((N + 15) // 16, M), float("nan"), dtype=torch.float32, device=cuda_device)
+    f = nat.Fusion(epilogue=nat.LI4_EPI_RESIDUAL, residual=res.data_ptr(), stride_rm=N, sumsq_out=ssq.data_ptr())
+    fused.int4_linear_fused(x, p, s, z, h, f)
+    want = h.float().view(M, -1, 16).pow(2).sum(-1).t()  # [tiles, M]
+    torch.testing.assert_close(ssq, want, rtol=1e-5, atol=0)
+    # the next launch's RMSNorm over h: from the sums of squares vs from h itself
+    p2, s2, z2, _ = quantized(3072, N, cuda_device, 5 * N + 1)
+    nw = (1 + 0.1 * randn((N,), cuda_device, 72).float()).half()
+    y_a = torch.empty(M, 3072, dtype=torch.float16, device=cuda_device)
+    y_b = torch.empty_like(y_a)
+    fused.int4_linear_fused(h, p2, s2, z2, y_a, nat.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5,
+                                                          epilogue=nat.LI4_EPI_STORE))
+    fused.int4_linear_fused(h, p2, s2, z2, y_b, nat.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5,
+                                                          epilogue=nat.LI4_EPI_STORE, sumsq_in=ssq.data_ptr(),
+                                                          sumsq_tiles=ssq.shape[0]))
+    close(y_b, y_a, what="norm from handed-over sums of squares")
