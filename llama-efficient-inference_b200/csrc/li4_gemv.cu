@@ -90,7 +90,7 @@ __device__ __forceinline__ bool epi_paired(const GemvArgs& a) {
 }
 
 // One output y[m, row] (LI4_EPI_STORE / LI4_EPI_RESIDUAL / LI4_EPI_STORE_F32); returns the value written.
-__device__ __noinline__ float emit_one(const GemvArgs& a, int m, int row, float v) {
+__device__ __forceinline__ float emit_one(const GemvArgs& a, int m, int row, float v) {
   __half h = __float2half_rn(v);
   if (a.epi == LI4_EPI_STORE_F32) {  // fp16 Linear output widened: logits = output(h).float() (llama/model.py:455)
     reinterpret_cast<float*>(a.y)[(long long)m * a.sym + row] = __half2float(h);
@@ -103,7 +103,7 @@ __device__ __noinline__ float emit_one(const GemvArgs& a, int m, int row, float 
 }
 
 // Pair `pair` of a paired-row weight: v0 from tile row j, v1 from tile row j + 8.
-__device__ __noinline__ void emit_pair(const GemvArgs& a, int m, int pair, float v0, float v1) {
+__device__ __forceinline__ void emit_pair(const GemvArgs& a, int m, int pair, float v0, float v1) {
   const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
   if (a.epi == LI4_EPI_SWIGLU) {  // F.silu(w1(x)) * w3(x) (llama/model.py:315)
     const float g = __half2float(h0);
@@ -341,45 +341,49 @@ __device__ __forceinline__ uint4 lds128_ordered(const uint8_t* p) {
 template <int NT, int THREADS = kThreads, bool NORM = false>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
                                         const float* s_rstd = nullptr) {
-  const int total = nks * NT * M8 * 16;
+  // One thread per 16-byte k-chunk (k = 8 values) and every row of it: the RMSNorm weight chunk
+  // is read once, and the rows' loads are independent, so they are in flight together.
+  const int chunks = nks * 16;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
-  for (int idx = threadIdx.x; idx < total; idx += THREADS) {
-    const int w = idx & 3;
-    const int block = idx >> 2;
-    const int quad = block & 3;
-    const int t = block >> 2;
-    const int m8 = t % M8;
-    const int t2 = t / M8;
-    const int nt = t2 % NT;
-    const int ks = t2 / NT;
-    const int m = nt * 8 + m8;
-    uint4 out = make_uint4(0u, 0u, 0u, 0u);
-    if (m < a.M) {
-      const long long k = (long long)(ks0 + ks) * 128 + 32 * quad + 8 * w;
-      const __half* src = a.x + (long long)m * a.sxm + k;
-      uint32_t u[4];
-      if (vec_ok) {
-        const uint4 v = *reinterpret_cast<const uint4*>(src);
-        u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
-      } else {
+  for (int c = threadIdx.x; c < chunks; c += THREADS) {
+    const int ks = c >> 4, quad = (c >> 2) & 3, w = c & 3;
+    const long long k = (long long)(ks0 + ks) * 128 + 32 * quad + 8 * w;
+    uint4 wn = make_uint4(0u, 0u, 0u, 0u);
+    if (NORM && a.norm_w != nullptr) wn = *reinterpret_cast<const uint4*>(a.norm_w + k);  // 16-byte aligned
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int m8 = 0; m8 < 8; ++m8) {
+        if (m8 >= M8) break;
+        const int m = nt * 8 + m8;
+        const int block = ((ks * NT + nt) * M8 + m8) * 4 + quad;
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (m < a.M) {
+          const __half* src = a.x + (long long)m * a.sxm + k;
+          uint32_t u[4];
+          if (vec_ok) {
+            const uint4 v = *reinterpret_cast<const uint4*>(src);
+            u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
+          }
+          if (NORM && a.norm_w != nullptr) {
+            const float r = s_rstd[m];
+            u[0] = norm_pair(u[0], wn.x, r);
+            u[1] = norm_pair(u[1], wn.y, r);
+            u[2] = norm_pair(u[2], wn.z, r);
+            u[3] = norm_pair(u[3], wn.w, r);
+          }
+          out.x = __byte_perm(u[0], u[2], 0x5410);  // (x0, x4)
+          out.y = __byte_perm(u[0], u[2], 0x7632);  // (x1, x5)
+          out.z = __byte_perm(u[1], u[3], 0x5410);  // (x2, x6)
+          out.w = __byte_perm(u[1], u[3], 0x7632);  // (x3, x7)
+        }
+        *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8)) = out;
       }
-      if (NORM && a.norm_w != nullptr) {  // 16-byte aligned weight (checked by the host)
-        const uint4 w = *reinterpret_cast<const uint4*>(a.norm_w + k);
-        const float r = s_rstd[m];
-        u[0] = norm_pair(u[0], w.x, r);
-        u[1] = norm_pair(u[1], w.y, r);
-        u[2] = norm_pair(u[2], w.z, r);
-        u[3] = norm_pair(u[3], w.w, r);
-      }
-      out.x = __byte_perm(u[0], u[2], 0x5410);  // (x0, x4)
-      out.y = __byte_perm(u[0], u[2], 0x7632);  // (x1, x5)
-      out.z = __byte_perm(u[1], u[3], 0x5410);  // (x2, x6)
-      out.w = __byte_perm(u[1], u[3], 0x7632);  // (x3, x7)
     }
-    *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8)) = out;
   }
 }
 
