@@ -8,8 +8,8 @@ adds.  Here a block is:
 
   1. QKV GEMV   RMSNorm(attention_norm) while staging x; RoPE on q and k; q to a
                 buffer, k and v into the KV cache at row *pos  (li4_int4_linear_fused)
-                (the mean of squares comes from the previous block's w2 epilogue, which
-                leaves per-tile sums of squares of h beside h: no extra pass over x)
+                (at batch <= 4 the mean of squares comes from the previous block's w2
+                epilogue, which leaves per-tile sums of squares of h beside h)
   2. attention  grouped-query decode attention over cache rows 0..*pos
                                                                 (li4_decode_attention)
   3. wo GEMV    h1 = h + wo(attn)                               (residual epilogue)
@@ -230,6 +230,9 @@ class FusedDecoder:
         E = native
         ssq_h, ssq_h1 = buf["ssq_h"], buf["ssq_h1"]
         tiles = ssq_h.shape[0]
+        # measured: the hand-over of sums of squares pays at small batches; at 16 rows the producer's
+        # reduction costs more than the consumer's pass over x
+        handoff = bs <= 4
         h_ssq = None  # the embedding rows carry no sums of squares: the first block's norm reads x
         for blk in self.blocks:
             att = blk.att
@@ -245,9 +248,9 @@ class FusedDecoder:
             decode_attention(q, ck, cv, pos, attn, self.n_heads, self.n_kv_heads)
             if att.tp_group is None:
                 f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h.data_ptr(), stride_rm=h.stride(0),
-                             sumsq_out=ssq_h1.data_ptr())
+                             sumsq_out=ssq_h1.data_ptr() if handoff else None)
                 int4_linear_fused(attn, *blk.wo, h1, f)
-                h1_ssq = ssq_h1.data_ptr()
+                h1_ssq = ssq_h1.data_ptr() if handoff else None
             else:
                 self._row_parallel(attn, blk.wo, h, h1, part, att.tp_group, slot=0)
                 h1_ssq = None
@@ -256,9 +259,9 @@ class FusedDecoder:
             int4_linear_fused(h1, *blk.gate_up, ffn, f)
             if blk.ff.tp_group is None:
                 f = E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=h1.data_ptr(), stride_rm=h1.stride(0),
-                             sumsq_out=ssq_h.data_ptr())
+                             sumsq_out=ssq_h.data_ptr() if handoff else None)
                 int4_linear_fused(ffn, *blk.w2, h, f)
-                h_ssq = ssq_h.data_ptr()
+                h_ssq = ssq_h.data_ptr() if handoff else None
             else:
                 self._row_parallel(ffn, blk.w2, h1, h, part, blk.ff.tp_group, slot=1)
                 h_ssq = None
