@@ -271,6 +271,7 @@ __device__ __forceinline__ void rms_from_ssq(const GemvArgs& a, float* s_rstd, i
 template <int WARPS>
 __device__ __forceinline__ void rms_factors(const GemvArgs& a, float* s_rstd, int warp, int lane) {
   const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
+#pragma unroll 2
   for (int m = warp; m < a.M; m += WARPS) {
     const __half* row = a.x + (long long)m * a.sxm;
     float ss = 0.f;
@@ -301,11 +302,12 @@ __device__ __forceinline__ void rms_factors(const GemvArgs& a, float* s_rstd, in
 }
 
 // fp16(fp16(x * rstd) * w): RMSNorm's output cast (type_as) and its fp16 weight product.
+// The fp16 x fp16 product is exact before its one rounding, so the half2 multiply gives the same
+// bits as the reference's float multiply rounded to fp16.
 __device__ __forceinline__ uint32_t norm_pair(uint32_t xv, uint32_t wv, float rstd) {
   const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xv));
-  const float2 wf = __half22float2(*reinterpret_cast<const __half2*>(&wv));
-  const float2 n = __half22float2(__floats2half2_rn(xf.x * rstd, xf.y * rstd));
-  const __half2 o = __floats2half2_rn(n.x * wf.x, n.y * wf.y);
+  const __half2 n = __floats2half2_rn(xf.x * rstd, xf.y * rstd);
+  const __half2 o = __hmul2(n, *reinterpret_cast<const __half2*>(&wv));
   return *reinterpret_cast<const uint32_t*>(&o);
 }
 
