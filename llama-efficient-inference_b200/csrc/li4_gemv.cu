@@ -911,7 +911,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
     else rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
     __syncthreads();
   }
-  stage_x<NT, kStreamThreads, FUSED>(a, ks0, nks, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) stage_x<NT, kStreamThreads, true>(a, ks0, nks, M8, xs, s_rstd);
+  else stage_x<NT, kStreamThreads, false>(a, ks0, nks, M8, xs);
   __syncthreads();
 
   // this thread's B-fragment offsets inside one (kstep, n-tile) group
@@ -1160,7 +1161,8 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
     else rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
     __syncthreads();
   }
-  stage_x<NT, kStreamThreads, FUSED>(a, ks0, NKS, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) stage_x<NT, kStreamThreads, true>(a, ks0, NKS, M8, xs, s_rstd);
+  else stage_x<NT, kStreamThreads, false>(a, ks0, NKS, M8, xs);
   __syncthreads();
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
@@ -1394,7 +1396,8 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
     else rms_factors<CW>(a, s_rstd, warp, lane);
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
   }
-  stage_x<NT, CW * 32, FUSED>(a, ks0, ks_n, M8, xs, s_rstd);
+  if (FUSED && a.norm_w != nullptr) stage_x<NT, CW * 32, true>(a, ks0, ks_n, M8, xs, s_rstd);
+  else stage_x<NT, CW * 32, false>(a, ks0, ks_n, M8, xs);
   asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 
   const bool bvalid = grp < ((NT == 1) ? a.M : 8);
