@@ -433,6 +433,79 @@ def size_floor(a):
         torch.cuda.empty_cache()
 
 
+def fused_cost(a):
+    """--fused-cost: each fused decode GEMV (llama.fused) against the same GEMV without its prologue /
+    epilogue, µs per launch in a CUDA graph of back-to-back launches over rotating weight copies."""
+    from llama import _native as E
+    from llama import fused
+    from llama.quantize import QuantizedLinear
+
+    dev = torch.device("cuda", 0)
+
+    def timeit(fn, copies):
+        fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ts.append(e0.elapsed_time(e1) / copies)
+        return round(statistics.median(ts) * 1e3, 2)
+
+    for M in (1, 16):
+        for name, N, K in (("qkv_fused", 3072, 2048), ("o_proj", 2048, 2048), ("gate_up_fused", 16384, 2048),
+                           ("down_proj", 2048, 8192)):
+            copies = max(2, 3 * L2_BYTES // gemv_bytes(N, K, 0) + 1)
+            gen = torch.Generator(device=dev).manual_seed(N + K)
+            w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+            p, s, z = QuantizedLinear.quantize_tensor(w, GROUP)
+            del w
+            ws = [(p, s, z)] + [(p.clone(), s.clone(), z.clone()) for _ in range(copies - 1)]
+            x = torch.randn(M, K, generator=gen, device=dev).half()
+            y = torch.empty(M, N, dtype=torch.float16, device=dev)
+            nw = torch.ones(K, dtype=torch.float16, device=dev)
+            res = torch.randn(M, N, generator=gen, device=dev).half()
+            pos = torch.tensor([5], dtype=torch.long, device=dev)
+            cos, sin = torch.ones(64, 32, device=dev), torch.zeros(64, 32, device=dev)
+            q = torch.empty(M, 2048, dtype=torch.float16, device=dev)
+            ck = torch.zeros(M, 64, 8, 64, dtype=torch.float16, device=dev)
+            cv = torch.zeros_like(ck)
+
+            def run(f):
+                def go():
+                    for pi, si, zi in ws:
+                        fused.int4_linear_fused(x, pi, si, zi, None if f.epilogue == E.LI4_EPI_QKV_ROPE else y, f)
+                return go
+
+            rec = {"fused_cost": name, "M": M, "plain": timeit(run(E.Fusion(epilogue=E.LI4_EPI_STORE)), copies)}
+            if name in ("qkv_fused", "gate_up_fused"):
+                rec["norm"] = timeit(run(E.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5, epilogue=E.LI4_EPI_STORE)),
+                                     copies)
+            if name == "qkv_fused":
+                rec["norm+rope"] = timeit(run(E.Fusion(
+                    norm_weight=nw.data_ptr(), norm_eps=1e-5, epilogue=E.LI4_EPI_QKV_ROPE, q_rows=2048, k_rows=512,
+                    head_dim=64, pos=pos.data_ptr(), rope_cos=cos.data_ptr(), rope_sin=sin.data_ptr(), rope_stride=32,
+                    q_out=q.data_ptr(), stride_qm=2048, cache_k=ck.data_ptr(), cache_v=cv.data_ptr(),
+                    cache_stride_b=ck.stride(0), cache_stride_s=ck.stride(1))), copies)
+            if name == "gate_up_fused":
+                rec["norm+swiglu"] = timeit(run(E.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5,
+                                                         epilogue=E.LI4_EPI_SWIGLU)), copies)
+            if name in ("o_proj", "down_proj"):
+                rec["residual"] = timeit(run(E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=res.data_ptr(),
+                                                      stride_rm=N)), copies)
+            print(json.dumps(rec), flush=True)
+            del ws
+            torch.cuda.empty_cache()
+
+
 def profile_shape(a):
     """--profile-shape NAME: `--launches` eager launches of one shape (a small case for ncu captures)."""
     from llama.int4_gemv import int4_linear_out
@@ -769,6 +842,8 @@ def main():
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
     ap.add_argument("--sweep", action="store_true", help="kernel-family x launch-shape sweep of the decode shapes")
+    ap.add_argument("--fused-cost", action="store_true",
+                    help="each fused decode GEMV against the same GEMV without its prologue / epilogue")
     ap.add_argument("--size-floor", action="store_true",
                     help="time a plain HBM read of each decode-GEMV byte count as back-to-back launches")
     ap.add_argument("--sweep-m", default="1,8,16")
@@ -782,6 +857,9 @@ def main():
         return
     if a.size_floor:
         size_floor(a)
+        return
+    if a.fused_cost:
+        fused_cost(a)
         return
     if a.warmup < 3:
         a.warmup = 3
