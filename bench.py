@@ -673,7 +673,8 @@ def build_decode_model(device, bs: int, max_seq_len: int, seed: int = 0):
     return model
 
 
-def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int, fused: bool = True):
+def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int, fused: bool = True,
+               program: bool = False):
     """Prefill + `gen` greedy decode steps replayed from one graph; timings are the max over ranks.
     fused: the step as llama.fused kernels (five launches per block), else the module-by-module step."""
     from llama.generation import DecodeGraph
@@ -684,7 +685,7 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
 
         shard_model(model)
     if fused:
-        model.enable_fused_decode()
+        model.enable_fused_decode(program=program)
     torch.cuda.synchronize(device)
     graph = DecodeGraph(model, bs)
     gen_t = torch.Generator(device=device).manual_seed(1)
@@ -710,10 +711,12 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
     e2e_ms = max_over_ranks(statistics.median(e2es), world, device)
     prefill_ms = max_over_ranks(statistics.median(prefills), world, device)
     q = statistics.quantiles(steps, n=10)
+    path = getattr(getattr(model, "_fused", None), "last_path", None)
     del graph, model
     torch.cuda.empty_cache()
     return {"bs": bs, "prompt": prompt_len, "generated": gen, "tp": world, "reps": reps,
-            "step": "fused (llama.fused)" if fused else "unfused (module by module)",
+            "step": ("one-launch program (llama.program)" if path == "program" else "fused launches (llama.fused)")
+            if fused else "unfused (module by module)",
             "decode_ms_per_step": round(step_ms, 4), "decode_p10_ms": round(q[0], 4), "decode_p90_ms": round(q[-1], 4),
             "decode_tok_s": round(bs / (step_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 3),
             "e2e_tok_s": round(bs * gen / (e2e_ms * 1e-3), 1)}
@@ -732,7 +735,8 @@ def run_gpu(a):
         rows = []
         for bs in a.decode_bs:
             log(f"decode: Llama-3.2-1B INT4, bs={bs}, {a.decode_prompt}-token prefill, {a.decode_gen} steps, tp={world}")
-            rows.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world))
+            rows.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world,
+                                   program=a.decode_program))
             if a.decode_unfused:
                 rows.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
         if rank == 0:
@@ -760,7 +764,8 @@ def run_gpu(a):
     if not a.no_decode:
         for bs in a.decode_bs:
             log(f"decode: Llama-3.2-1B INT4, bs={bs}, {a.decode_prompt}-token prefill, {a.decode_gen} steps, tp={world}")
-            decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world))
+            decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world,
+                                     program=a.decode_program))
             if a.decode_unfused:
                 decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
     log("per-shape isolated timing")
@@ -833,6 +838,8 @@ def main():
     ap.add_argument("--decode-prompt", type=int, default=512)
     ap.add_argument("--decode-gen", type=int, default=128)
     ap.add_argument("--decode-reps", type=int, default=3)
+    ap.add_argument("--decode-program", action="store_true",
+                    help="run the fused decode step as one persistent launch (llama.program)")
     ap.add_argument("--decode-unfused", action="store_true",
                     help="also time the module-by-module decode step (ATen ops around the INT4 GEMVs)")
     ap.add_argument("--profile-shape", default=None,

@@ -226,8 +226,9 @@ int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, i
 
 /* Device-side error flags of the current device (bit 0: a bounded pipeline wait
  * inside a GEMV kernel ran out; bit 1: a bounded wait for a peer's flag in
- * li4_allreduce_add ran out -- the kernel carried on and its outputs are not
- * valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
+ * li4_allreduce_add ran out; bit 2: a decode program's wait for another op
+ * ran out; bit 3: a program gather met an id outside its table -- the kernel
+ * carried on and its outputs are not valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);
 
@@ -279,6 +280,86 @@ int li4_dequantize(const void* packed, const void* scale, const void* zero, void
  * Replaces: QuantizedLinear.quantize_tensor (llama/quantize.py:44-75). */
 int li4_quantize(const void* w, int w_dtype, void* packed, void* scale, void* zero,
                  int64_t N, int64_t K, int64_t group_size, int64_t stride_wn, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode program: a list of ops run by ONE persistent launch (one CTA per SM).
+ *
+ * Each CTA has a producer warp that streams the weight tiles of every linear op
+ * of the program, in program order, into a ring of shared-memory stages with
+ * bulk copies -- it never waits for activations, so the weights of the next ops
+ * are already on chip while the current op waits for its inputs.  The consumer
+ * warps run the ops in order; an op with wait = j first waits (bounded) until
+ * every CTA has finished op j, and reads its inputs after that.  Ops without a
+ * wait run as soon as their weights arrive.  An op reads and writes its buffers
+ * only after its wait completes, so a write-after-read hazard needs a wait too.
+ *
+ * Replaces: the per-token sequence of launches of the reference's decode step
+ * (Llama.forward at seqlen 1, llama/model.py:222-277, 310-315, 358-362, 440-455,
+ * and the greedy argmax of llama/generation.py:59-60) by one launch; each op
+ * computes what the per-launch entry points above compute (li4_int4_linear_fused,
+ * li4_decode_attention, li4_argmax_rows).
+ *
+ * Build once (outside CUDA graph capture: finalize allocates device memory),
+ * then launch any number of times (a launch is capturable).  Every pointer an
+ * op was given is read at each launch; its contents may change between
+ * launches.  Launches of one program must not overlap (one stream).
+ * --------------------------------------------------------------------------- */
+typedef struct li4_program li4_program;
+
+#define LI4_NO_WAIT (-1)
+
+int li4_program_create(li4_program** prog);
+int li4_program_destroy(li4_program* prog);
+
+/* An INT4 linear with an optional fusion (as li4_int4_linear_fused; fusion may be
+ * NULL).  Program linears take group 128, N >= 16, K % 128 == 0 with
+ * K <= 2048 or K % 2048 == 0, 16-byte aligned x rows and packed / scale / zero
+ * rows (stride_pn % 16 == 0; stride_sn % 8 == 0 unless the rows are contiguous).
+ * *op receives the op index. */
+int li4_program_add_linear(li4_program* prog, const void* x, const void* packed, const void* scale,
+                           const void* zero, void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                           int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym,
+                           const li4_fusion* fusion, int wait, int* op);
+
+/* Decode attention as li4_decode_attention (n_heads / n_kv_heads in {1, 2, 4, 8},
+ * head_dim 32, 64 or 128, (n_heads / n_kv_heads) * head_dim <= 512).  One CTA per
+ * (sequence, KV head); max_seq is bounded by the CTA's shared memory
+ * (LI4_ERR_UNSUPPORTED beyond it). */
+int li4_program_add_attention(li4_program* prog, const void* q, int64_t stride_qb, const void* cache_k,
+                              const void* cache_v, int64_t cache_stride_b, int64_t cache_stride_s, void* out,
+                              int64_t stride_ob, int64_t batch, int64_t n_heads, int64_t n_kv_heads,
+                              int64_t head_dim, const int64_t* pos, int64_t max_seq, int wait, int* op);
+
+/* out[r, :] = table[ids[r], :] for r < rows (fp16 rows of `cols` values; an id
+ * outside [0, table_rows) is clamped and sets bit 3 of li4_device_errors).
+ * Replaces: the token embedding lookup (llama/model.py:440). */
+int li4_program_add_gather(li4_program* prog, const void* table, int64_t table_rows, int64_t cols,
+                           int64_t stride_t, const int64_t* ids, int64_t rows, void* out, int64_t stride_o,
+                           int wait, int* op);
+
+/* out[r * out_stride] = torch.argmax(logits[r, :cols]) for fp32 logits (first
+ * index on ties, NaN above all), as li4_argmax_rows. */
+int li4_program_add_argmax(li4_program* prog, const float* logits, int64_t rows, int64_t cols, int64_t stride,
+                           int64_t* out, int64_t out_stride, int wait, int* op);
+
+/* *value += 1 once every op of the launch has finished (the decode position). */
+int li4_program_add_increment(li4_program* prog, int64_t* value);
+
+/* Plan the launch on the current device, allocate the program's device state
+ * (op table, completion counters, split-K scratch) and upload it. */
+int li4_program_finalize(li4_program* prog);
+
+/* Launch the whole program on `stream`. */
+int li4_program_launch(li4_program* prog, void* stream);
+
+/* Per-op timeline of the following launches (NULL turns it off): stamps[(op * ctas + cta) * 4 + i]
+ * = %globaltimer (ns) when the CTA started op `op` (i = 0), its input wait ended (1), its x was
+ * staged (2, linear ops) and its units were done (3); ops a CTA has no units of are not stamped.
+ * capacity >= ops * ctas * 4 int64 values (after finalize). */
+int li4_program_set_trace(li4_program* prog, int64_t* stamps, int64_t capacity);
+
+/* CTAs, ring stages per CTA and dynamic shared memory of the launch (after finalize). */
+int li4_program_info(const li4_program* prog, int* ctas, int* stages, size_t* smem_bytes);
 
 #ifdef __cplusplus
 }

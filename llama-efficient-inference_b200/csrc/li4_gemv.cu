@@ -32,6 +32,7 @@
 //     group scale in fp32, and the 4 lanes of a row are reduced by warp
 //     shuffles.
 #include "li4_common.cuh"
+#include "li4_gemv_device.cuh"
 #include "li4_internal.h"
 
 #include <algorithm>
@@ -39,355 +40,6 @@
 #include <vector>
 
 namespace li4 {
-
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kMaxKsPerCta = 16;  // K range of one CTA <= 16 * 128 = 2048 (x staging)
-constexpr int kBatch = 4;         // ksteps one warp loads before it computes
-
-struct GemvArgs {
-  const __half* x;
-  const uint8_t* packed;
-  const __half* scale;
-  const __half* zero;
-  __half* y;
-  int M, N, K;
-  int log2_group;
-  long long sxm, spn, ssn, sym;  // strides: x, scale/zero, y in elements; packed in bytes
-  int n_tiles;                   // ceil(N / ROWS)
-  int split;                     // number of K ranges (grid.y)
-  int ks_per_split;              // ksteps per K range
-  float* partial;                // [split][M][N] fp32, split > 1 only
-  unsigned* counters;            // [n_tiles] arrival counters, split > 1 only
-  // li4_int4_linear_fused (zero / null otherwise)
-  const __half* norm_w;          // RMSNorm weight [K] applied while staging x
-  float norm_eps;
-  int epi;                       // li4_epilogue_kind
-  const __half* res;             // LI4_EPI_RESIDUAL
-  long long srm;
-  int q_rows, k_rows, head_dim;  // LI4_EPI_QKV_ROPE
-  const long long* pos;
-  const float* rope_cos;
-  const float* rope_sin;
-  long long rope_stride;
-  __half* q_out;
-  long long sqm;
-  __half* cache_k;
-  __half* cache_v;
-  long long cache_sb, cache_ss;
-  float* ssq_out;                // LI4_EPI_RESIDUAL: per 16-row tile, per row m, sum of the written values squared
-  const float* ssq_in;           // RMSNorm prologue: the producer's ssq_out, [ssq_tiles][M]
-  int ssq_tiles;
-};
-
-// ---------------------------------------------------------------------------
-// Fused epilogues.  Every GEMV output is rounded to fp16 first, as the
-// reference's fp16 Linear output is, and each later fp16 intermediate of the
-// reference is rounded again at the same point.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ bool epi_paired(const GemvArgs& a) {
-  return a.epi == LI4_EPI_SWIGLU || a.epi == LI4_EPI_QKV_ROPE;
-}
-
-// One output y[m, row] (LI4_EPI_STORE / LI4_EPI_RESIDUAL / LI4_EPI_STORE_F32); returns the value written.
-__device__ __forceinline__ float emit_one(const GemvArgs& a, int m, int row, float v) {
-  __half h = __float2half_rn(v);
-  if (a.epi == LI4_EPI_STORE_F32) {  // fp16 Linear output widened: logits = output(h).float() (llama/model.py:455)
-    reinterpret_cast<float*>(a.y)[(long long)m * a.sym + row] = __half2float(h);
-    return __half2float(h);
-  }
-  if (a.epi == LI4_EPI_RESIDUAL)  // h = x + wo(...): fp16 + fp16 (llama/model.py:358-362)
-    h = __float2half_rn(__half2float(h) + __half2float(a.res[(long long)m * a.srm + row]));
-  a.y[(long long)m * a.sym + row] = h;
-  return __half2float(h);
-}
-
-// Pair `pair` of a paired-row weight: v0 from tile row j, v1 from tile row j + 8.
-__device__ __forceinline__ void emit_pair(const GemvArgs& a, int m, int pair, float v0, float v1) {
-  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-  if (a.epi == LI4_EPI_SWIGLU) {  // F.silu(w1(x)) * w3(x) (llama/model.py:315)
-    const float g = __half2float(h0);
-    const float sg = __half2float(__float2half_rn(g / (1.0f + expf(-g))));
-    a.y[(long long)m * a.sym + pair] = __float2half_rn(sg * __half2float(h1));
-    return;
-  }
-  // LI4_EPI_QKV_ROPE: rows (2 pair, 2 pair + 1) of [q | k | v]
-  const int row = 2 * pair;
-  const long long p = *a.pos;
-  if (row < a.q_rows + a.k_rows) {  // (even, odd) as one complex number times e^{i pos f_i} (llama/model.py:126-152)
-    const int d = row < a.q_rows ? row : row - a.q_rows;
-    const int i = (d % a.head_dim) >> 1;
-    const float c = a.rope_cos[p * a.rope_stride + i], s = a.rope_sin[p * a.rope_stride + i];
-    const float x0 = __half2float(h0), x1 = __half2float(h1);
-    const __half2 o = __floats2half2_rn(x0 * c - x1 * s, x0 * s + x1 * c);
-    __half* dst = row < a.q_rows ? a.q_out + (long long)m * a.sqm + d
-                                 : a.cache_k + (long long)m * a.cache_sb + p * a.cache_ss + d;
-    *reinterpret_cast<__half2*>(dst) = o;
-  } else {  // v goes to the cache unrotated (llama/model.py:257-258)
-    const int d = row - a.q_rows - a.k_rows;
-    *reinterpret_cast<__half2*>(a.cache_v + (long long)m * a.cache_sb + p * a.cache_ss + d) = __halves2half2(h0, h1);
-  }
-}
-
-// The reduced outputs of one 16-row tile, value(r, m) for local row r, emitted
-// by threads tid = 0 .. nthr-1 of the caller's group.
-// value(r, m) of a tile reduced over the split-K partial sums (fixed order).
-struct PartialSum {
-  const float* base;  // partial + first row of the tile
-  int M;
-  long long N;
-  int split;
-  __device__ __forceinline__ float operator()(int r, int m) const {
-    float v = 0.f;
-    for (int sp = 0; sp < split; ++sp) v += __ldcg(&base[((long long)sp * M + m) * N + r]);
-    return v;
-  }
-};
-
-// value(r, m) of a tile reduced over the warps' partial tiles in shared memory.
-template <int COLS, int WARPS>
-struct WarpTileSum {
-  const float* rb;  // [warps][16][COLS]
-  __device__ __forceinline__ float operator()(int r, int m) const {
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) v += rb[(w * 16 + r) * COLS + m];
-    return v;
-  }
-};
-
-// Pull the residual rows a tile's epilogue will read into L1 while x is being staged, so the
-// epilogue's loads do not add an L2 round trip to the end of the launch.  Threads tid < M of
-// the group prefetch one 32-byte segment each (rows tile*16 .. +16 of row m).
-template <bool FUSED>
-__device__ __forceinline__ void prefetch_residual(const GemvArgs& a, int tile16, int tid) {
-  if (FUSED && a.epi == LI4_EPI_RESIDUAL && tid < a.M && tile16 >= 0 && tile16 * 16 < a.N)
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(a.res + (long long)tid * a.srm + tile16 * 16));
-}
-
-// One output through the epilogue (FUSED) or as a plain fp16 store.
-template <bool FUSED>
-__device__ __forceinline__ void emit_value(const GemvArgs& a, int m, int row, float v) {
-  if constexpr (FUSED) emit_one(a, m, row, v);
-  else a.y[(long long)m * a.sym + row] = __float2half_rn(v);
-}
-
-template <bool FUSED, typename F>
-__device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, int nthr, F value) {
-  const int row0 = tile * 16;
-  if (FUSED && a.ssq_out != nullptr) {
-    // (row m, tile row r) in half-warp groups of 16 rows: each group also leaves the sum of its
-    // written values squared for the next kernel's RMSNorm.  nthr is a multiple of 32 and the
-    // loop bound is uniform, so every lane reaches the shuffles.
-    const int rows = min(16, a.N - row0);
-    for (int base = 0; base < 16 * a.M; base += nthr) {
-      const int idx = base + tid, m = idx >> 4, r = idx & 15;
-      const bool live = idx < 16 * a.M;
-      float sq = 0.f;
-      if (live && r < rows) {
-        const float h = emit_one(a, m, row0 + r, value(r, m));
-        sq = h * h;
-      }
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-      if (live && r == 0) a.ssq_out[(long long)tile * a.M + m] = sq;
-    }
-    return;
-  }
-  if (FUSED && epi_paired(a)) {  // N is a multiple of 16: full tiles
-    for (int idx = tid; idx < 8 * a.M; idx += nthr) {
-      const int j = idx / a.M, m = idx - j * a.M;
-      emit_pair(a, m, tile * 8 + j, value(j, m), value(j + 8, m));
-    }
-  } else {
-    const int rows = min(16, a.N - row0);
-    for (int idx = tid; idx < rows * a.M; idx += nthr) {
-      const int r = idx / a.M, m = idx - r * a.M;
-      emit_value<FUSED>(a, m, row0 + r, value(r, m));
-    }
-  }
-}
-
-// Rows mode: a warp's 16-row tile `tile16` straight from its lanes' accumulators (lane (grp, quad)
-// holds rows grp and grp + 8, columns nt*8 + 2*quad + {0, 1}); split == 1.
-template <bool FUSED, int NT>
-__device__ __forceinline__ void emit_warp_tile(const GemvArgs& a, int tile16, const float (&acc)[NT][4], int grp,
-                                               int quad) {
-  const int row0 = tile16 * 16;
-  const int rows = min(16, a.N - row0);
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    if (FUSED && epi_paired(a)) {  // rows grp and grp + 8 of the tile are a pair
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = nt * 8 + 2 * quad + e;
-        if (m < a.M && row0 < a.N) emit_pair(a, m, tile16 * 8 + grp, acc[nt][e], acc[nt][e + 2]);
-      }
-      continue;
-    }
-    float sq[2] = {0.f, 0.f};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
-      if (r < rows && m < a.M) {
-        if constexpr (FUSED) {
-          const float h = emit_one(a, m, row0 + r, acc[nt][e]);
-          sq[e & 1] += h * h;
-        } else {
-          a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(acc[nt][e]);
-        }
-      }
-    }
-    if (FUSED && a.ssq_out != nullptr) {  // sum over the tile's rows: the 8 lanes of a quad column
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        sq[0] += __shfl_xor_sync(0xffffffffu, sq[0], o);
-        sq[1] += __shfl_xor_sync(0xffffffffu, sq[1], o);
-      }
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = nt * 8 + 2 * quad + e;
-        if (grp == 0 && m < a.M && row0 < a.N) a.ssq_out[(long long)tile16 * a.M + m] = sq[e];
-      }
-    }
-  }
-}
-
-// 1 / rms from the producer's per-tile sums of squares (fusion.sumsq_in): one warp per row.
-template <int WARPS>
-__device__ __forceinline__ void rms_from_ssq(const GemvArgs& a, float* s_rstd, int warp, int lane) {
-  for (int m = warp; m < a.M; m += WARPS) {
-    float ss = 0.f;
-    for (int t = lane; t < a.ssq_tiles; t += 32) ss += a.ssq_in[(long long)t * a.M + m];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) s_rstd[m] = rsqrtf(ss / (float)a.K + a.norm_eps);
-  }
-}
-
-// Per-row 1 / rms of x for the RMSNorm prologue: s_rstd[m] = rsqrt(mean_k x[m,k]^2 + eps),
-// the mean in fp32 over all K columns (llama/model.py:61).  One warp per row, 16-byte loads
-// unrolled so a row's loads are in flight together; the caller synchronises before use.
-template <int WARPS>
-__device__ __forceinline__ void rms_factors(const GemvArgs& a, float* s_rstd, int warp, int lane) {
-  const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
-#pragma unroll 2
-  for (int m = warp; m < a.M; m += WARPS) {
-    const __half* row = a.x + (long long)m * a.sxm;
-    float ss = 0.f;
-    if (vec) {
-      const uint4* r4 = reinterpret_cast<const uint4*>(row);
-      const int n4 = a.K >> 3;
-#pragma unroll 4
-      for (int c = lane; c < n4; c += 32) {
-        const uint4 u = r4[c];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-          ss = fmaf(f.x, f.x, ss);
-          ss = fmaf(f.y, f.y, ss);
-        }
-      }
-    } else {
-      for (int k = lane; k < a.K; k += 32) {
-        const float v = __half2float(row[k]);
-        ss = fmaf(v, v, ss);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) s_rstd[m] = rsqrtf(ss / (float)a.K + a.norm_eps);
-  }
-}
-
-// fp16(fp16(x * rstd) * w): RMSNorm's output cast (type_as) and its fp16 weight product.
-// The fp16 x fp16 product is exact before its one rounding, so the half2 multiply gives the same
-// bits as the reference's float multiply rounded to fp16.
-__device__ __forceinline__ uint32_t norm_pair(uint32_t xv, uint32_t wv, float rstd) {
-  const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xv));
-  const __half2 n = __floats2half2_rn(xf.x * rstd, xf.y * rstd);
-  const __half2 o = __hmul2(n, *reinterpret_cast<const __half2*>(&wv));
-  return *reinterpret_cast<const uint32_t*>(&o);
-}
-
-// ---------------------------------------------------------------------------
-// x staging.  Block b = ((ks * NT + nt) * M8 + m8) * 4 + quad holds the 32
-// values x[m][k0 .. k0+32), m = nt*8 + m8, k0 = kstep*128 + 32*quad, as 16
-// half2 words; word 4w + i = (x[k0 + 8w + i], x[k0 + 8w + i + 4]).  Chunk w
-// (16 bytes) of block b sits at b*64 + ((w ^ key) << 4) with
-// key = (2*m8 + (quad >> 1)) & 3, which keeps the 128-bit reads of 8
-// consecutive blocks on distinct banks and does not depend on the kstep (so a
-// reader can precompute its offsets).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ int xs_key(int m8, int quad) { return (2 * m8 + (quad >> 1)) & 3; }
-
-// block = ((kstep * NT + nt) * M8 + m8) * 4 + quad
-__device__ __forceinline__ int xs_chunk_offset(int block, int w, int m8) {
-  return block * 64 + ((w ^ xs_key(m8, block & 3)) << 4);
-}
-
-__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-
-// The same load as an ordered instruction: loop-invariant B fragments stay in
-// shared memory instead of being hoisted into registers across tiles.
-__device__ __forceinline__ uint4 lds128_ordered(const uint8_t* p) {
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "r"((uint32_t)__cvta_generic_to_shared(p)));
-  return r;
-}
-
-// s_rstd: per-row RMSNorm factors (rms_factors) when a.norm_w is set, else unused.
-template <int NT, int THREADS = kThreads, bool NORM = false>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
-                                        const float* s_rstd = nullptr) {
-  // One thread per 16-byte k-chunk (k = 8 values) and every row of it: the RMSNorm weight chunk
-  // is read once, and the rows' loads are independent, so they are in flight together.
-  const int chunks = nks * 16;
-  const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
-  for (int c = threadIdx.x; c < chunks; c += THREADS) {
-    const int ks = c >> 4, quad = (c >> 2) & 3, w = c & 3;
-    const long long k = (long long)(ks0 + ks) * 128 + 32 * quad + 8 * w;
-    uint4 wn = make_uint4(0u, 0u, 0u, 0u);
-    if (NORM && a.norm_w != nullptr) wn = *reinterpret_cast<const uint4*>(a.norm_w + k);  // 16-byte aligned
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-      for (int m8 = 0; m8 < 8; ++m8) {
-        if (m8 >= M8) break;
-        const int m = nt * 8 + m8;
-        const int block = ((ks * NT + nt) * M8 + m8) * 4 + quad;
-        uint4 out = make_uint4(0u, 0u, 0u, 0u);
-        if (m < a.M) {
-          const __half* src = a.x + (long long)m * a.sxm + k;
-          uint32_t u[4];
-          if (vec_ok) {
-            const uint4 v = *reinterpret_cast<const uint4*>(src);
-            u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
-          }
-          if (NORM && a.norm_w != nullptr) {
-            const float r = s_rstd[m];
-            u[0] = norm_pair(u[0], wn.x, r);
-            u[1] = norm_pair(u[1], wn.y, r);
-            u[2] = norm_pair(u[2], wn.z, r);
-            u[3] = norm_pair(u[3], wn.w, r);
-          }
-          out.x = __byte_perm(u[0], u[2], 0x5410);  // (x0, x4)
-          out.y = __byte_perm(u[0], u[2], 0x7632);  // (x1, x5)
-          out.z = __byte_perm(u[1], u[3], 0x5410);  // (x2, x6)
-          out.w = __byte_perm(u[1], u[3], 0x7632);  // (x3, x7)
-        }
-        *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8)) = out;
-      }
-    }
-  }
-}
 
 // Start pulling the first row tile's weight bytes into L2 (TMA bulk prefetch)
 // before waiting on the preceding kernel.
@@ -776,11 +428,6 @@ constexpr int kStreamWarps = 8;
 constexpr int kStreamThreads = kStreamWarps * 32;
 constexpr int kStreamDepth = 5;
 
-struct StreamUnit {
-  uint4 lo, hi;          // bytes [16 quad, +16) of the kstep for rows grp and grp + 8
-  uint32_t sz_lo, sz_hi; // fp16 bits: scale | zero << 16, for the two rows
-};
-
 // Per-warp walk over (tile, kstep) units.
 struct StreamCursor {
   int tile;   // current tile (>= n_tiles: done)
@@ -833,42 +480,6 @@ __device__ __forceinline__ void stream_load(const GemvArgs& a, StreamUnit& u, co
   const int g = (ks * 128) >> a.log2_group;
   u.sz_lo = ldg_u16(r.s_lo + g) | (ldg_u16(r.z_lo + g) << 16);
   u.sz_hi = ldg_u16(r.s_hi + g) | (ldg_u16(r.z_hi + g) << 16);
-}
-
-// acc += s * (W[rows] . x) for one unit.  xs_ks: the unit's kstep in the x
-// staging; n-tile nt of it starts nt * nt_stride bytes further.
-template <int NT>
-__device__ __forceinline__ void stream_compute(const StreamUnit& u, const uint8_t* xs_ks, int nt_stride,
-                                               const int boff[4], bool bvalid, float acc[NT][4]) {
-  const ZeroConsts zl = make_zero_consts(__ushort_as_half((unsigned short)(u.sz_lo >> 16)));
-  const ZeroConsts zh = make_zero_consts(__ushort_as_half((unsigned short)(u.sz_hi >> 16)));
-  float c[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) c[nt][e] = 0.f;
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    __half2 pl[4], ph[4];
-    unpack8_qz((w == 0) ? u.lo.x : (w == 1) ? u.lo.y : (w == 2) ? u.lo.z : u.lo.w, zl, pl);
-    unpack8_qz((w == 0) ? u.hi.x : (w == 1) ? u.hi.y : (w == 2) ? u.hi.z : u.hi.w, zh, ph);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      uint4 bq = make_uint4(0u, 0u, 0u, 0u);
-      if (bvalid) bq = lds128(xs_ks + nt * nt_stride + boff[w]);
-      mma_16816(c[nt], h2_as_u32(pl[0]), h2_as_u32(ph[0]), h2_as_u32(pl[1]), h2_as_u32(ph[1]), bq.x, bq.y);
-      mma_16816(c[nt], h2_as_u32(pl[2]), h2_as_u32(ph[2]), h2_as_u32(pl[3]), h2_as_u32(ph[3]), bq.z, bq.w);
-    }
-  }
-  const float sl = __half2float(__ushort_as_half((unsigned short)(u.sz_lo & 0xFFFFu)));
-  const float sh = __half2float(__ushort_as_half((unsigned short)(u.sz_hi & 0xFFFFu)));
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    acc[nt][0] = fmaf(sl, c[nt][0], acc[nt][0]);
-    acc[nt][1] = fmaf(sl, c[nt][1], acc[nt][1]);
-    acc[nt][2] = fmaf(sh, c[nt][2], acc[nt][2]);
-    acc[nt][3] = fmaf(sh, c[nt][3], acc[nt][3]);
-  }
 }
 
 template <int NT, bool KSPLIT, bool FUSED>
@@ -1249,73 +860,6 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
 __host__ __device__ constexpr int bulk_consumer_warps(int nt) { return nt == 1 ? 10 : 8; }
 __host__ __device__ constexpr int bulk_threads(int nt) { return (bulk_consumer_warps(nt) + 1) * 32; }  // + producer
 constexpr int kBulkMaxStages = 10;  // = bulk_consumer_warps(1)
-constexpr unsigned kBulkWaitLimit = 1u << 22;  // try_wait rounds: well under a second of polling, never forever
-
-__device__ unsigned g_li4_device_error;  // bit 0: a bounded pipeline wait ran out
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Wait for phase `parity` of `bar` to complete, at most kBulkWaitLimit rounds.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (unsigned i = 0; i < kBulkWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  atomicOr(&g_li4_device_error, 1u);
-  return false;
-}
-
-// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// Shared-memory layout of one stage: 16 packed rows of K-range/2 bytes, then
-// 16 scale rows and 16 zero rows of KS fp16 values.  When the tile's rows are
-// one contiguous block of HBM (contiguous tensors, one K range) a stage is
-// three bulk copies and the rows sit back to back; otherwise each row is its
-// own copy and the row pitch is K-range/2 + 64, which keeps the 16-byte reads
-// of the eight row pairs of a quarter warp on distinct banks.
-struct BulkLayout {
-  int ks;       // ksteps per K range (8 or 16)
-  int pitch;    // bytes between packed rows
-  int sz_off;   // scale rows, then zero rows at + 16 * ks * 2
-  int stage;    // bytes per stage (multiple of 128)
-};
-
-__host__ __device__ inline BulkLayout bulk_layout(int ks, bool contig) {
-  BulkLayout L;
-  L.ks = ks;
-  L.pitch = ks * 64 + (contig ? 0 : 64);
-  L.sz_off = 16 * L.pitch;
-  L.stage = (L.sz_off + 2 * 16 * ks * 2 + 127) & ~127;
-  return L;
-}
-
 template <int NT, bool FUSED>
 __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs a, int stages,
                                                                         int contig) {
@@ -1914,20 +1458,15 @@ static int check_fusion(const li4_fusion& f, int64_t M, int64_t N, int64_t K) {
   }
 }
 
-static int int4_linear_impl(const void* x, const void* packed, const void* scale, const void* zero, void* y,
-                            int64_t M, int64_t N, int64_t K, int64_t group, int64_t sxm, int64_t spn, int64_t ssn,
-                            int64_t sym, void* workspace, size_t workspace_bytes, void* stream, int kernel,
-                            int rows_req, int split_req, int max_ctas, const li4_fusion* f = nullptr) {
-  Plan p = {};
-  const int sm = current_sm_count();
+int prepare_linear(const void* x, const void* packed, const void* scale, const void* zero, void* y, int64_t M,
+                   int64_t N, int64_t K, int64_t group, int64_t sxm, int64_t spn, int64_t ssn, int64_t sym,
+                   const li4_fusion* f, GemvArgs* out) {
   const bool fused = f != nullptr && (f->norm_weight != nullptr || f->epilogue != LI4_EPI_STORE);
-  int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p, fused);
-  if (rc != LI4_OK) return rc;
   const int epi = f ? f->epilogue : LI4_EPI_STORE;
   // columns of y: N, N/2 for SwiGLU pairs, none for the QKV epilogue (outputs go to q_out and the cache)
   const int64_t y_cols = epi == LI4_EPI_SWIGLU ? N / 2 : (epi == LI4_EPI_QKV_ROPE ? 0 : N);
   if (fused) {
-    rc = check_fusion(*f, M, N, K);
+    const int rc = check_fusion(*f, M, N, K);
     if (rc != LI4_OK) return rc;
   }
   if (!x || !packed || !scale || !zero || (!y && y_cols > 0))
@@ -1943,28 +1482,6 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     return set_error(LI4_ERR_ALIGNMENT, "int4_linear: fp16 tensors must be 2-byte aligned");
   if (epi == LI4_EPI_STORE_F32 && (reinterpret_cast<uintptr_t>(y) & 3u))
     return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: an fp32 output must be 4-byte aligned");
-  if (p.kernel == LI4_KERNEL_TILE && ((N - 1) * spn + K / 2 > (int64_t)UINT32_MAX ||
-                                      (N - 1) * ssn + K / group > (int64_t)UINT32_MAX)) {
-    // the tile kernel addresses rows with 32-bit offsets
-    if (kernel != LI4_KERNEL_AUTO)
-      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: the tile kernel needs packed / scale offsets below 2^32");
-    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
-    if (rc != LI4_OK) return rc;
-  }
-  if (p.kernel == LI4_KERNEL_BULK && (!aligned16(scale) || !aligned16(zero) || ssn % 8 != 0)) {
-    // the scale / zero rows move as 16-byte-aligned bulk copies
-    if (kernel != LI4_KERNEL_AUTO)
-      return set_error(LI4_ERR_ALIGNMENT, "int4_linear: the bulk-copy kernel needs 16-byte aligned scale / zero "
-                       "rows (row stride %% 8 == 0)");
-    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
-    if (rc != LI4_OK) return rc;
-  }
-  if (p.ws_bytes > 0) {
-    if (!workspace || workspace_bytes < p.ws_bytes)
-      return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "
-                       "workspace, got %zu", p.split, p.ws_bytes, workspace ? workspace_bytes : (size_t)0);
-    if (!aligned16(workspace)) return set_error(LI4_ERR_ALIGNMENT, "int4_linear: workspace must be 16-byte aligned");
-  }
   GemvArgs args = {};
   if (fused) {
     args.norm_w = static_cast<const __half*>(f->norm_weight);
@@ -2002,6 +1519,44 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
   args.spn = spn;
   args.ssn = ssn;
   args.sym = sym;
+  *out = args;
+  return LI4_OK;
+}
+
+static int int4_linear_impl(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                            int64_t M, int64_t N, int64_t K, int64_t group, int64_t sxm, int64_t spn, int64_t ssn,
+                            int64_t sym, void* workspace, size_t workspace_bytes, void* stream, int kernel,
+                            int rows_req, int split_req, int max_ctas, const li4_fusion* f = nullptr) {
+  Plan p = {};
+  const int sm = current_sm_count();
+  const bool fused = f != nullptr && (f->norm_weight != nullptr || f->epilogue != LI4_EPI_STORE);
+  int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p, fused);
+  if (rc != LI4_OK) return rc;
+  GemvArgs args = {};
+  rc = prepare_linear(x, packed, scale, zero, y, M, N, K, group, sxm, spn, ssn, sym, f, &args);
+  if (rc != LI4_OK) return rc;
+  if (p.kernel == LI4_KERNEL_TILE && ((N - 1) * spn + K / 2 > (int64_t)UINT32_MAX ||
+                                      (N - 1) * ssn + K / group > (int64_t)UINT32_MAX)) {
+    // the tile kernel addresses rows with 32-bit offsets
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: the tile kernel needs packed / scale offsets below 2^32");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
+  if (p.kernel == LI4_KERNEL_BULK && (!aligned16(scale) || !aligned16(zero) || ssn % 8 != 0)) {
+    // the scale / zero rows move as 16-byte-aligned bulk copies
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_ALIGNMENT, "int4_linear: the bulk-copy kernel needs 16-byte aligned scale / zero "
+                       "rows (row stride %% 8 == 0)");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
+  if (p.ws_bytes > 0) {
+    if (!workspace || workspace_bytes < p.ws_bytes)
+      return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "
+                       "workspace, got %zu", p.split, p.ws_bytes, workspace ? workspace_bytes : (size_t)0);
+    if (!aligned16(workspace)) return set_error(LI4_ERR_ALIGNMENT, "int4_linear: workspace must be 16-byte aligned");
+  }
   args.n_tiles = p.n_tiles;
   args.split = p.split;
   args.ks_per_split = p.ks_per_split;
@@ -2056,6 +1611,9 @@ extern "C" int li4_device_errors(unsigned* flags, int reset) {
   unsigned comm = 0;
   if (rc == LI4_OK) rc = li4::comm_device_errors(&comm, reset != 0);
   if (rc == LI4_OK) *flags |= comm;
+  unsigned prog = 0;
+  if (rc == LI4_OK) rc = li4::program_device_errors(&prog, reset != 0);
+  if (rc == LI4_OK) *flags |= prog;
   if (rc == LI4_OK) li4::clear_error();
   return rc;
 }

@@ -19,6 +19,8 @@ int check_cuda(cudaError_t err, const char* what);
 int current_sm_count();
 // Device error word of the communication kernels (li4_comm.cu); reset clears it.
 int comm_device_errors(unsigned* flags, bool reset);
+// Device error words of the decode program kernel (li4_program.cu); reset clears them.
+int program_device_errors(unsigned* flags, bool reset);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }

@@ -82,6 +82,19 @@ SIGNATURES = {
     "li4_ipc_open_handle": (_INT, [_P, ctypes.POINTER(_P)]),
     "li4_ipc_close": (_INT, [_P]),
     "li4_allreduce_add": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _INT, _INT, _INT, _I64, _P, _P, _P]),
+    "li4_program_create": (_INT, [ctypes.POINTER(_P)]),
+    "li4_program_destroy": (_INT, [_P]),
+    "li4_program_add_linear": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                      ctypes.POINTER(Fusion), _INT, ctypes.POINTER(_INT)]),
+    "li4_program_add_attention": (_INT, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P,
+                                         _I64, _INT, ctypes.POINTER(_INT)]),
+    "li4_program_add_gather": (_INT, [_P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _INT, ctypes.POINTER(_INT)]),
+    "li4_program_add_argmax": (_INT, [_P, _P, _I64, _I64, _I64, _P, _I64, _INT, ctypes.POINTER(_INT)]),
+    "li4_program_add_increment": (_INT, [_P, _P]),
+    "li4_program_finalize": (_INT, [_P]),
+    "li4_program_launch": (_INT, [_P, _P]),
+    "li4_program_set_trace": (_INT, [_P, _P, _I64]),
+    "li4_program_info": (_INT, [_P, ctypes.POINTER(_INT), ctypes.POINTER(_INT), ctypes.POINTER(_SZ)]),
     "li4_dequantize": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_quantize": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
 }

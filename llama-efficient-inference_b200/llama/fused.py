@@ -154,9 +154,13 @@ class FusedDecoder:
     step serves every position.
     """
 
-    def __init__(self, model, nvlink_allreduce: bool = True):
+    def __init__(self, model, nvlink_allreduce: bool = True, program: bool = False):
         self.model = model
         self.nvlink_allreduce = nvlink_allreduce
+        # single GPU: the whole step as one persistent launch (llama.program) where it applies
+        self.use_program = program
+        self._programs = {}
+        self.last_path = None  # "program" or "launches": how the last decode_step ran
         self._ar = None  # NvlinkAllReduce of the model's TP group, built on first use
         p = model.params
         emb = model.tok_embeddings.weight
@@ -218,11 +222,80 @@ class FusedDecoder:
             int4_linear_fused(x, *w, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
             self._allreduce_add(part, residual, out, group)
 
+    def _staging(self, bs: int):
+        """Decoder-owned token / position buffers of the staged program (see _program)."""
+        key = ("staging", bs)
+        b = self._bufs.get(key)
+        if b is None:
+            i64 = dict(dtype=torch.long, device=self.device)
+            b = {"tok": torch.zeros(bs, 1, **i64), "pos": torch.zeros(1, **i64), "out": torch.zeros(bs, 1, **i64)}
+            self._bufs[key] = b
+        return b
+
+    def _program(self, tokens: torch.Tensor, pos: torch.Tensor, next_tokens: Optional[torch.Tensor],
+                 advance_pos: bool):
+        """(program, direct): the cached one-launch program of this step, built on first use (outside
+        graph capture), or None where it does not apply (tensor parallelism, shapes it does not take).
+
+        direct: the caller feeds the greedy tokens back in place (next_tokens is tokens, as
+        DecodeGraph does), so the program reads tokens and pos and writes the next tokens and
+        pos + 1 itself.  Otherwise (fresh tensors each step) one program per batch size reads
+        decoder-owned buffers that decode_step fills with two small copies."""
+        if not self.use_program or self.model.tp_group is not None:
+            return None, False
+        bs = tokens.shape[0]
+        for blk in self.blocks:
+            blk.att._ensure_cache(self._buffers(bs)["h"])
+        caches = tuple(b.att.cache_k.data_ptr() for b in self.blocks)
+        direct = next_tokens is not None and next_tokens.data_ptr() == tokens.data_ptr()
+        key = ("direct", bs, tokens.data_ptr(), pos.data_ptr(), advance_pos, caches) if direct \
+            else ("staged", bs, caches)
+        if key in self._programs:
+            return self._programs[key], direct
+        from .program import decode_step_program
+
+        try:
+            if direct:
+                prog = decode_step_program(self, tokens, pos, next_tokens, advance_pos)
+            else:
+                st = self._staging(bs)
+                prog = decode_step_program(self, st["tok"], st["pos"], st["out"], False)
+        except native.Li4Error as e:
+            if e.status != native.LI4_ERR_UNSUPPORTED:
+                raise
+            prog = None  # e.g. a context longer than the program's attention holds: per-launch kernels
+        self._programs[key] = prog
+        return prog, direct
+
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor,
-                    next_tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    next_tokens: Optional[torch.Tensor] = None, advance_pos: bool = False) -> torch.Tensor:
         """fp32 logits [bs, 1, vocab]; with next_tokens (int64 [bs, 1], may be `tokens`) also
-        the greedy argmax of each row, written on the GPU."""
+        the greedy argmax of each row, written on the GPU; with advance_pos, pos += 1 after the step."""
+        bs = tokens.shape[0]
+        prog, direct = self._program(tokens, pos, next_tokens, advance_pos)
+        if prog is not None:
+            if not direct:
+                st = self._staging(bs)
+                st["tok"].copy_(tokens.view(bs, 1))
+                st["pos"].copy_(pos.view(1))
+            prog.launch(native.stream_ptr(self.device))
+            if not direct:
+                if next_tokens is not None:
+                    next_tokens.view(bs, 1).copy_(st["out"])
+                if advance_pos:
+                    pos.add_(1)
+            self.last_path = "program"
+            return self._buffers(bs)["logits"].view(bs, 1, -1)
+        self.last_path = "launches"
+        logits = self._decode_launches(tokens, pos, next_tokens)
+        if advance_pos:
+            pos.add_(1)
+        return logits
+
+    def _decode_launches(self, tokens: torch.Tensor, pos: torch.Tensor,
+                         next_tokens: Optional[torch.Tensor]) -> torch.Tensor:
+        """The step as five launches per block (and the tensor-parallel path)."""
         bs = tokens.shape[0]
         buf = self._buffers(bs)
         h, h1, q, attn, ffn, part = buf["h"], buf["h1"], buf["q"], buf["attn"], buf["ffn"], buf["part"]

@@ -45,11 +45,10 @@ class DecodeGraph:
 
     def _step(self):
         fused = getattr(self.model, "_fused", None)
-        if fused is not None:  # fused step: the greedy argmax runs in li4_argmax_rows
-            logits = fused.decode_step(self.tok, self.pos, next_tokens=self.tok)
-        else:
-            logits = self.model.decode_step(self.tok, self.pos)
-            self.tok.copy_(logits[:, -1].argmax(-1, keepdim=True))
+        if fused is not None:  # fused step: the greedy argmax and pos += 1 run on the GPU kernels
+            return fused.decode_step(self.tok, self.pos, next_tokens=self.tok, advance_pos=True)
+        logits = self.model.decode_step(self.tok, self.pos)
+        self.tok.copy_(logits[:, -1].argmax(-1, keepdim=True))
         self.pos.add_(1)
         return logits
 

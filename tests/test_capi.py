@@ -147,3 +147,46 @@ def test_allreduce_validates(native):
     assert lib.li4_allreduce_add(arr, arr, 16, 16, 2, 2, 64, 16, 16, None) == native.LI4_ERR_INVALID_ARG  # rank
     odd = (ctypes.c_void_p * 2)(18, 16)
     assert lib.li4_allreduce_add(odd, arr, 16, 16, 2, 0, 64, 16, 16, None) == native.LI4_ERR_ALIGNMENT
+
+
+def test_program_builder_validates(native):
+    """Decode-program ops are checked when they are added (no GPU needed); launching an
+    unfinalized program is refused."""
+    import ctypes
+
+    lib = native.lib()
+    h = ctypes.c_void_p()
+    assert lib.li4_program_create(ctypes.byref(h)) == native.LI4_OK
+    idx = ctypes.c_int(-7)
+    try:
+        def lin(M=1, N=2048, K=2048, group=128, ps=1024, ss=16, scale=256, wait=-1):
+            return lib.li4_program_add_linear(h, 256, 256, scale, 256, 256, M, N, K, group, K, ps, ss, N, None, wait,
+                                              ctypes.byref(idx))
+
+        assert lin() == native.LI4_OK and idx.value == 0
+        assert lin(wait=0) == native.LI4_OK and idx.value == 1
+        assert lin(wait=5) == native.LI4_ERR_INVALID_ARG          # waits for a later op
+        assert lin(M=17) == native.LI4_ERR_UNSUPPORTED
+        assert lin(N=8) == native.LI4_ERR_UNSUPPORTED             # fewer rows than a tile
+        assert lin(K=3072, ps=1536, ss=24) == native.LI4_ERR_UNSUPPORTED  # K > 2048 not a multiple of 2048
+        assert lin(group=64, ss=32) == native.LI4_ERR_UNSUPPORTED
+        assert lin(scale=264) == native.LI4_ERR_ALIGNMENT         # scale rows off 16 bytes
+        assert lin(K=512, ps=512, ss=8) == native.LI4_ERR_ALIGNMENT  # strided rows of K < 1024
+        assert lin(K=8192, ps=4096, ss=64) == native.LI4_OK       # K ranges of 2048
+        # attention: head_dim 48, rep 3, a context too long for the CTA's shared memory
+        att = lib.li4_program_add_attention
+        assert att(h, 256, 256, 256, 256, 64 * 256, 256, 256, 256, 1, 4, 1, 48, 256, 64, -1, None) == \
+            native.LI4_ERR_UNSUPPORTED
+        assert att(h, 256, 384, 256, 256, 64 * 128, 128, 256, 384, 1, 6, 2, 64, 256, 64, -1, None) == \
+            native.LI4_ERR_UNSUPPORTED
+        assert att(h, 256, 2048, 256, 256, 100000 * 512, 512, 256, 2048, 1, 32, 8, 64, 256, 100000, -1, None) == \
+            native.LI4_ERR_UNSUPPORTED
+        assert att(h, 256, 2048, 256, 256, 640 * 512, 512, 256, 2048, 1, 32, 8, 64, 256, 640, 1,
+                   ctypes.byref(idx)) == native.LI4_OK
+        assert lib.li4_program_add_gather(h, 256, 1000, 2044, 2044, 256, 1, 256, 2044, -1, None) == \
+            native.LI4_ERR_INVALID_ARG                             # rows of cols % 8 != 0
+        assert lib.li4_program_add_argmax(h, 256, 2, 1000, 999, 256, 1, -1, None) == native.LI4_ERR_INVALID_ARG
+        assert lib.li4_program_add_increment(h, 260) == native.LI4_ERR_ALIGNMENT
+        assert lib.li4_program_launch(h, None) == native.LI4_ERR_INVALID_ARG  # not finalized
+    finally:
+        assert lib.li4_program_destroy(h) == native.LI4_OK
