@@ -433,6 +433,86 @@ def size_floor(a):
         torch.cuda.empty_cache()
 
 
+def program_report(a):
+    """--program-report: the decode program (llama.program) on the decode workloads.  (1) the 113
+    GEMVs of the step at M = 1 and 16 as one program of independent ops, and the lm_head alone;
+    (2) the Llama-3.2-1B decode step as one program at bs 1 and 16 (512-token context): launch
+    time and, from one traced launch, per op kind the mean of: poll (last CTA of the previous op
+    done -> median CTA past its wait), stage (x staging), work (wait -> units done, median CTA),
+    tail (median -> last CTA done) and span (previous op done -> this op done), in µs."""
+    from llama import fused as F_
+    from llama import program as P_
+
+    dev = torch.device("cuda", 0)
+
+    def timeit(fn, n=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n * 1e3
+
+    for M in (1, 16):
+        st = Stream(dev, M)
+        prog = P_.Program()
+        for x, (p, s, z), y in zip(st.xs, st.weights, st.ys):
+            prog.linear(x, p, s, z, y)
+        prog.finalize()
+        us = timeit(prog.launch)
+        lm = P_.Program()
+        lm.linear(st.xs[-1], *st.weights[-1], st.ys[-1])
+        lm.finalize()
+        us_lm = timeit(lm.launch)
+        print(json.dumps({"program": "gemv_list", "M": M, "ops": prog.n_ops, "us": round(us, 1),
+                          "GBps": round(st.bytes_per_step / us / 1e3, 1), "lm_head_us": round(us_lm, 1),
+                          "lm_head_GBps": round(gemv_bytes(*LM_HEAD[1:], M) / us_lm / 1e3, 1), **prog.info()}),
+              flush=True)
+        del st, prog, lm
+        torch.cuda.empty_cache()
+    names = ["gather"] + ["qkv", "attention", "wo", "gate_up", "down"] * N_LAYERS + ["lm_head", "argmax"]
+    for bs in (1, 16):
+        model = build_decode_model(dev, bs, 640)
+        dec = F_.FusedDecoder(model, program=True)
+        tok = torch.randint(0, model.params.vocab_size, (bs, 1), device=dev)
+        pos = torch.tensor([512], dtype=torch.long, device=dev)
+        dec.decode_step(tok, pos, next_tokens=tok)
+        prog = [p for p in dec._programs.values() if p is not None][0]
+        info = prog.info()
+        G, n = info["ctas"], info["ops"]
+        us = timeit(prog.launch)
+        stamps = torch.zeros(n, G, 4, dtype=torch.long, device=dev)
+        prog.set_trace(stamps)
+        prog.launch()
+        torch.cuda.synchronize(dev)
+        prog.set_trace(None)
+        s = stamps.cpu().numpy()
+        t0 = s[s > 0].min()
+        agg, prev_end = {}, None
+        for j in range(n):
+            act = s[j][:, 0] > 0
+            if not act.any():
+                continue
+            r = s[j][act] - t0
+            end = r[:, 3].max()
+            staged = r[:, 2] > 0
+            d = {"poll": (statistics.median(r[:, 1]) - prev_end) if prev_end is not None else 0.0,
+                 "stage": statistics.median(r[staged, 2] - r[staged, 1]) if staged.any() else 0.0,
+                 "work": statistics.median(r[:, 3] - r[:, 1]), "tail": end - statistics.median(r[:, 3]),
+                 "span": end - (prev_end if prev_end is not None else r[:, 0].min())}
+            agg.setdefault(names[j] if j < len(names) else str(j), []).append(d)
+            prev_end = end
+        ops = {k: {q: round(float(statistics.mean(x[q] for x in v)) / 1e3, 2) for q in v[0]} for k, v in agg.items()}
+        print(json.dumps({"program": "decode_step", "bs": bs, "launch_us": round(us, 1), **info, "per_op_us": ops}),
+              flush=True)
+        del dec, model, prog
+        torch.cuda.empty_cache()
+
+
 def fused_cost(a):
     """--fused-cost: each fused decode GEMV (llama.fused) against the same GEMV without its prologue /
     epilogue, µs per launch in a CUDA graph of back-to-back launches over rotating weight copies."""
@@ -849,6 +929,8 @@ def main():
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
     ap.add_argument("--sweep", action="store_true", help="kernel-family x launch-shape sweep of the decode shapes")
+    ap.add_argument("--program-report", action="store_true",
+                    help="the decode program (one persistent launch): GEMV-list and decode-step timings, per-op trace")
     ap.add_argument("--fused-cost", action="store_true",
                     help="each fused decode GEMV against the same GEMV without its prologue / epilogue")
     ap.add_argument("--size-floor", action="store_true",
@@ -867,6 +949,9 @@ def main():
         return
     if a.fused_cost:
         fused_cost(a)
+        return
+    if a.program_report:
+        program_report(a)
         return
     if a.warmup < 3:
         a.warmup = 3
