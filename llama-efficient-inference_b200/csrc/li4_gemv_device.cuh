@@ -438,11 +438,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
   return false;
 }
 
-// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`; the weight
+// bytes it moves are marked evict-first in L2 (weight_l2_policy).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(weight_l2_policy())
       : "memory");
 }
 
