@@ -208,7 +208,10 @@ int li4_int4_linear_fused(const void* x, const void* packed, const void* scale, 
  * head_dim] (row stride stride_qb); cache_k / cache_v: fp16 [batch, seq,
  * n_kv_heads, head_dim] with element strides cache_stride_b / cache_stride_s;
  * out: fp16 [batch, n_heads * head_dim] (row stride stride_ob).  head_dim 32, 64 or 128;
- * *pos < max_seq (the kernel clamps to max_seq - 1).
+ * *pos < max_seq (the kernel clamps to max_seq - 1).  Launched with programmatic
+ * dependent launch: q and cache row *pos may come from the preceding kernel on the
+ * stream, but the rows before *pos are read while that kernel may still run, so
+ * they must have been written before it (as a decode step's earlier positions are).
  * Replaces: Attention.forward's repeat_kv, two matmuls and softmax
  * (llama/model.py:262-275) at seqlen 1. */
 int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, const void* cache_v,

@@ -69,6 +69,7 @@ struct AttnArgs {
   const long long* pos;
   int max_seq;
   int chunk_max;  // keys per CTA at most: ceil(max_seq / cluster size)
+  int red_in_k;   // STAGE: the warps' P.V partials reuse the key staging (free once the scores are in)
 };
 
 // STAGE: the CTA's keys and values are first copied into shared memory with cp.async (all of
@@ -80,26 +81,49 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   constexpr int CPR = HD / 8;   // 16-byte chunks per cached row
   constexpr int SWZ = (CPR < 8 ? CPR : 8) - 1;
   extern __shared__ __align__(16) float smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();   // CTAs sharing this (KV head, sequence)
+  const int c = (int)cluster.block_rank();
   float* q_s = smem;                         // [REP][HD]
-  float* red = q_s + REP * HD;               // [warps][REP][HD]
-  float* part = red + kAttnWarps * REP * HD; // [cluster][REP][HD] partial P.V (collected in the first CTA)
-  float* scores = part + 8 * REP * HD;       // [REP][chunk_max]
+  float* part = q_s + REP * HD;              // [S][REP][HD] partial P.V (collected in the first CTA)
+  float* scores = part + S * REP * HD;       // [REP][chunk_max]
   // STAGE: [chunk_max][HD] keys (swizzled), then values, from the next 16-byte boundary (cp.async targets)
   __half* k_s = reinterpret_cast<__half*>((reinterpret_cast<uintptr_t>(scores + REP * a.chunk_max) + 15) & ~uintptr_t(15));
   __half* v_s = k_s + (size_t)a.chunk_max * HD;                         // STAGE: [chunk_max][HD]
+  // [warps][REP][HD]: in the key staging when it is large enough, else after the staging / scores
+  float* red = a.red_in_k ? reinterpret_cast<float*>(k_s)
+                          : reinterpret_cast<float*>(STAGE ? reinterpret_cast<uintptr_t>(v_s + (size_t)a.chunk_max * HD)
+                                                           : reinterpret_cast<uintptr_t>(k_s));
   __shared__ float s_wmax[kAttnWarps][REP], s_wsum[kAttnWarps][REP];
   __shared__ float s_lmax[REP], s_gmax[REP], s_gsum[REP];
   __shared__ float s_cm[8][REP], s_cl[8][REP];  // (max, sum) of every CTA of the cluster, pushed by each
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const int S = (int)cluster.num_blocks();   // CTAs sharing this (KV head, sequence)
-  const int c = (int)cluster.block_rank();
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * HD;
+  const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * HD;
+  auto stage_rows = [&](int r0, int r1, int j0) {  // cache rows [r0, r1) into their staging slots (row j0 first)
+    for (int idx = tid; idx < (r1 - r0) * CPR; idx += kAttnThreads) {
+      const int jj = r0 - j0 + idx / CPR, cc = idx % CPR;
+      cp_async16(k_s + jj * HD + ((cc ^ (jj & SWZ)) << 3), kbase + (long long)(j0 + jj) * a.css + cc * 8);
+      cp_async16(v_s + jj * HD + cc * 8, vbase + (long long)(j0 + jj) * a.css + cc * 8);
+    }
+  };
   // Every CTA of the cluster must have started before a peer writes into its shared memory:
   // arrive now, wait just before the first remote store (by then the barrier is long complete).
   cluster.barrier_arrive();
   pdl_launch_dependents();
+  // The preceding kernel writes q and cache row *pos only; the rows before it were written by
+  // earlier steps.  Start copying them while that kernel finishes, with the position as it reads
+  // now; after the wait, fetch row *pos -- or everything again if the position has moved.
+  long long pe = *a.pos;
+  pe = pe < 0 ? 0 : (pe >= a.max_seq ? a.max_seq - 1 : pe);
+  const int chunk_e = ((int)pe + 1 + S - 1) / S;
+  const int j0e = c * chunk_e, j1e = min((int)pe + 1, j0e + chunk_e);
+  if (STAGE) {
+    stage_rows(j0e, min(j1e, (int)pe), j0e);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   pdl_wait_primary();  // q and the cache row of this step come from the preceding kernel
 
   long long p = *a.pos;
@@ -107,14 +131,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   const int L = (int)p + 1;
   const int chunk = (L + S - 1) / S;
   const int j0 = c * chunk, j1 = min(L, j0 + chunk);
-  const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * HD;
-  const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * HD;
 
   if (STAGE) {
-    for (int idx = tid; idx < (j1 - j0) * CPR; idx += kAttnThreads) {
-      const int jj = idx / CPR, cc = idx - jj * CPR;
-      cp_async16(k_s + jj * HD + ((cc ^ (jj & SWZ)) << 3), kbase + (long long)(j0 + jj) * a.css + cc * 8);
-      cp_async16(v_s + jj * HD + cc * 8, vbase + (long long)(j0 + jj) * a.css + cc * 8);
+    if (p == pe) {
+      if (j0 <= (int)p && (int)p < j1) stage_rows((int)p, (int)p + 1, j0);
+    } else {  // the position moved: the copies in flight land first, then the whole range again
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      stage_rows(j0, j1, j0);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
@@ -274,9 +297,17 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   }
 }
 
-static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max, bool stage) {
-  return sizeof(float) * ((size_t)rep * head_dim * (1 + kAttnWarps + 8) + (size_t)rep * chunk_max) +
-         (stage ? (size_t)2 * chunk_max * head_dim * sizeof(__half) + 16 : 0);
+// The warps' P.V partials reuse the key staging when it holds them.
+static bool attn_red_in_k(int rep, int head_dim, int chunk_max, bool stage) {
+  return stage && (size_t)chunk_max * head_dim * sizeof(__half) >= (size_t)kAttnWarps * rep * head_dim * sizeof(float);
+}
+
+// q, the cluster's partials, the scores, the K / V staging and the warps' partials (see the kernel).
+static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max, bool stage, int cluster) {
+  size_t bytes = sizeof(float) * ((size_t)rep * head_dim * (1 + cluster) + (size_t)rep * chunk_max) + 16;
+  if (stage) bytes += (size_t)2 * chunk_max * head_dim * sizeof(__half);
+  if (!attn_red_in_k(rep, head_dim, chunk_max, stage)) bytes += sizeof(float) * (size_t)kAttnWarps * rep * head_dim;
+  return bytes;
 }
 
 constexpr size_t kAttnStageLimit = 96 * 1024;  // K + V of a CTA's keys staged when they fit in this
@@ -352,12 +383,13 @@ extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void
   if (max_seq > (1 << 20))
     return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld above 2^20", (long long)max_seq);
   int cluster = attn_cluster_size(batch * n_kv_heads, max_seq, current_sm_count());
-  while (cluster < 8 && attn_smem_bytes((int)rep, (int)head_dim, (int)((max_seq + cluster - 1) / cluster), false) >
-                            200 * 1024)
+  while (cluster < 8 &&
+         attn_smem_bytes((int)rep, (int)head_dim, (int)((max_seq + cluster - 1) / cluster), false, cluster) >
+             200 * 1024)
     cluster *= 2;
   const int chunk_max = (int)((max_seq + cluster - 1) / cluster);
   const bool stage = (size_t)2 * chunk_max * head_dim * sizeof(__half) <= kAttnStageLimit;
-  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, chunk_max, stage);
+  const size_t smem = attn_smem_bytes((int)rep, (int)head_dim, chunk_max, stage, cluster);
   if (smem > 200 * 1024)
     return set_error(LI4_ERR_UNSUPPORTED, "decode_attention: max_seq=%lld needs %zu bytes of shared memory per CTA",
                      (long long)max_seq, smem);
@@ -375,6 +407,7 @@ extern "C" int li4_decode_attention(const void* q, int64_t stride_qb, const void
   a.pos = reinterpret_cast<const long long*>(pos);
   a.max_seq = (int)max_seq;
   a.chunk_max = chunk_max;
+  a.red_in_k = attn_red_in_k((int)rep, (int)head_dim, chunk_max, stage) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc;
   const int sel = (int)rep * 1000 + (int)head_dim;
