@@ -102,10 +102,16 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __half* kbase = a.cache_k + (long long)b * a.csb + (long long)kvh * HD;
   const __half* vbase = a.cache_v + (long long)b * a.csb + (long long)kvh * HD;
-  auto stage_rows = [&](int r0, int r1, int j0) {  // cache rows [r0, r1) into their staging slots (row j0 first)
+  // cache rows [r0, r1) into their staging slots (slot 0 = row j0): keys (swizzled), then values
+  auto stage_k = [&](int r0, int r1, int j0) {
     for (int idx = tid; idx < (r1 - r0) * CPR; idx += kAttnThreads) {
       const int jj = r0 - j0 + idx / CPR, cc = idx % CPR;
       cp_async16(k_s + jj * HD + ((cc ^ (jj & SWZ)) << 3), kbase + (long long)(j0 + jj) * a.css + cc * 8);
+    }
+  };
+  auto stage_v = [&](int r0, int r1, int j0) {
+    for (int idx = tid; idx < (r1 - r0) * CPR; idx += kAttnThreads) {
+      const int jj = r0 - j0 + idx / CPR, cc = idx % CPR;
       cp_async16(v_s + jj * HD + cc * 8, vbase + (long long)(j0 + jj) * a.css + cc * 8);
     }
   };
@@ -114,14 +120,17 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   cluster.barrier_arrive();
   pdl_launch_dependents();
   // The preceding kernel writes q and cache row *pos only; the rows before it were written by
-  // earlier steps.  Start copying them while that kernel finishes, with the position as it reads
-  // now; after the wait, fetch row *pos -- or everything again if the position has moved.
+  // earlier steps.  Start copying them while that kernel finishes (keys and values as two
+  // groups, so the scores can start before the values land), with the position as it reads now;
+  // after the wait, copy row *pos -- or everything again if the position has moved.
   long long pe = *a.pos;
   pe = pe < 0 ? 0 : (pe >= a.max_seq ? a.max_seq - 1 : pe);
   const int chunk_e = ((int)pe + 1 + S - 1) / S;
   const int j0e = c * chunk_e, j1e = min((int)pe + 1, j0e + chunk_e);
   if (STAGE) {
-    stage_rows(j0e, min(j1e, (int)pe), j0e);
+    stage_k(j0e, min(j1e, (int)pe), j0e);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    stage_v(j0e, min(j1e, (int)pe), j0e);
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
   pdl_wait_primary();  // q and the cache row of this step come from the preceding kernel
@@ -131,19 +140,32 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
   const int L = (int)p + 1;
   const int chunk = (L + S - 1) / S;
   const int j0 = c * chunk, j1 = min(L, j0 + chunk);
+  const bool moved = p != pe;
 
   if (STAGE) {
-    if (p == pe) {
-      if (j0 <= (int)p && (int)p < j1) stage_rows((int)p, (int)p + 1, j0);
+    if (!moved) {
+      if (j0 <= (int)p && (int)p < j1 && tid < 2 * CPR) {  // row *pos: one 16-byte chunk per thread
+        const int jj = (int)p - j0, cc = tid % CPR;
+        if (tid < CPR)
+          *reinterpret_cast<uint4*>(k_s + jj * HD + ((cc ^ (jj & SWZ)) << 3)) =
+              __ldcg(reinterpret_cast<const uint4*>(kbase + p * a.css + cc * 8));
+        else
+          *reinterpret_cast<uint4*>(v_s + jj * HD + cc * 8) =
+              __ldcg(reinterpret_cast<const uint4*>(vbase + p * a.css + cc * 8));
+      }
     } else {  // the position moved: the copies in flight land first, then the whole range again
       asm volatile("cp.async.wait_group 0;" ::: "memory");
-      stage_rows(j0, j1, j0);
+      stage_k(j0, j1, j0);
+      stage_v(j0, j1, j0);
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   for (int t = tid; t < REP * HD; t += kAttnThreads)
     q_s[t] = __half2float(a.q[(long long)b * a.sqb + (long long)kvh * REP * HD + t]);
-  if (STAGE) asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (STAGE) {  // the keys (the values may still be in flight)
+    if (!moved) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+  }
   __syncthreads();
 
   // scores of this CTA's keys: one key per thread, REP dot products over HD dims
@@ -239,6 +261,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const __
       scores[r * a.chunk_max + j] =
           __half2float(__float2half_rn(expf(scores[r * a.chunk_max + j] - s_gmax[r]) / s_gsum[r]));
   }
+  if (STAGE) asm volatile("cp.async.wait_group 0;" ::: "memory");  // the values
   __syncthreads();
 
   // P.V over this CTA's keys: warp w takes keys j0 + w, j0 + w + 8, ...; lane holds DPL dims
