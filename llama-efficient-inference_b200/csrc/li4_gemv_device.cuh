@@ -313,7 +313,7 @@ template <int NT, int THREADS = kThreads, bool NORM = false>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
                                         const float* s_rstd = nullptr) {
   // One thread per 16-byte k-chunk (k = 8 values) and every row of it: the RMSNorm weight chunk
-  // is read once, and the rows' loads are independent, so they are in flight together.
+  // is read once.
   const int chunks = nks * 16;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
   for (int c = threadIdx.x; c < chunks; c += THREADS) {
@@ -321,6 +321,41 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int
     const long long k = (long long)(ks0 + ks) * 128 + 32 * quad + 8 * w;
     uint4 wn = make_uint4(0u, 0u, 0u, 0u);
     if (NORM && a.norm_w != nullptr) wn = *reinterpret_cast<const uint4*>(a.norm_w + k);  // 16-byte aligned
+    // M > 8 (two n-tiles): the rows' loads in flight together, 8 at a time.  M <= 8 keeps the
+    // loop below, measured faster at M = 1 (where it has one load per chunk) -- the batched
+    // form in the same kernel slowed the M = 1 launches by up to 0.3 us.
+    if (NT == 2 && vec_ok) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {  // the 8 rows of an n-tile in flight together
+      uint4 v[8];
+#pragma unroll
+      for (int m8 = 0; m8 < 8; ++m8) {
+        const int i = nt * 8 + m8;
+        v[m8] = (m8 < M8 && i < a.M) ? *reinterpret_cast<const uint4*>(a.x + (long long)i * a.sxm + k)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int m8 = 0; m8 < 8; ++m8) {
+        const int i = nt * 8 + m8;
+        if (m8 >= M8) continue;
+        uint32_t u[4] = {v[m8].x, v[m8].y, v[m8].z, v[m8].w};
+        if (NORM && a.norm_w != nullptr && i < a.M) {
+          const float r = s_rstd[i];
+          u[0] = norm_pair(u[0], wn.x, r);
+          u[1] = norm_pair(u[1], wn.y, r);
+          u[2] = norm_pair(u[2], wn.z, r);
+          u[3] = norm_pair(u[3], wn.w, r);
+        }
+        uint4 out;
+        out.x = __byte_perm(u[0], u[2], 0x5410);  // (x0, x4)
+        out.y = __byte_perm(u[0], u[2], 0x7632);  // (x1, x5)
+        out.z = __byte_perm(u[1], u[3], 0x5410);  // (x2, x6)
+        out.w = __byte_perm(u[1], u[3], 0x7632);  // (x3, x7)
+        *reinterpret_cast<uint4*>(xs + xs_chunk_offset(((ks * NT + nt) * M8 + m8) * 4 + quad, w, m8)) = out;
+      }
+      }
+      continue;
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
