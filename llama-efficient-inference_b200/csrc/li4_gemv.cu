@@ -584,7 +584,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
               __threadfence();
-              emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
+              if constexpr (NT == 2) emit_partial_tile<FUSED>(a, tile, lane, PartialSum{a.partial + row0, a.M, a.N, a.split});
+              else emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
               __syncwarp();
               if (lane == 0) a.counters[tile] = 0u;
             }
@@ -617,7 +618,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               last = __shfl_sync(0xffffffffu, last, 0);
               if (last) {
                 __threadfence();
-                emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
+                if constexpr (NT == 2) emit_partial_tile<FUSED>(a, tile, lane, PartialSum{a.partial + row0, a.M, a.N, a.split});
+                else emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
                 __syncwarp();
                 if (lane == 0) a.counters[tile] = 0u;
               }
@@ -831,7 +833,8 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
         for (int rt = 0; rt < RT; ++rt) {
           const int sub = tile * RT + rt;
           if (sub * 16 >= a.N) break;
-          emit_tile<FUSED>(a, sub, lane, 32, PartialSum{a.partial + sub * 16, a.M, a.N, a.split});
+          if constexpr (NT == 2) emit_partial_tile<FUSED>(a, sub, lane, PartialSum{a.partial + sub * 16, a.M, a.N, a.split});
+          else emit_tile<FUSED>(a, sub, lane, 32, PartialSum{a.partial + sub * 16, a.M, a.N, a.split});
         }
         __syncwarp();
         if (lane == 0) a.counters[tile] = 0u;
@@ -1003,7 +1006,8 @@ __global__ void __launch_bounds__(bulk_threads(NT), 1) gemv_bulk_kernel(const __
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
         __threadfence();
-        emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
+        if constexpr (NT == 2) emit_partial_tile<FUSED>(a, tile, lane, PartialSum{a.partial + row0, a.M, a.N, a.split});
+        else emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
         __syncwarp();
         if (lane == 0) a.counters[tile] = 0u;
       }

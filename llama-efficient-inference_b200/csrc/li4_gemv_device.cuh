@@ -177,6 +177,65 @@ __device__ __forceinline__ void emit_tile(const GemvArgs& a, int tile, int tid, 
   }
 }
 
+// emit_one with the residual value already loaded (rv; LI4_EPI_RESIDUAL only).
+__device__ __forceinline__ void emit_one_pre(const GemvArgs& a, int m, int row, float v, float rv) {
+  __half h = __float2half_rn(v);
+  if (a.epi == LI4_EPI_STORE_F32) {
+    reinterpret_cast<float*>(a.y)[(long long)m * a.sym + row] = __half2float(h);
+    return;
+  }
+  if (a.epi == LI4_EPI_RESIDUAL) h = __float2half_rn(__half2float(h) + rv);
+  a.y[(long long)m * a.sym + row] = h;
+}
+
+// The split-K reduction of one 16-row tile by one warp, for M > 8 (up to 8 outputs per lane):
+// every partial the lane sums (four K ranges at a time, in the fixed order of PartialSum) and
+// every residual it adds are loaded before it stores anything, so the epilogue costs a few L2
+// round trips instead of one per output (two K ranges per round: more would spill registers in
+// the register-ring kernels).  The paired and sum-of-squares epilogues take emit_tile.
+template <bool FUSED>
+__device__ __forceinline__ void emit_partial_tile(const GemvArgs& a, int tile, int lane, const PartialSum& ps) {
+  if (FUSED && (a.ssq_out != nullptr || epi_paired(a))) {
+    emit_tile<FUSED>(a, tile, lane, 32, ps);
+    return;
+  }
+  const int row0 = tile * 16, rows = min(16, a.N - row0), n = rows * a.M;
+  int off[8];  // offset of output i of this lane in a K range's partial block (M * N < 2^31)
+  float acc[8], rv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = lane + 32 * i, r = idx / a.M, m = idx - r * a.M;
+    off[i] = idx < n ? m * (int)ps.N + r : 0;
+    acc[i] = 0.f;
+    rv[i] = (FUSED && a.epi == LI4_EPI_RESIDUAL && idx < n) ? __half2float(a.res[(long long)m * a.srm + row0 + r]) : 0.f;
+  }
+  const long long range = (long long)ps.M * ps.N;
+  int sp = 0;
+  for (; sp + 2 <= ps.split; sp += 2) {
+    float t[2][8];
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[q][i] = lane + 32 * i < n ? __ldcg(ps.base + (sp + q) * range + off[i]) : 0.f;
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += t[q][i];
+  }
+  for (; sp < ps.split; ++sp) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += lane + 32 * i < n ? __ldcg(ps.base + sp * range + off[i]) : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = lane + 32 * i;
+    if (idx >= n) continue;
+    const int r = idx / a.M, m = idx - r * a.M;
+    if constexpr (FUSED) emit_one_pre(a, m, row0 + r, acc[i], rv[i]);
+    else a.y[(long long)m * a.sym + row0 + r] = __float2half_rn(acc[i]);
+  }
+}
+
 // Rows mode: a warp's 16-row tile `tile16` straight from its lanes' accumulators (lane (grp, quad)
 // holds rows grp and grp + 8, columns nt*8 + 2*quad + {0, 1}); split == 1.
 template <bool FUSED, int NT>

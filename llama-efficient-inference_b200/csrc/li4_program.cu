@@ -411,7 +411,8 @@ __device__ __forceinline__ void program_linear(const ProgOp& op, int n, int seq0
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
       __threadfence();
-      emit_tile<true>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, op.chunks});
+      if constexpr (NT == 2) emit_partial_tile<true>(a, tile, lane, PartialSum{a.partial + row0, a.M, a.N, op.chunks});
+      else emit_tile<true>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, op.chunks});
       __syncwarp();
       if (lane == 0) a.counters[tile] = 0u;
     }
