@@ -607,6 +607,28 @@ def profile_shape(a):
                       "bytes_per_launch": gemv_bytes(N, K, a.m)}))
 
 
+def profile_attention(a):
+    """--profile-attention BS: `--launches` decode-attention launches (Llama-3.2-1B heads: 32 query /
+    8 KV, head_dim 64) at position 512 of a 640-row fp16 cache of batch BS, an L2 flush (256 MB
+    write) before each -- the small case for ncu captures of li4_decode_attention."""
+    from llama import fused
+
+    dev = torch.device("cuda", 0)
+    bs, S, H, KV, HD = a.profile_attention, 640, 32, 8, 64
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(bs, H * HD, generator=gen, device=dev).half()
+    ck = torch.randn(bs, S, KV, HD, generator=gen, device=dev).half()
+    cv = torch.randn(bs, S, KV, HD, generator=gen, device=dev).half()
+    out = torch.empty_like(q)
+    pos = torch.tensor([512], dtype=torch.long, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(a.launches):
+        flush.zero_()
+        fused.decode_attention(q, ck, cv, pos, out, H, KV)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_attention": bs, "launches": a.launches, "kv_bytes": 2 * bs * 513 * KV * HD * 2}))
+
+
 def roofline_traffic():
     """DRAM bytes per step of the GEMV kernels from the committed ncu summary, if present (M=1 only)."""
     path = os.path.join(REPO, "profiles", "gemv_step_m1_traffic.json")
@@ -925,6 +947,8 @@ def main():
     ap.add_argument("--profile-shape", default=None,
                     choices=[n for n, _, _ in LAYER_SHAPES] + [LM_HEAD[0], "qkv_fused", "gate_up_fused"],
                     help="only run --launches launches of one shape (for ncu), no timing")
+    ap.add_argument("--profile-attention", type=int, default=0, metavar="BS",
+                    help="only run --launches decode-attention launches at batch BS (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
@@ -940,6 +964,9 @@ def main():
     a = ap.parse_args()
     if a.profile_shape:
         profile_shape(a)
+        return
+    if a.profile_attention:
+        profile_attention(a)
         return
     if a.sweep:
         kernel_sweep(a)
