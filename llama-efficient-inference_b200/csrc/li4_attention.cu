@@ -336,10 +336,11 @@ static size_t attn_smem_bytes(int rep, int head_dim, int chunk_max, bool stage, 
 constexpr size_t kAttnStageLimit = 96 * 1024;  // K + V of a CTA's keys staged when they fit in this
 
 // CTAs per (KV head, sequence): a cluster of up to 8 when the (KV head, sequence)
-// pairs alone leave SMs idle, keeping >= 32 keys per CTA at max_seq.
+// pairs alone leave SMs idle, as long as the doubled launch stays within 2 CTAs per SM
+// and >= 32 keys per CTA at max_seq.
 static int attn_cluster_size(int64_t pairs, int64_t max_seq, int sm) {
   int S = 1;
-  while (S < 8 && pairs * S < 2LL * sm && max_seq / (2 * S) >= 32) S *= 2;
+  while (S < 8 && pairs * S * 2 <= 2LL * sm && max_seq / (2 * S) >= 32) S *= 2;
   return S;
 }
 

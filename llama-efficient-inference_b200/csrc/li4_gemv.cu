@@ -1059,11 +1059,13 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (kernel == LI4_KERNEL_AUTO) {
     // By measured B200 sweeps of the Llama-3.2-1B shapes (bench.py --sweep):
     // tile streaming when every warp slot gets several 16-row x 2048-k tiles
-    // (lm_head-sized N); the bulk-copy ring for 2 <= M <= 8, and otherwise when
-    // each SM gets about four tiles or more (fused gate/up; down_proj at M > 8);
-    // streaming warps below that; CUDA-core / MMA kernels for groups below 128.
+    // (lm_head-sized N) at M <= 8; the bulk-copy ring for 2 <= M <= 8, at M > 8
+    // for lm_head-sized N too (41.6 against 47.7 us for lm_head at M = 16), and
+    // otherwise when each SM gets about four tiles or more (fused gate/up;
+    // down_proj at M > 8); streaming warps below that; CUDA-core / MMA kernels for
+    // groups below 128.
     const int64_t tiles_2048 = ((N + 15) / 16) * std::max<int64_t>(1, K / 2048);
-    if (group == 128 && K > 0 && K % 2048 == 0 && tiles_2048 >= 32LL * sm) kernel = LI4_KERNEL_TILE;
+    if (group == 128 && K > 0 && K % 2048 == 0 && tiles_2048 >= 32LL * sm && M <= 8) kernel = LI4_KERNEL_TILE;
     else if (group == 128 && K > 0 && K % 1024 == 0 &&
              ((M >= 2 && M <= 8) || tiles_2048 >= 4LL * sm || (M > 8 && tiles_2048 >= 2LL * sm)))
       kernel = LI4_KERNEL_BULK;
