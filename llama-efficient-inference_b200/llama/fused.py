@@ -154,6 +154,12 @@ class FusedDecoder:
     step serves every position.
     """
 
+    # Batches up to this hand sums of squares from the residual epilogues to the next RMSNorm
+    # (li4_fusion.sumsq_*); larger ones let the norm's GEMV read x once more instead.  Measured
+    # (A/B on one B200): at batch 16 the hand-over costs 6% of the step (1.023 vs 0.966 ms); at
+    # batch 4 it is even (0.7372 vs 0.7363 ms).
+    sumsq_handoff_max_batch = 4
+
     def __init__(self, model, nvlink_allreduce: bool = True, program: bool = False):
         self.model = model
         self.nvlink_allreduce = nvlink_allreduce
@@ -303,9 +309,7 @@ class FusedDecoder:
         E = native
         ssq_h, ssq_h1 = buf["ssq_h"], buf["ssq_h1"]
         tiles = ssq_h.shape[0]
-        # measured: the hand-over of sums of squares pays at small batches; at 16 rows the producer's
-        # reduction costs more than the consumer's pass over x
-        handoff = bs <= 4
+        handoff = bs <= self.sumsq_handoff_max_batch
         h_ssq = None  # the embedding rows carry no sums of squares: the first block's norm reads x
         for blk in self.blocks:
             att = blk.att
