@@ -936,7 +936,7 @@ def main():
     ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the full-model decode measurement")
     ap.add_argument("--decode-bs", type=int, nargs="+", default=None,
-                    help="decode batch sizes (default: 1 and 16 on one GPU, 16 under tensor parallelism)")
+                    help="decode batch sizes (default: 1, 8 and 16 on one GPU, 16 under tensor parallelism)")
     ap.add_argument("--decode-prompt", type=int, default=512)
     ap.add_argument("--decode-gen", type=int, default=128)
     ap.add_argument("--decode-reps", type=int, default=3)
@@ -983,7 +983,7 @@ def main():
     if a.warmup < 3:
         a.warmup = 3
     if a.decode_bs is None:
-        a.decode_bs = [1, 16] if int(os.environ.get("WORLD_SIZE", "1")) == 1 else [16]
+        a.decode_bs = [1, 8, 16] if int(os.environ.get("WORLD_SIZE", "1")) == 1 else [16]
     if a.impl == "reference":
         run_reference(a)
     else:
