@@ -195,12 +195,12 @@ __device__ __forceinline__ void emit_one_pre(const GemvArgs& a, int m, int row, 
 // the register-ring kernels).  The paired and sum-of-squares epilogues take emit_tile.
 template <bool FUSED>
 __device__ __forceinline__ void emit_partial_tile(const GemvArgs& a, int tile, int lane, const PartialSum& ps) {
-  if (FUSED && (a.ssq_out != nullptr || epi_paired(a))) {
-    emit_tile<FUSED>(a, tile, lane, 32, ps);
+  if ((FUSED && (a.ssq_out != nullptr || epi_paired(a))) || (long long)ps.M * ps.N > 0x7FFFFFFFLL) {
+    emit_tile<FUSED>(a, tile, lane, 32, ps);  // (and partial blocks beyond 32-bit offsets)
     return;
   }
   const int row0 = tile * 16, rows = min(16, a.N - row0), n = rows * a.M;
-  int off[8];  // offset of output i of this lane in a K range's partial block (M * N < 2^31)
+  int off[8];  // offset of output i of this lane in a K range's partial block (M * N < 2^31, above)
   float acc[8], rv[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
