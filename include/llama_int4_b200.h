@@ -227,10 +227,19 @@ int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, 
 int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
                     int64_t* out, int64_t out_stride, void* stream);
 
+/* out[r, :] = table[ids[r], :] for r < rows: fp16 rows of `cols` values (cols % 8 == 0,
+ * 16-byte aligned rows; rows <= 65535).  An id outside [0, table_rows) is clamped and
+ * sets bit 3 of li4_device_errors.  The ids may come from the preceding kernel on the
+ * stream (programmatic dependent launch: they are read after its completion).
+ * Replaces: the token embedding lookup of the decode step (llama/model.py:440). */
+int li4_gather_rows(const void* table, int64_t table_rows, int64_t cols, int64_t stride_t, const int64_t* ids,
+                    int64_t rows, void* out, int64_t stride_o, void* stream);
+
 /* Device-side error flags of the current device (bit 0: a bounded pipeline wait
  * inside a GEMV kernel ran out; bit 1: a bounded wait for a peer's flag in
  * li4_allreduce_add ran out; bit 2: a decode program's wait for another op
- * ran out; bit 3: a program gather met an id outside its table -- the kernel
+ * ran out; bit 3: a gather (li4_gather_rows or a program gather) met an id
+ * outside its table -- the kernel
  * carried on and its outputs are not valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);

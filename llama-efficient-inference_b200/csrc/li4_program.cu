@@ -797,8 +797,63 @@ __global__ void __launch_bounds__(prog_threads(NT), 1) decode_program_kernel(con
 
 }  // namespace li4
 
+namespace li4 {
+
 // ---------------------------------------------------------------------------
-// Host side.
+// Standalone row gather (the embedding lookup of the per-launch decode step): one CTA per row,
+// 16-byte vectors; the ids come from the preceding kernel (read after the dependency wait).
+// ---------------------------------------------------------------------------
+constexpr int kGatherThreads = 256;
+
+__global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const __half* table, long long table_rows,
+                                                                     long long stride_t, const long long* ids,
+                                                                     __half* out, long long stride_o, int cols) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int r = blockIdx.x;
+  long long id = ids[r];
+  if (id < 0 || id >= table_rows) {
+    if (threadIdx.x == 0) atomicOr(&g_prog_device_error, 8u);
+    id = id < 0 ? 0 : table_rows - 1;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * stride_t);
+  uint4* dst = reinterpret_cast<uint4*>(out + (long long)r * stride_o);
+  for (int t = threadIdx.x; t < cols / 8; t += kGatherThreads) dst[t] = src[t];
+}
+
+}  // namespace li4
+
+extern "C" int li4_gather_rows(const void* table, int64_t table_rows, int64_t cols, int64_t stride_t,
+                               const int64_t* ids, int64_t rows, void* out, int64_t stride_o, void* stream) {
+  using namespace li4;
+  if (!table || !ids || !out || table_rows < 1 || rows < 0 || rows > 65535 || cols < 8 || cols % 8 != 0 ||
+      cols > INT32_MAX / 2 || stride_t < cols || stride_o < cols)
+    return set_error(LI4_ERR_INVALID_ARG, "gather_rows: rows=%lld cols=%lld (cols %% 8 == 0) strides %lld, %lld",
+                     (long long)rows, (long long)cols, (long long)stride_t, (long long)stride_o);
+  if (!aligned16(table) || !aligned16(out) || stride_t % 8 != 0 || stride_o % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(ids) & 7u))
+    return set_error(LI4_ERR_ALIGNMENT, "gather_rows: rows must be 16-byte aligned");
+  if (rows == 0) return LI4_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows, 1, 1);
+  cfg.blockDim = dim3(kGatherThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int rc = check_cuda(cudaLaunchKernelEx(&cfg, gather_rows_kernel, static_cast<const __half*>(table),
+                                               (long long)table_rows, (long long)stride_t,
+                                               reinterpret_cast<const long long*>(ids), static_cast<__half*>(out),
+                                               (long long)stride_o, (int)cols),
+                            "gather_rows: kernel launch");
+  if (rc == LI4_OK) clear_error();
+  return rc;
+}
+
+// ---------------------------------------------------------------------------
+// Host side of the program.
 // ---------------------------------------------------------------------------
 struct li4_program {
   std::vector<li4::ProgOp> ops;

@@ -72,8 +72,19 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void*
       take(best, __half2float(x[i]), i);
   } else {
     const float* x = static_cast<const float*>(logits) + row * stride;
-#pragma unroll 4
-    for (long long i = c0 + threadIdx.x; i < c1; i += kArgmaxThreads) take(best, x[i], i);
+    // chunk is a multiple of 8: each CTA's first 16-byte vector is aligned when the row is; the
+    // loop is unrolled so a thread's loads are in flight together
+    const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0);
+    const long long v0 = vec ? c0 / 4 : 0, v1 = vec ? c1 / 4 : 0;
+#pragma unroll 8
+    for (long long v = v0 + threadIdx.x; v < v1; v += kArgmaxThreads) {
+      const float4 f = reinterpret_cast<const float4*>(x)[v];
+      take(best, f.x, 4 * v);
+      take(best, f.y, 4 * v + 1);
+      take(best, f.z, 4 * v + 2);
+      take(best, f.w, 4 * v + 3);
+    }
+    for (long long i = (vec ? max(c0, 4 * v1) : c0) + threadIdx.x; i < c1; i += kArgmaxThreads) take(best, x[i], i);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

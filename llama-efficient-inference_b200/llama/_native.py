@@ -82,6 +82,7 @@ SIGNATURES = {
     "li4_ipc_open_handle": (_INT, [_P, ctypes.POINTER(_P)]),
     "li4_ipc_close": (_INT, [_P]),
     "li4_allreduce_add": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _INT, _INT, _INT, _I64, _P, _P, _P]),
+    "li4_gather_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P]),
     "li4_program_create": (_INT, [ctypes.POINTER(_P)]),
     "li4_program_destroy": (_INT, [_P]),
     "li4_program_add_linear": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,

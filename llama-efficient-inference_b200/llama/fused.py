@@ -17,7 +17,8 @@ adds.  Here a block is:
                                                                 (SwiGLU epilogue)
   5. w2 GEMV    h = h1 + w2(ffn)                                (residual epilogue)
 
-and the step ends with lm_head with the final RMSNorm fused into its staging.
+and the step ends with lm_head with the final RMSNorm fused into its staging.  The embedding rows
+come from li4_gather_rows and the greedy tokens from li4_argmax_rows.
 Under tensor parallelism the wo / w2 outputs are partial sums: each rank's GEMV
 writes its partial into a buffer every rank has mapped, and one kernel sums the
 ranks' partials over NVLink and adds the residual (llama.comm; NCCL plus a torch
@@ -108,6 +109,14 @@ def decode_attention(q: torch.Tensor, cache_k: torch.Tensor, cache_v: torch.Tens
                                            B, n_heads, n_kv_heads, cache_k.shape[3], pos.data_ptr(),
                                            S if max_seq is None else max_seq, native.stream_ptr(q.device))
     native.check(rc, "decode_attention")
+
+
+def gather_rows(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor) -> None:
+    """out[r] = table[ids[r]] (li4_gather_rows): fp16 rows, ids int64, on the current stream."""
+    rc = native.lib().li4_gather_rows(table.data_ptr(), table.shape[0], table.shape[1], table.stride(0),
+                                      ids.data_ptr(), ids.numel(), out.data_ptr(), out.stride(0),
+                                      native.stream_ptr(out.device))
+    native.check(rc, "gather_rows")
 
 
 def argmax_rows(logits: torch.Tensor, out: torch.Tensor) -> None:
@@ -305,7 +314,7 @@ class FusedDecoder:
         bs = tokens.shape[0]
         buf = self._buffers(bs)
         h, h1, q, attn, ffn, part = buf["h"], buf["h1"], buf["q"], buf["attn"], buf["ffn"], buf["part"]
-        torch.index_select(self.model.tok_embeddings.weight, 0, tokens.view(-1), out=h)
+        gather_rows(self.model.tok_embeddings.weight, tokens.view(-1), h)
         E = native
         ssq_h, ssq_h1 = buf["ssq_h"], buf["ssq_h1"]
         tiles = ssq_h.shape[0]

@@ -149,6 +149,14 @@ def test_allreduce_validates(native):
     assert lib.li4_allreduce_add(odd, arr, 16, 16, 2, 0, 64, 16, 16, None) == native.LI4_ERR_ALIGNMENT
 
 
+def test_gather_rows_validates(native):
+    lib = native.lib()
+    assert lib.li4_gather_rows(256, 1000, 2044, 2044, 256, 1, 256, 2044, None) == native.LI4_ERR_INVALID_ARG  # cols % 8
+    assert lib.li4_gather_rows(264, 1000, 2048, 2048, 256, 1, 256, 2048, None) == native.LI4_ERR_ALIGNMENT
+    assert lib.li4_gather_rows(256, 1000, 2048, 2048, 256, 70000, 256, 2048, None) == native.LI4_ERR_INVALID_ARG
+    assert lib.li4_gather_rows(256, 1000, 2048, 2048, 256, 0, 256, 2048, None) == native.LI4_OK  # nothing to do
+
+
 def test_program_builder_validates(native):
     """Decode-program ops are checked when they are added (no GPU needed); launching an
     unfinalized program is refused."""

@@ -369,3 +369,23 @@ def test_sumsq_handoff(M, N, K, fz, cuda_device):
                                                           epilogue=nat.LI4_EPI_STORE, sumsq_in=ssq.data_ptr(),
                                                           sumsq_tiles=ssq.shape[0]))
     close(y_b, y_a, what="norm from handed-over sums of squares")
+
+
+def test_gather_rows_matches_index_select(fz, cuda_device):
+    """li4_gather_rows: the embedding lookup, bit-exact against torch.index_select; an id outside the
+    table is clamped and flagged (bit 3 of li4_device_errors)."""
+    fused, nat = fz
+    table = randn((5000, 2048), cuda_device, 91)
+    for ids in ([7], [4999, 0, 3, 3, 1234] * 3 + [17]):
+        idx = torch.tensor(ids, dtype=torch.long, device=cuda_device)
+        out = torch.empty(len(ids), 2048, dtype=torch.float16, device=cuda_device)
+        fused.gather_rows(table, idx, out)
+        torch.cuda.synchronize()
+        assert torch.equal(out, torch.index_select(table, 0, idx))
+    assert nat.device_errors(reset=True) == 0
+    bad = torch.tensor([2, 5000], dtype=torch.long, device=cuda_device)
+    out = torch.empty(2, 2048, dtype=torch.float16, device=cuda_device)
+    fused.gather_rows(table, bad, out)
+    torch.cuda.synchronize()
+    assert nat.device_errors(reset=True) & 8
+    assert torch.equal(out[1], table[4999])
