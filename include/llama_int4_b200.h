@@ -186,6 +186,14 @@ typedef struct li4_fusion {
   float* sumsq_out;
   const float* sumsq_in;
   int64_t sumsq_tiles;
+  /* Greedy argmax of the written logits (LI4_EPI_STORE_F32 only): argmax_out[m * argmax_stride]
+   * = torch.argmax(y[m, :N]) (int64), written by the launch's last CTA.  argmax_scratch: device
+   * memory of 8 * M + 8 bytes, zero before the first use; launches leave it zero (launches that
+   * may overlap need their own).  Runs on the tile kernel (lm_head-sized N at M <= 8); other
+   * launch plans return LI4_ERR_UNSUPPORTED.  NULL = not used. */
+  int64_t* argmax_out;
+  int64_t argmax_stride;
+  void* argmax_scratch;
 } li4_fusion;
 
 /* li4_int4_linear with a fused prologue / epilogue (`fusion` NULL = plain).

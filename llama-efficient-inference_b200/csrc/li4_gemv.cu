@@ -807,6 +807,30 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
       }
     }
     const int row0 = tile * ROWS;
+    if (FUSED && a.am_keys != nullptr) {  // greedy argmax of the logits this warp writes (split == 1)
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt) {
+        if (row0 + rt * 16 >= a.N) continue;  // (uniform over the warp)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          unsigned long long kb[2] = {0ull, 0ull};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int row = row0 + rt * 16 + grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
+            if (row < a.N && m < a.M)  // the value the epilogue writes: fp16-rounded, widened
+              kb[e & 1] = max(kb[e & 1], argmax_key(__half2float(__float2half_rn(acc[rt][nt][e])), row));
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            unsigned long long v = kb[j];
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+            const int m = nt * 8 + 2 * quad + j;
+            if (grp == 0 && m < a.M && v != 0ull) atomicMax(&a.am_keys[m], v);
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int rt = 0; rt < RT; ++rt) {
       if (a.split == 1) {
@@ -842,6 +866,7 @@ __global__ void __launch_bounds__(kStreamThreads, (RT == 1 ? 2 : 1)) gemv_tile_k
     }
     cur = nxt;
   }
+  if (FUSED && a.am_keys != nullptr) argmax_finish(a, [] { __syncthreads(); });
 }
 
 // ---------------------------------------------------------------------------
@@ -1488,6 +1513,13 @@ int prepare_linear(const void* x, const void* packed, const void* scale, const v
     return set_error(LI4_ERR_ALIGNMENT, "int4_linear: fp16 tensors must be 2-byte aligned");
   if (epi == LI4_EPI_STORE_F32 && (reinterpret_cast<uintptr_t>(y) & 3u))
     return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: an fp32 output must be 4-byte aligned");
+  if (f && f->argmax_out) {
+    if (epi != LI4_EPI_STORE_F32 || !f->argmax_scratch || f->argmax_stride < 1)
+      return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: the fused argmax takes LI4_EPI_STORE_F32, an "
+                       "argmax_scratch and argmax_stride >= 1");
+    if ((reinterpret_cast<uintptr_t>(f->argmax_out) | reinterpret_cast<uintptr_t>(f->argmax_scratch)) & 7u)
+      return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: argmax_out / argmax_scratch must be 8-byte aligned");
+  }
   GemvArgs args = {};
   if (fused) {
     args.norm_w = static_cast<const __half*>(f->norm_weight);
@@ -1511,6 +1543,12 @@ int prepare_linear(const void* x, const void* packed, const void* scale, const v
     args.ssq_out = f->sumsq_out;
     args.ssq_in = f->sumsq_in;
     args.ssq_tiles = (int)f->sumsq_tiles;
+    if (f->argmax_out != nullptr) {
+      args.am_keys = static_cast<unsigned long long*>(f->argmax_scratch);
+      args.am_count = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(f->argmax_scratch) + 8 * M);
+      args.am_out = reinterpret_cast<long long*>(f->argmax_out);
+      args.am_stride = f->argmax_stride;
+    }
   }
   args.x = static_cast<const __half*>(x);
   args.packed = static_cast<const uint8_t*>(packed);
@@ -1557,6 +1595,9 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
     if (rc != LI4_OK) return rc;
   }
+  if (args.am_keys != nullptr && (p.kernel != LI4_KERNEL_TILE || p.split != 1))
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: the fused argmax runs on the tile kernel without a "
+                     "K split (lm_head-sized N at M <= 8); this launch plan has neither");
   if (p.ws_bytes > 0) {
     if (!workspace || workspace_bytes < p.ws_bytes)
       return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "

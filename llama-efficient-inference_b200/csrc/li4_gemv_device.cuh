@@ -47,6 +47,10 @@ struct GemvArgs {
   float* ssq_out;                // LI4_EPI_RESIDUAL: per 16-row tile, per row m, sum of the written values squared
   const float* ssq_in;           // RMSNorm prologue: the producer's ssq_out, [ssq_tiles][M]
   int ssq_tiles;
+  unsigned long long* am_keys;   // greedy argmax (LI4_EPI_STORE_F32, tile kernel): [M] running keys,
+  unsigned* am_count;            // then the CTA arrival count (li4_fusion.argmax_scratch)
+  long long* am_out;
+  long long am_stride;
 };
 
 // ---------------------------------------------------------------------------
@@ -448,6 +452,40 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int ks0, int nks, int
         }
         *reinterpret_cast<uint4*>(xs + xs_chunk_offset(block, w, m8)) = out;
       }
+    }
+  }
+}
+
+// torch.argmax order as one 64-bit key: the value's order-preserving bits (NaN above every
+// number, -0 as +0) above the complement of the index (the first index wins a tie).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  unsigned u = __float_as_uint(v);
+  unsigned ord;
+  if (v != v) {
+    ord = 0xFFFFFFFFu;
+  } else {
+    if (v == 0.f) u = 0u;
+    ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
+}
+
+// The fused greedy argmax's end of launch: after every warp of the CTA has issued its
+// atomicMax (sync), the CTA counts itself in; the last one writes the indices and leaves the
+// keys and the count at zero for the next launch.
+template <typename Sync>
+__device__ __forceinline__ void argmax_finish(const GemvArgs& a, Sync sync) {
+  sync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(a.am_count, 1u) == total - 1u) {
+      __threadfence();
+      for (int m = 0; m < a.M; ++m) {
+        const unsigned long long k = atomicExch(&a.am_keys[m], 0ull);
+        a.am_out[(long long)m * a.am_stride] = (long long)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull));
+      }
+      atomicExch(a.am_count, 0u);
     }
   }
 }

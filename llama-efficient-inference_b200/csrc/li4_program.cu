@@ -633,20 +633,6 @@ __device__ __forceinline__ void gather_unit(const GatherOp& ga, int r) {
   for (int t = threadIdx.x; t < ga.cols / 8; t += CW * 32) dst[t] = src[t];
 }
 
-// torch.argmax order as one 64-bit key: the value's order-preserving bits (NaN above every
-// number, -0 as +0) above the complement of the index (the first index wins a tie).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
-  unsigned u = __float_as_uint(v);
-  unsigned ord;
-  if (v != v) {
-    ord = 0xFFFFFFFFu;
-  } else {
-    if (v == 0.f) u = 0u;
-    ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  }
-  return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
-}
-
 template <int CW>
 __device__ __forceinline__ void argmax_unit(const ArgmaxOp& am, int u, unsigned long long* s_key, int warp,
                                             int lane) {
@@ -931,6 +917,9 @@ extern "C" int li4_program_add_linear(li4_program* prog, const void* x, const vo
   if (group_size != 128)
     return set_error(LI4_ERR_UNSUPPORTED, "program_add_linear: group size %lld (program linears take 128)",
                      (long long)group_size);
+  if (fusion && fusion->argmax_out)
+    return set_error(LI4_ERR_UNSUPPORTED, "program_add_linear: the fused argmax is a per-launch epilogue; "
+                     "programs take li4_program_add_argmax");
   ProgOp op = {};
   op.kind = kOpLinear;
   op.wait = wait;

@@ -59,6 +59,9 @@ class Fusion(ctypes.Structure):
         ("sumsq_out", ctypes.c_void_p),
         ("sumsq_in", ctypes.c_void_p),
         ("sumsq_tiles", ctypes.c_int64),
+        ("argmax_out", ctypes.c_void_p),
+        ("argmax_stride", ctypes.c_int64),
+        ("argmax_scratch", ctypes.c_void_p),
     ]
 
 

@@ -175,6 +175,7 @@ class FusedDecoder:
         # single GPU: the whole step as one persistent launch (llama.program) where it applies
         self.use_program = program
         self._programs = {}
+        self._fused_argmax = {}  # batch size -> whether the lm_head launch runs the greedy argmax
         self.last_path = None  # "program" or "launches": how the last decode_step ran
         self._ar = None  # NvlinkAllReduce of the model's TP group, built on first use
         p = model.params
@@ -354,6 +355,23 @@ class FusedDecoder:
         logits = buf["logits"]  # fp32: the lm_head writes its fp16 outputs widened (output(h).float())
         f = E.Fusion(norm_weight=self.final_norm.data_ptr(), norm_eps=self.final_eps, epilogue=E.LI4_EPI_STORE_F32,
                      sumsq_in=h_ssq, sumsq_tiles=tiles if h_ssq else 0)
+        # the greedy argmax in the lm_head's own launch where its plan takes it (single GPU)
+        fuse_argmax = next_tokens is not None and self.model.tp_group is None and self._fused_argmax.get(bs, True)
+        if fuse_argmax:
+            scratch = self._bufs.get(("argmax", bs))
+            if scratch is None:
+                scratch = self._bufs[("argmax", bs)] = torch.zeros(8 * bs + 8, dtype=torch.uint8, device=self.device)
+            nt = next_tokens.view(bs, 1)
+            f.argmax_out, f.argmax_stride, f.argmax_scratch = nt.data_ptr(), nt.stride(0), scratch.data_ptr()
+            try:
+                int4_linear_fused(h, *self.out, None, f, y_ptr=logits.data_ptr(), y_stride=logits.stride(0))
+                self._fused_argmax[bs] = True
+                return logits.view(bs, 1, -1)
+            except native.Li4Error as e:
+                if e.status != native.LI4_ERR_UNSUPPORTED:
+                    raise
+                self._fused_argmax[bs] = False  # e.g. M > 8 runs the lm_head off the tile kernel
+                f.argmax_out, f.argmax_stride, f.argmax_scratch = None, 0, None
         int4_linear_fused(h, *self.out, None, f, y_ptr=logits.data_ptr(), y_stride=logits.stride(0))
         if self.model.tp_group is not None:
             import torch.distributed as dist

@@ -389,3 +389,29 @@ def test_gather_rows_matches_index_select(fz, cuda_device):
     torch.cuda.synchronize()
     assert nat.device_errors(reset=True) & 8
     assert torch.equal(out[1], table[4999])
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_fused_argmax_epilogue(M, fz, cuda_device):
+    """The lm_head's fused greedy argmax (li4_fusion.argmax_*): torch.argmax of the fp32 logits the same
+    launch writes, on two launches in a row (the scratch is left zero); M > 8 is refused."""
+    fused, nat = fz
+    N, K = 128256, 2048
+    p, s, z, _ = quantized(N, K, cuda_device, 1234)
+    scratch = torch.zeros(8 * 16 + 8, dtype=torch.uint8, device=cuda_device)
+    lg = torch.empty(M, N, dtype=torch.float32, device=cuda_device)
+    out = torch.full((M, 1), -1, dtype=torch.long, device=cuda_device)
+    for seed in (1, 2):
+        x = randn((M, K), cuda_device, 300 + seed + M)
+        f = nat.Fusion(epilogue=nat.LI4_EPI_STORE_F32, argmax_out=out.data_ptr(), argmax_stride=out.stride(0),
+                       argmax_scratch=scratch.data_ptr())
+        fused.int4_linear_fused(x, p, s, z, None, f, y_ptr=lg.data_ptr(), y_stride=lg.stride(0))
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(-1), torch.argmax(lg, dim=-1))
+        assert int(scratch.count_nonzero()) == 0
+    x16 = randn((16, K), cuda_device, 399)
+    lg16 = torch.empty(16, N, dtype=torch.float32, device=cuda_device)
+    with pytest.raises(nat.Li4Error) as err:
+        fused.int4_linear_fused(x16, p, s, z, None, f, y_ptr=lg16.data_ptr(), y_stride=lg16.stride(0))
+    assert err.value.status == nat.LI4_ERR_UNSUPPORTED
+    assert nat.device_errors(reset=True) == 0
