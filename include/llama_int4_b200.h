@@ -56,7 +56,9 @@ typedef enum li4_kernel {
                                 K % 1024 == 0, 16-byte aligned scale / zero rows   */
 } li4_kernel;
 
-/* Library version, (major << 16) | (minor << 8) | patch. */
+/* Library version, (major << 16) | (minor << 8) | patch.  0.2: li4_fusion has the argmax_*
+ * fields (callers built against 0.1 pass a shorter struct); the li4_program_* and
+ * li4_gather_rows entry points. */
 int li4_version(void);
 
 /* Message describing the last failed call on this host thread ("" if none). */

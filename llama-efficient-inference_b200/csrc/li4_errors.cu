@@ -43,6 +43,7 @@ int current_sm_count() {
 
 }  // namespace li4
 
-extern "C" int li4_version(void) { return (0 << 16) | (1 << 8) | 0; }
+// 0.2.0: li4_fusion gained the argmax_* fields (a larger struct); the decode program, li4_gather_rows.
+extern "C" int li4_version(void) { return (0 << 16) | (2 << 8) | 0; }
 
 extern "C" const char* li4_last_error(void) { return li4::g_last_error; }

@@ -42,7 +42,7 @@ def test_library_exports_every_declared_symbol(native):
 
 def test_version(native):
     v = native.lib().li4_version()
-    assert v >> 16 == 0 and (v >> 8) & 0xFF >= 1
+    assert v >> 16 == 0 and (v >> 8) & 0xFF >= 2  # 0.2: the li4_fusion layout with the argmax fields
 
 
 def call_linear(native, M=1, N=64, K=256, group=128, x=16, packed=16, scale=16, zero=16, y=16,
