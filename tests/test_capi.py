@@ -198,3 +198,25 @@ def test_program_builder_validates(native):
         assert lib.li4_program_launch(h, None) == native.LI4_ERR_INVALID_ARG  # not finalized
     finally:
         assert lib.li4_program_destroy(h) == native.LI4_OK
+
+
+def test_fusion_struct_layout_matches_header(native, tmp_path):
+    """The ctypes Fusion structure has the size and field offsets of the header's li4_fusion
+    (compiled with the host C compiler)."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    fields = [name for name, _ in native.Fusion._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "llama_int4_b200.h"\nint main(void) {\n'
+                   '  printf("%zu\\n", sizeof(li4_fusion));\n' +
+                   "".join(f'  printf("%zu\\n", offsetof(li4_fusion, {f}));\n' for f in fields) + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert got[0] == ctypes.sizeof(native.Fusion)
+    for f, off in zip(fields, got[1:]):
+        assert getattr(native.Fusion, f).offset == off, f
