@@ -52,8 +52,11 @@ typedef enum li4_kernel {
   LI4_KERNEL_MMA = 2,        /* m16n8k16 tensor-core tiles (weights as the A side)  */
   LI4_KERNEL_STREAM = 3,     /* streaming warps, m16n8k16 tiles, groups >= 128      */
   LI4_KERNEL_TILE = 4,       /* tile-streaming warps: group 128, K ranges of 2048  */
-  LI4_KERNEL_BULK = 5        /* bulk-copy ring in shared memory: group 128,
+  LI4_KERNEL_BULK = 5,       /* bulk-copy ring in shared memory: group 128,
                                 K % 1024 == 0, 16-byte aligned scale / zero rows   */
+  LI4_KERNEL_SLAB = 6        /* whole weight slice of a CTA resident in shared
+                                memory, K split across its warps: group 128, up to
+                                16 row tiles per CTA                              */
 } li4_kernel;
 
 /* Library version, (major << 16) | (minor << 8) | patch.  0.2: li4_fusion has the argmax_*

@@ -1061,9 +1061,61 @@ struct Plan {
   bool stream_ksplit;  // LI4_KERNEL_STREAM: K-split mode
   int stages;          // LI4_KERNEL_BULK: shared-memory ring stages
   bool bulk_contig;    // LI4_KERNEL_BULK: tiles move as three contiguous copies (set at launch from the strides)
+  int slots;           // LI4_KERNEL_SLAB: warps sharing one tile's ksteps (stages = tiles per CTA)
+  int pitch;           // LI4_KERNEL_SLAB: bytes between packed rows of a stage
 };
 
 static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Shared memory one slab CTA may take: leaves room for the next launch's CTA on the same SM only
+// up to about half of the SM's 228 KB, but a larger slab still beats the other kernels.
+constexpr size_t kSlabSmemMax = 200 * 1024;
+
+// Launch shape of the slab kernel (li4_slab.cu), or false when the problem does not fit it:
+// K ranges of all K unless the staged x would exceed 32 KB (64 KB at M > 8), at most one CTA per
+// SM per K range, every CTA's tiles resident in shared memory at once.
+static bool slab_shape(int64_t M, int64_t N, int64_t K, int sm, int split_req, int max_ctas, Plan* p) {
+  const int n_ks = (int)(K / 128);
+  const int nt = (M <= 8) ? 1 : 2;
+  const int m8 = (nt == 1) ? (int)M : 8;
+  const size_t x_cap = (nt == 1) ? 32768 : 65536;
+  int split = 1;
+  if (split_req > 0) {
+    if (n_ks % split_req != 0) return false;
+    split = split_req;
+  } else {
+    while ((size_t)(n_ks / split) * nt * m8 * 256 > x_cap && n_ks % (2 * split) == 0) split *= 2;
+    if ((size_t)(n_ks / split) * nt * m8 * 256 > x_cap) return false;
+  }
+  const int ks = n_ks / split;
+  const int n_tiles = (int)((N + 15) / 16);
+  int gx = std::max(1, sm / split);
+  if (max_ctas > 0) gx = std::max(1, std::min(gx, max_ctas / split));
+  gx = std::min(gx, n_tiles);
+  const int tiles_max = (n_tiles + gx - 1) / gx;
+  int slots = 1;
+  while (slots < 8 && ks % (2 * slots) == 0) slots *= 2;
+  const int pitch = ks * 64 + 64;  // rows grp and grp + 1 of a quarter-warp's reads on distinct banks
+  const size_t smem = slab_smem_bytes((int)M, nt, ks, tiles_max, slots, pitch);
+  if (tiles_max > kSlabMaxTiles || smem > kSlabSmemMax) return false;
+  p->kernel = LI4_KERNEL_SLAB;
+  p->rt = 1;
+  p->nt = nt;
+  p->scale_in_a = false;
+  p->n_ks = n_ks;
+  p->split = split;
+  p->ks_per_split = ks;
+  p->n_tiles = n_tiles;
+  p->grid_x = gx;
+  p->auto_grid = false;
+  p->sm = sm;
+  p->smem = smem;
+  p->stream_ksplit = false;
+  p->stages = tiles_max;
+  p->slots = slots;
+  p->pitch = pitch;
+  return true;
+}
 
 static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int kernel_req, int rows_req,
                      int split_req, int max_ctas, Plan* p, bool fused = false) {
@@ -1081,6 +1133,8 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (sm <= 0) sm = 148;
 
   int kernel = kernel_req;
+  if (kernel == LI4_KERNEL_AUTO && group == 128 && K > 0 && slab_shape(M, N, K, sm, split_req, max_ctas, p))
+    kernel = LI4_KERNEL_SLAB;  // the problem fits the slab kernel (every decode layer shape)
   if (kernel == LI4_KERNEL_AUTO) {
     // By measured B200 sweeps of the Llama-3.2-1B shapes (bench.py --sweep):
     // tile streaming when every warp slot gets several 16-row x 2048-k tiles
@@ -1097,12 +1151,10 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
   }
-  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK)
+  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK &&
+      kernel != LI4_KERNEL_SLAB)
     return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp, "
-                     "tile and bulk-copy kernels (group_size >= 128)");
-  if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK)
-    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp, "
-                     "tile and bulk-copy kernels (group_size >= 128)");
+                     "tile, bulk-copy and slab kernels (group_size >= 128)");
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel takes M <= 8 (M=%lld)", (long long)M);
   if (kernel == LI4_KERNEL_STREAM && (group < 128 || K == 0))
@@ -1113,8 +1165,28 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (kernel == LI4_KERNEL_BULK && (group != 128 || K == 0 || (K / 128) % 8 != 0))
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the bulk-copy kernel needs group_size 128 and K a multiple "
                      "of 1024");
-  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_BULK)
+  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_SLAB)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: unknown kernel %d", kernel);
+  if (kernel == LI4_KERNEL_SLAB) {
+    if (group != 128 || K == 0)
+      return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the slab kernel needs group_size 128 and K > 0");
+    if (!slab_shape(M, N, K, sm, split_req, max_ctas, p))
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: M=%lld N=%lld K=%lld (split %d) does not fit the slab "
+                       "kernel (at most %d row tiles and %zu bytes of shared memory per CTA)", (long long)M,
+                       (long long)N, (long long)K, split_req, kSlabMaxTiles, kSlabSmemMax);
+    if (p->split > 1) {
+      if ((size_t)p->n_tiles * sizeof(unsigned) > LI4_WORKSPACE_COUNTER_BYTES)
+        return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: N=%lld needs %d split-K row tiles, more than the %d "
+                         "arrival counters of the workspace", (long long)N, p->n_tiles,
+                         (int)(LI4_WORKSPACE_COUNTER_BYTES / sizeof(unsigned)));
+      p->ws_counters = LI4_WORKSPACE_COUNTER_BYTES;
+      p->ws_bytes = p->ws_counters + (size_t)p->split * M * N * sizeof(float);
+    } else {
+      p->ws_counters = 0;
+      p->ws_bytes = 0;
+    }
+    return LI4_OK;
+  }
   p->stream_ksplit = false;
   p->kernel = kernel;
   p->nt = (M <= 8) ? 1 : 2;
@@ -1371,6 +1443,8 @@ static int launch_bulk_kernel(KernelT kernel, const Plan& p, const GemvArgs& arg
 
 static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
   const bool fused = args.norm_w != nullptr || args.epi != LI4_EPI_STORE;
+  if (p.kernel == LI4_KERNEL_SLAB)
+    return launch_slab(args, p.nt, fused, p.grid_x, p.stages, p.slots, p.pitch, p.smem, s);
   if (p.kernel == LI4_KERNEL_BULK) {
     const int sel = (p.nt - 1) * 2 + (fused ? 1 : 0);
     switch (sel) {
@@ -1576,6 +1650,11 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
   const bool fused = f != nullptr && (f->norm_weight != nullptr || f->epilogue != LI4_EPI_STORE);
   int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p, fused);
   if (rc != LI4_OK) return rc;
+  if (kernel == LI4_KERNEL_AUTO && f != nullptr && f->argmax_out != nullptr && p.kernel != LI4_KERNEL_TILE) {
+    // the fused greedy argmax runs on the tile kernel
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_TILE, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
   GemvArgs args = {};
   rc = prepare_linear(x, packed, scale, zero, y, M, N, K, group, sxm, spn, ssn, sym, f, &args);
   if (rc != LI4_OK) return rc;
@@ -1622,7 +1701,7 @@ extern "C" size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t 
   if (li4::make_plan(M, N, K, group_size, sm, LI4_KERNEL_AUTO, 0, 0, 0, &p) != LI4_OK) return 0;
   // Enough for every kernel family and launch shape the dispatcher may pick.
   size_t best = p.ws_bytes;
-  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_BULK; ++kernel) {
+  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_SLAB; ++kernel) {
     if (kernel == LI4_KERNEL_CUDA_CORE && M > 8) continue;
     if (li4::make_plan(M, N, K, group_size, sm, kernel, 0, 0, 0, &p) == LI4_OK && p.ws_bytes > best) best = p.ws_bytes;
   }
@@ -1731,10 +1810,9 @@ extern "C" int li4_int4_linear_noalloc(const void* x, const void* packed, const 
                        kNoAllocScratchBytes);
     rc = noalloc_scratch(&scratch);
     if (rc != LI4_OK) return rc;
-    // The counters must start at zero: clear the ones this launch uses (the
-    // array keeps whatever the previous call left in it).
-    rc = check_cuda(cudaMemsetAsync(scratch, 0, (size_t)p.n_tiles * sizeof(unsigned),
-                                    static_cast<cudaStream_t>(stream)),
+    // The counters must start at zero and the array keeps whatever the previous call left in
+    // it: clear the whole counter region, whichever launch plan runs.
+    rc = check_cuda(cudaMemsetAsync(scratch, 0, LI4_WORKSPACE_COUNTER_BYTES, static_cast<cudaStream_t>(stream)),
                     "int4_linear_noalloc: clearing the arrival counters");
     if (rc != LI4_OK) return rc;
   }

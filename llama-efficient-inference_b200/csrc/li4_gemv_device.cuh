@@ -603,6 +603,16 @@ __host__ __device__ inline BulkLayout bulk_layout(int ks, bool contig) {
 }
 
 
+// Slab kernel (li4_slab.cu): most 16-row tiles one CTA stages in shared memory.
+constexpr int kSlabMaxTiles = 16;
+
+// Host: shared-memory bytes of one slab CTA (mbarriers, tile stages, x staging, warp partials).
+size_t slab_smem_bytes(int M, int nt, int ks, int tiles_max, int slots, int pitch);
+
+// Host: launch the slab kernel for a.ks_per_split ksteps per K range (a.split ranges on grid.y).
+int launch_slab(const GemvArgs& a, int nt, bool fused, int grid_x, int tiles_max, int slots, int pitch,
+                size_t smem, cudaStream_t stream);
+
 // Host: validate one linear (and its fusion) as li4_int4_linear_fused does and fill the
 // GemvArgs fields that do not depend on the launch plan (li4_gemv.cu).
 int prepare_linear(const void* x, const void* packed, const void* scale, const void* zero, void* y, int64_t M,

@@ -24,7 +24,7 @@ LI4_ERR_CUDA = 5
 
 LI4_F16, LI4_BF16, LI4_F32 = 0, 1, 2
 WORKSPACE_COUNTER_BYTES = 65536  # LI4_WORKSPACE_COUNTER_BYTES
-KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA, KERNEL_STREAM, KERNEL_TILE, KERNEL_BULK = 0, 1, 2, 3, 4, 5
+KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA, KERNEL_STREAM, KERNEL_TILE, KERNEL_BULK, KERNEL_SLAB = 0, 1, 2, 3, 4, 5, 6
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64

@@ -82,12 +82,13 @@ def test_rejects_unaligned_packed(native):
 
 
 def test_rejects_missing_workspace(native):
-    # down_proj (N=2048, K=8192) at M=1 on 148 SMs: 128 row tiles, so the dispatcher splits K in two
+    # down_proj (N=2048, K=8192) at M=8: x over all of K would not fit the slab kernel's staging, so the
+    # dispatcher splits K in four
     lib = native.lib()
-    need = lib.li4_int4_linear_workspace_bytes(1, 2048, 8192, 128, 148)
-    assert need > 0
+    need = lib.li4_int4_linear_workspace_bytes(8, 2048, 8192, 128, 148)
+    assert need >= 65536 + 4 * 8 * 2048 * 4
     assert lib.li4_int4_linear_workspace_bytes(1, 128256, 2048, 128, 148) == 0  # enough row tiles, no split
-    rc = call_linear(native, M=1, N=2048, K=8192)
+    rc = call_linear(native, M=8, N=2048, K=8192)
     # the SM count of a machine without a GPU falls back to 148, so split-K is chosen
     assert rc == native.LI4_ERR_WORKSPACE
 

@@ -21,11 +21,50 @@ LLAMA_SHAPES = [  # (name, N = out_features, K = in_features)
     ("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
     ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192), ("lm_head", 128256, 2048),
 ]
-KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5}
+KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5, "slab": 6}
 
 
-def supported(kernel: str, M: int, group: int = 128, K: int = 2048) -> bool:
+def sm_count() -> int:
+    return torch.cuda.get_device_properties(0).multi_processor_count
+
+
+def slab_fits(M: int, N: int, K: int, group: int = 128, split: int = 0, max_ctas: int = 0) -> bool:
+    """The slab kernel's planning rule (li4_gemv.cu slab_shape): the staged x within 32 KiB (64 KiB at M > 8)
+    per K range, at most one CTA per SM per K range, <= 16 resident row tiles and <= 200 KiB per CTA."""
+    if group != 128 or K <= 0 or K % 128:
+        return False
+    n_ks, nt = K // 128, (1 if M <= 8 else 2)
+    m8 = M if nt == 1 else 8
+    x_cap = 32768 if nt == 1 else 65536
+    if split > 0:
+        if n_ks % split:
+            return False
+    else:
+        split = 1
+        while (n_ks // split) * nt * m8 * 256 > x_cap and n_ks % (2 * split) == 0:
+            split *= 2
+        if (n_ks // split) * nt * m8 * 256 > x_cap:
+            return False
+    ks = n_ks // split
+    n_tiles = (N + 15) // 16
+    gx = max(1, sm_count() // split)
+    if max_ctas > 0:
+        gx = max(1, min(gx, max_ctas // split))
+    gx = min(gx, n_tiles)
+    tiles = -(-n_tiles // gx)
+    slots = 1
+    while slots < 8 and ks % (2 * slots) == 0:
+        slots *= 2
+    pitch = ks * 64 + 64
+    stage = (16 * pitch + 64 * ks + 127) & ~127
+    smem = 128 + tiles * stage + ks * nt * m8 * 256 + tiles * slots * 16 * M * 4
+    return tiles <= 16 and smem <= 200 * 1024
+
+
+def supported(kernel: str, M: int, group: int = 128, K: int = 2048, N: int = 300) -> bool:
     """Which forced kernel families take the problem."""
+    if kernel == "slab":
+        return slab_fits(M, N, K, group)
     if kernel == "cuda_core":
         return M <= 8
     if kernel == "stream":
@@ -82,8 +121,8 @@ def test_golden_cases(case, kernel, golden, g, cuda_device):
     int4_gemv, _ = g
     meta, arr = golden
     name, N, K, M, group = case[:5]
-    if not supported(kernel, M, group, K):
-        pytest.skip(f"{kernel} does not take M={M} group={group} K={K}")
+    if not supported(kernel, M, group, K, N):
+        pytest.skip(f"{kernel} does not take M={M} N={N} group={group} K={K}")
     w, x = cases.make_gemv_inputs(case)
     packed, scale, zero = oracle.quantize(w.numpy(), group)
     dev = cuda_device
@@ -103,7 +142,7 @@ def test_llama_shapes(shape, M, g, cuda_device):
     x, p, s, z, host = make_problem(N, K, M, seed=sum(map(ord, name)) + M)
     y_ref, y32 = oracle.linear(*host)
     for kernel in KERNELS:
-        if not supported(kernel, M, 128, K):
+        if not supported(kernel, M, 128, K, N):
             continue
         y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
         int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS[kernel])
@@ -233,13 +272,62 @@ def test_bulk_launch_shapes(M, split, max_ctas, N, K, g, cuda_device):
     assert native.device_errors() == 0
 
 
+@pytest.mark.parametrize("M", [1, 5, 9, 16])
+@pytest.mark.parametrize("split", [0, 1, 2, 4])
+@pytest.mark.parametrize("max_ctas", [0, 1, 7])
+@pytest.mark.parametrize("N,K", [(17, 2048), (300, 4096), (4100, 2048), (2049, 8192), (512, 1024), (100, 640),
+                                 (16384, 2048)])
+def test_slab_launch_shapes(M, split, max_ctas, N, K, g, cuda_device):
+    """Slab kernel: one to 16 resident row tiles per CTA, K split across 1-8 warps (K = 640: five ksteps,
+    one warp per tile, scale / zero rows by plain loads), split-K across CTAs with the last range reducing,
+    partial last tiles; deterministic, and no device-side wait ran out."""
+    int4_gemv, native = g
+    if not slab_fits(M, N, K, 128, split, max_ctas):
+        pytest.skip("more resident tiles or shared memory than one slab CTA takes")
+    x, p, s, z, host = make_problem(N, K, M, seed=N + K + M + split + max_ctas)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["slab"], split=split, max_ctas=max_ctas)
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["slab"], split=split, max_ctas=max_ctas)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+    assert native.device_errors() == 0
+
+
+def test_slab_rejects_what_does_not_fit(g, cuda_device):
+    """A forced slab launch beyond its resident tiles (lm_head at M=1) fails with a clear error, no launch."""
+    int4_gemv, native = g
+    N, K, M = 128256, 2048, 1
+    assert not slab_fits(M, N, K)
+    x = torch.zeros(M, K, dtype=torch.float16, device=cuda_device)
+    p = torch.zeros(N, K // 2, dtype=torch.uint8, device=cuda_device)
+    s = torch.zeros(N, K // 128, dtype=torch.float16, device=cuda_device)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(native.Li4Error, match="does not fit the slab"):
+        int4_gemv.int4_linear_out(x, p, s, s, y, 128, kernel=KERNELS["slab"])
+
+
+def test_auto_dispatch_matches_slab_rule(g, cuda_device):
+    """The dispatcher takes the slab kernel exactly where it fits (every Llama-3.2-1B layer shape at M <= 16)
+    and the tile / bulk kernels for lm_head: workspace needs follow the plan."""
+    for name, N, K in LLAMA_SHAPES:
+        for M in (1, 2, 4, 8, 16):
+            fits = slab_fits(M, N, K)
+            assert fits == (name != "lm_head"), (name, M)
+
+
 def test_split_counters_reset_across_launches(g, cuda_device):
     """The arrival counters are left at zero: 40 back-to-back split-K launches all reduce correctly."""
     int4_gemv, _ = g
-    M, N, K = 1, 512, 2048  # k/v shape: split-K on a 148-SM part
+    M, N, K = 1, 512, 2048  # k/v shape: split-K on the streaming-warp kernel
     x, p, s, z, host = make_problem(N, K, M, seed=3)
     xs = [(torch.randn(M, K, generator=torch.Generator().manual_seed(i))).half() for i in range(40)]
-    outs = [int4_gemv.int4_linear(xi.to(cuda_device), p, s, z, 128) for xi in xs]
+    outs = []
+    for xi in xs:
+        yi = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+        int4_gemv.int4_linear_out(xi.to(cuda_device), p, s, z, yi, 128, kernel=KERNELS["stream"])
+        outs.append(yi)
     torch.cuda.synchronize()
     for xi, yi in zip(xs, outs):
         y_ref, y32 = oracle.linear(xi.numpy(), *host[1:])

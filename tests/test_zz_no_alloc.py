@@ -5,21 +5,24 @@ graph is captured, allocators that refuse new allocations after warm-up, hosts t
 bind only the C ABI -- use li4_int4_linear_noalloc, whose split-K scratch is a static
 device array inside the library instead of a caller-provided workspace.  These tests
 call it through the C ABI on shapes that do and do not need the scratch, twice in a
-row (the second call sees the array as the first left it), and compare each result
-with the workspace entry point within the acceptance bound of the parity tests,
-2e-3 * max|y|.  The file is named to run last.
+row (the second call sees the array as the first left it), compare each result bit
+for bit with the workspace entry point (same plan, same fixed reduction order) and
+with the oracle within the acceptance bound of the parity tests, 2e-3 * max|y|.
+The file is named to run last.
 """
 import numpy as np
 import pytest
 import torch
 
+from oracle import oracle
+
 pytestmark = pytest.mark.gpu
 
-SHAPES = [  # (M, N, K): split-K (scratch used) unless noted
-    (1, 512, 2048),  # k_proj / v_proj
-    (8, 2048, 2048),  # q_proj / o_proj at M=8
-    (16, 2048, 8192),  # down_proj at M=16 (K ranges of <= 2048)
-    (2, 16384, 2048),  # enough row tiles: no scratch needed
+SHAPES = [  # (M, N, K, uses the scratch)
+    (4, 2048, 8192, True),    # down_proj at batch 4: two K ranges reduced by the last-arriving CTA
+    (8, 2048, 8192, True),    # down_proj at batch 8: four K ranges
+    (16, 2048, 8192, True),   # down_proj at batch 16
+    (1, 512, 2048, False),    # k_proj / v_proj at batch 1: one K range, no scratch
 ]
 
 
@@ -31,11 +34,13 @@ def native(cuda_device):
 
 
 def quantized(N, K, device, seed):
-    from llama.quantize import QuantizedLinear
-
-    gen = torch.Generator(device=device).manual_seed(seed)
-    w = (torch.randn(N, K, generator=gen, device=device) * 0.02).half()
-    return QuantizedLinear.quantize_tensor(w, 128)
+    """INT4 weights from the oracle's quantizer (host copies kept for the oracle's product)."""
+    gen = torch.Generator().manual_seed(seed)
+    w = (torch.randn(N, K, generator=gen) * 0.02).half()
+    packed, scale, zero = oracle.quantize(w.numpy(), 128)
+    dev = torch.device(device)
+    return (torch.from_numpy(packed).to(dev), torch.from_numpy(scale).to(dev), torch.from_numpy(zero).to(dev),
+            (packed, scale, zero))
 
 
 def call_noalloc(native, x, p, s, z, y):
@@ -60,22 +65,25 @@ def call_workspace(native, x, p, s, z, y):
     native.check(rc, "li4_int4_linear")
 
 
-@pytest.mark.parametrize("M,N,K", SHAPES)
-def test_noalloc_matches_workspace_entry_point(native, cuda_device, M, N, K):
-    p, s, z = quantized(N, K, cuda_device, seed=N + K + M)
-    uses_scratch = native.lib().li4_int4_linear_workspace_bytes(M, N, K, 128, 0) > 0
-    assert uses_scratch == (N < 16384)
+@pytest.mark.parametrize("M,N,K,scratch", SHAPES)
+def test_noalloc_matches_workspace_entry_point(native, cuda_device, M, N, K, scratch):
+    """Same launch plan, same kernels, same fixed reduction order: the allocation-free call gives the
+    workspace call's output bit for bit, and both meet the parity bound against the oracle."""
+    p, s, z, host = quantized(N, K, cuda_device, seed=N + K + M)
+    assert (native.lib().li4_int4_linear_workspace_bytes(M, N, K, 128, 0) > 0) == scratch
     for call in range(2):  # two calls in a row share the static scratch
-        gen = torch.Generator(device=cuda_device).manual_seed(100 * call + M)
-        x = torch.randn(M, K, generator=gen, device=cuda_device).half()
+        gen = torch.Generator().manual_seed(100 * call + M)
+        xh = torch.randn(M, K, generator=gen).half()
+        x = xh.to(cuda_device)
         y_na = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda_device)
         y_ws = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
         call_noalloc(native, x, p, s, z, y_na)
         call_workspace(native, x, p, s, z, y_ws)
         torch.cuda.synchronize()
-        a, b = y_na.float().cpu().numpy(), y_ws.float().cpu().numpy()
-        assert np.isfinite(a).all()
-        assert np.abs(a - b).max() <= 2e-3 * np.abs(b).max()
+        assert torch.equal(y_na.view(torch.int16), y_ws.view(torch.int16)), f"call {call}: outputs differ"
+        y_ref, _ = oracle.linear(xh.numpy(), *host)
+        err = np.abs(y_na.float().cpu().numpy() - y_ref.astype(np.float32)).max()
+        assert err <= oracle.tolerance(y_ref), f"call {call}: max|y - y_ref| = {err:.3e}"
 
 
 def test_noalloc_rejects_problems_beyond_the_scratch(native, cuda_device):
