@@ -1650,9 +1650,11 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
   const bool fused = f != nullptr && (f->norm_weight != nullptr || f->epilogue != LI4_EPI_STORE);
   int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p, fused);
   if (rc != LI4_OK) return rc;
-  if (kernel == LI4_KERNEL_AUTO && f != nullptr && f->argmax_out != nullptr && p.kernel != LI4_KERNEL_TILE) {
-    // the fused greedy argmax runs on the tile kernel; where that does not take the problem, the
-    // check below reports the fusion as unsupported (callers then run the argmax separately)
+  if (kernel == LI4_KERNEL_AUTO && f != nullptr && f->argmax_out != nullptr && p.kernel != LI4_KERNEL_TILE &&
+      M <= 8) {
+    // the fused greedy argmax runs on the tile kernel at M <= 8; where that does not take the
+    // problem, the check below reports the fusion as unsupported (callers then run the argmax
+    // separately)
     Plan tp = {};
     if (make_plan(M, N, K, group, sm, LI4_KERNEL_TILE, rows_req, split_req, max_ctas, &tp, fused) == LI4_OK) p = tp;
   }
