@@ -50,6 +50,7 @@ METRIC = "INT4 dequant-GEMV HBM GB/s (% of B200 peak) at M=1–16; 1B decode tok
 LAYER_SHAPES = [("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
                 ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192)]
 LM_HEAD = ("lm_head", 128256, 2048)
+FUSED_SHAPES = [("qkv_fused", 3072, 2048), ("gate_up_fused", 16384, 2048)]  # the fused decode step's linears
 N_LAYERS = 16
 GROUP = 128
 L2_BYTES = 126 * 2 ** 20
@@ -326,272 +327,12 @@ def per_shape_isolated(stream: Stream, reps: int = 5):
     return out
 
 
-SWEEP_SHAPES = LAYER_SHAPES[:2] + LAYER_SHAPES[4:5] + LAYER_SHAPES[6:] + [LM_HEAD, ("qkv_fused", 3072, 2048),
-                                                                           ("gate_up_fused", 16384, 2048)]
-KERNEL_NAMES = {0: "auto", 1: "cuda_core", 2: "mma", 3: "stream", 4: "tile", 5: "bulk"}
-
-
-def kernel_sweep(a):
-    """--sweep: every kernel family x launch shape on the decode shapes (one JSON line per config, then the
-    best per shape).  Each config is a CUDA graph of back-to-back launches over rotating weight copies
-    totalling > 3x L2, device time per launch, median of 5 replays."""
-    from llama.int4_gemv import int4_linear_out
-    from llama.quantize import QuantizedLinear
-
-    dev = torch.device("cuda", 0)
-    Ms = [int(v) for v in a.sweep_m.split(",")]
-    kernels = [int(v) for v in a.sweep_kernels.split(",")]
-    out = []
-    for name, N, K in SWEEP_SHAPES:
-        wbytes = gemv_bytes(N, K, 0)
-        copies = max(2, (3 * L2_BYTES) // wbytes + 1)
-        gen = torch.Generator(device=dev).manual_seed(N + K)
-        w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
-        p, s, z = QuantizedLinear.quantize_tensor(w, GROUP)
-        del w
-        ws = [(p, s, z)] + [(p.clone(), s.clone(), z.clone()) for _ in range(copies - 1)]
-        n_ks = K // 128
-        for M in Ms:
-            x = torch.randn(M, K, generator=gen, device=dev).half()
-            y = torch.empty(M, N, dtype=torch.float16, device=dev)
-            for kernel in kernels:
-                for rows in ((16, 32) if kernel in (1, 2, 4) else (16,)):
-                    for sp in [0] + [v for v in (1, 2, 4, 8) if n_ks % v == 0]:
-                        if kernel == 1 and M > 8:
-                            continue
-
-                        def run():
-                            for pi, si, zi in ws:
-                                int4_linear_out(x, pi, si, zi, y, GROUP, kernel=kernel, rows_per_cta=rows, split=sp)
-
-                        rec = dict(shape=name, N=N, K=K, M=M, kernel=KERNEL_NAMES[kernel], rows=rows, split=sp)
-                        try:
-                            run()
-                            torch.cuda.synchronize(dev)
-                            g = torch.cuda.CUDAGraph()
-                            with torch.cuda.graph(g):
-                                run()
-                            g.replay()
-                            ts = []
-                            for _ in range(5):
-                                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                                e0.record()
-                                g.replay()
-                                e1.record()
-                                torch.cuda.synchronize(dev)
-                                ts.append(e0.elapsed_time(e1) / copies)
-                            us = statistics.median(ts) * 1e3
-                            rec.update(us=round(us, 2), GBps=round(gemv_bytes(N, K, M) / us / 1e3, 1))
-                            del g
-                        except Exception as e:  # noqa: BLE001 -- a launch shape the family rejects
-                            rec["error"] = str(e)[:160]
-                        out.append(rec)
-                        print(json.dumps(rec), flush=True)
-        del ws
-        torch.cuda.empty_cache()
-    best = {}
-    for r in out:
-        if "us" in r and ((r["shape"], r["M"]) not in best or r["us"] < best[(r["shape"], r["M"])]["us"]):
-            best[(r["shape"], r["M"])] = r
-    for (shape, M), r in sorted(best.items()):
-        print(json.dumps({"best": shape, "M": M, **{k: r[k] for k in ("kernel", "rows", "split", "us", "GBps")}}))
-
-
-def size_floor(a):
-    """--size-floor: the time a plain HBM read of each decode-GEMV byte count takes as one launch among
-    back-to-back launches (torch's sum of fp16 buffers in a CUDA graph over rotating copies > 3x L2):
-    the per-launch floor a GEMV of that size competes with, beside the 6550 GB/s of a long copy."""
-    dev = torch.device("cuda", 0)
-    sizes = [("k_proj", gemv_bytes(512, 2048, 0)), ("q_proj", gemv_bytes(2048, 2048, 0)),
-             ("gate_proj", gemv_bytes(8192, 2048, 0)), ("gate_up_fused", gemv_bytes(16384, 2048, 0)),
-             ("lm_head", gemv_bytes(128256, 2048, 0))]
-    for name, nbytes in sizes:
-        copies = max(2, (3 * L2_BYTES) // nbytes + 1)
-        bufs = [torch.ones(nbytes // 2, dtype=torch.float16, device=dev) for _ in range(copies)]
-        out = torch.empty(1, dtype=torch.float32, device=dev)
-
-        def run():
-            for b in bufs:
-                torch.sum(b.view(1, -1), dim=1, dtype=torch.float32, out=out)
-
-        run()
-        torch.cuda.synchronize(dev)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            run()
-        ts = []
-        for _ in range(5):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize(dev)
-            ts.append(e0.elapsed_time(e1) / copies)
-        us = statistics.median(ts) * 1e3
-        print(json.dumps({"size_floor": name, "bytes": nbytes, "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}))
-        del g, bufs
-        torch.cuda.empty_cache()
-
-
-def program_report(a):
-    """--program-report: the decode program (llama.program) on the decode workloads.  (1) the 113
-    GEMVs of the step at M = 1 and 16 as one program of independent ops, and the lm_head alone;
-    (2) the Llama-3.2-1B decode step as one program at bs 1 and 16 (512-token context): launch
-    time and, from one traced launch, per op kind the mean of: poll (last CTA of the previous op
-    done -> median CTA past its wait), stage (x staging), work (wait -> units done, median CTA),
-    tail (median -> last CTA done) and span (previous op done -> this op done), in µs."""
-    from llama import fused as F_
-    from llama import program as P_
-
-    dev = torch.device("cuda", 0)
-
-    def timeit(fn, n=20):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(n):
-            fn()
-        e1.record()
-        torch.cuda.synchronize(dev)
-        return e0.elapsed_time(e1) / n * 1e3
-
-    for M in (1, 16):
-        st = Stream(dev, M)
-        prog = P_.Program()
-        for x, (p, s, z), y in zip(st.xs, st.weights, st.ys):
-            prog.linear(x, p, s, z, y)
-        prog.finalize()
-        us = timeit(prog.launch)
-        lm = P_.Program()
-        lm.linear(st.xs[-1], *st.weights[-1], st.ys[-1])
-        lm.finalize()
-        us_lm = timeit(lm.launch)
-        print(json.dumps({"program": "gemv_list", "M": M, "ops": prog.n_ops, "us": round(us, 1),
-                          "GBps": round(st.bytes_per_step / us / 1e3, 1), "lm_head_us": round(us_lm, 1),
-                          "lm_head_GBps": round(gemv_bytes(*LM_HEAD[1:], M) / us_lm / 1e3, 1), **prog.info()}),
-              flush=True)
-        del st, prog, lm
-        torch.cuda.empty_cache()
-    names = ["gather"] + ["qkv", "attention", "wo", "gate_up", "down"] * N_LAYERS + ["lm_head", "argmax"]
-    for bs in (1, 16):
-        model = build_decode_model(dev, bs, 640)
-        dec = F_.FusedDecoder(model, program=True)
-        tok = torch.randint(0, model.params.vocab_size, (bs, 1), device=dev)
-        pos = torch.tensor([512], dtype=torch.long, device=dev)
-        dec.decode_step(tok, pos, next_tokens=tok)
-        prog = [p for p in dec._programs.values() if p is not None][0]
-        info = prog.info()
-        G, n = info["ctas"], info["ops"]
-        us = timeit(prog.launch)
-        stamps = torch.zeros(n, G, 4, dtype=torch.long, device=dev)
-        prog.set_trace(stamps)
-        prog.launch()
-        torch.cuda.synchronize(dev)
-        prog.set_trace(None)
-        s = stamps.cpu().numpy()
-        t0 = s[s > 0].min()
-        agg, prev_end = {}, None
-        for j in range(n):
-            act = s[j][:, 0] > 0
-            if not act.any():
-                continue
-            r = s[j][act] - t0
-            end = r[:, 3].max()
-            staged = r[:, 2] > 0
-            d = {"poll": (statistics.median(r[:, 1]) - prev_end) if prev_end is not None else 0.0,
-                 "stage": statistics.median(r[staged, 2] - r[staged, 1]) if staged.any() else 0.0,
-                 "work": statistics.median(r[:, 3] - r[:, 1]), "tail": end - statistics.median(r[:, 3]),
-                 "span": end - (prev_end if prev_end is not None else r[:, 0].min())}
-            agg.setdefault(names[j] if j < len(names) else str(j), []).append(d)
-            prev_end = end
-        ops = {k: {q: round(float(statistics.mean(x[q] for x in v)) / 1e3, 2) for q in v[0]} for k, v in agg.items()}
-        print(json.dumps({"program": "decode_step", "bs": bs, "launch_us": round(us, 1), **info, "per_op_us": ops}),
-              flush=True)
-        del dec, model, prog
-        torch.cuda.empty_cache()
-
-
-def fused_cost(a):
-    """--fused-cost: each fused decode GEMV (llama.fused) against the same GEMV without its prologue /
-    epilogue, µs per launch in a CUDA graph of back-to-back launches over rotating weight copies."""
-    from llama import _native as E
-    from llama import fused
-    from llama.quantize import QuantizedLinear
-
-    dev = torch.device("cuda", 0)
-
-    def timeit(fn, copies):
-        fn()
-        torch.cuda.synchronize(dev)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            fn()
-        g.replay()
-        torch.cuda.synchronize(dev)
-        ts = []
-        for _ in range(5):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize(dev)
-            ts.append(e0.elapsed_time(e1) / copies)
-        return round(statistics.median(ts) * 1e3, 2)
-
-    for M in (1, 16):
-        for name, N, K in (("qkv_fused", 3072, 2048), ("o_proj", 2048, 2048), ("gate_up_fused", 16384, 2048),
-                           ("down_proj", 2048, 8192)):
-            copies = max(2, 3 * L2_BYTES // gemv_bytes(N, K, 0) + 1)
-            gen = torch.Generator(device=dev).manual_seed(N + K)
-            w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
-            p, s, z = QuantizedLinear.quantize_tensor(w, GROUP)
-            del w
-            ws = [(p, s, z)] + [(p.clone(), s.clone(), z.clone()) for _ in range(copies - 1)]
-            x = torch.randn(M, K, generator=gen, device=dev).half()
-            y = torch.empty(M, N, dtype=torch.float16, device=dev)
-            nw = torch.ones(K, dtype=torch.float16, device=dev)
-            res = torch.randn(M, N, generator=gen, device=dev).half()
-            pos = torch.tensor([5], dtype=torch.long, device=dev)
-            cos, sin = torch.ones(64, 32, device=dev), torch.zeros(64, 32, device=dev)
-            q = torch.empty(M, 2048, dtype=torch.float16, device=dev)
-            ck = torch.zeros(M, 64, 8, 64, dtype=torch.float16, device=dev)
-            cv = torch.zeros_like(ck)
-
-            def run(f):
-                def go():
-                    for pi, si, zi in ws:
-                        fused.int4_linear_fused(x, pi, si, zi, None if f.epilogue == E.LI4_EPI_QKV_ROPE else y, f)
-                return go
-
-            rec = {"fused_cost": name, "M": M, "plain": timeit(run(E.Fusion(epilogue=E.LI4_EPI_STORE)), copies)}
-            if name in ("qkv_fused", "gate_up_fused"):
-                rec["norm"] = timeit(run(E.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5, epilogue=E.LI4_EPI_STORE)),
-                                     copies)
-            if name == "qkv_fused":
-                rec["norm+rope"] = timeit(run(E.Fusion(
-                    norm_weight=nw.data_ptr(), norm_eps=1e-5, epilogue=E.LI4_EPI_QKV_ROPE, q_rows=2048, k_rows=512,
-                    head_dim=64, pos=pos.data_ptr(), rope_cos=cos.data_ptr(), rope_sin=sin.data_ptr(), rope_stride=32,
-                    q_out=q.data_ptr(), stride_qm=2048, cache_k=ck.data_ptr(), cache_v=cv.data_ptr(),
-                    cache_stride_b=ck.stride(0), cache_stride_s=ck.stride(1))), copies)
-            if name == "gate_up_fused":
-                rec["norm+swiglu"] = timeit(run(E.Fusion(norm_weight=nw.data_ptr(), norm_eps=1e-5,
-                                                         epilogue=E.LI4_EPI_SWIGLU)), copies)
-            if name in ("o_proj", "down_proj"):
-                rec["residual"] = timeit(run(E.Fusion(epilogue=E.LI4_EPI_RESIDUAL, residual=res.data_ptr(),
-                                                      stride_rm=N)), copies)
-            print(json.dumps(rec), flush=True)
-            del ws
-            torch.cuda.empty_cache()
-
-
 def profile_shape(a):
     """--profile-shape NAME: `--launches` eager launches of one shape (a small case for ncu captures)."""
     from llama.int4_gemv import int4_linear_out
     from llama.quantize import QuantizedLinear
 
-    shapes = {n: (N, K) for n, N, K in LAYER_SHAPES + SWEEP_SHAPES + [LM_HEAD]}
+    shapes = {n: (N, K) for n, N, K in LAYER_SHAPES + FUSED_SHAPES + [LM_HEAD]}
     N, K = shapes[a.profile_shape]
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(0)
@@ -952,33 +693,12 @@ def main():
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
-    ap.add_argument("--sweep", action="store_true", help="kernel-family x launch-shape sweep of the decode shapes")
-    ap.add_argument("--program-report", action="store_true",
-                    help="the decode program (one persistent launch): GEMV-list and decode-step timings, per-op trace")
-    ap.add_argument("--fused-cost", action="store_true",
-                    help="each fused decode GEMV against the same GEMV without its prologue / epilogue")
-    ap.add_argument("--size-floor", action="store_true",
-                    help="time a plain HBM read of each decode-GEMV byte count as back-to-back launches")
-    ap.add_argument("--sweep-m", default="1,8,16")
-    ap.add_argument("--sweep-kernels", default="0,1,2,3,4,5", help="0 auto, 1 cuda_core, 2 mma, 3 stream, 4 tile, 5 bulk")
     a = ap.parse_args()
     if a.profile_shape:
         profile_shape(a)
         return
     if a.profile_attention:
         profile_attention(a)
-        return
-    if a.sweep:
-        kernel_sweep(a)
-        return
-    if a.size_floor:
-        size_floor(a)
-        return
-    if a.fused_cost:
-        fused_cost(a)
-        return
-    if a.program_report:
-        program_report(a)
         return
     if a.warmup < 3:
         a.warmup = 3

@@ -108,6 +108,18 @@ int li4_int4_linear_ex(const void* x, const void* packed, const void* scale, con
                        void* workspace, size_t workspace_bytes, void* stream,
                        int kernel, int rows_per_cta, int split, int max_ctas);
 
+/* The launch plan li4_int4_linear chooses for this problem on a device with
+ * `sm_count` SMs (0 = the current device), for contiguous, 16-byte aligned
+ * operands: the kernel family (li4_kernel), the number of K ranges (split),
+ * the CTAs along N per K range (grid_x; the streaming-warp and tile kernels
+ * cap it by occupancy at launch) and the dynamic shared memory per CTA.  Any
+ * output pointer may be null.  Launches nothing.
+ * Replaces: nothing in the reference, whose int4_linear picks split-K in
+ * _split_k (llama/int4_gemv.py:95-102) without reporting it; benchmarks and
+ * profiles use it to name the kernel each shape runs on. */
+int li4_int4_linear_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count,
+                         int* kernel, int* split, int* grid_x, size_t* smem_bytes);
+
 /* Size of the static device scratch behind li4_int4_linear_noalloc. */
 #define LI4_NOALLOC_SCRATCH_BYTES (4u << 20)
 

@@ -1711,6 +1711,20 @@ extern "C" size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t 
   return best;
 }
 
+extern "C" int li4_int4_linear_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count, int* kernel,
+                                    int* split, int* grid_x, size_t* smem_bytes) {
+  li4::Plan p = {};
+  const int sm = sm_count > 0 ? sm_count : li4::current_sm_count();
+  const int rc = li4::make_plan(M, N, K, group_size, sm, LI4_KERNEL_AUTO, 0, 0, 0, &p);
+  if (rc != LI4_OK) return rc;
+  if (kernel) *kernel = p.kernel;
+  if (split) *split = p.split;
+  if (grid_x) *grid_x = p.grid_x;
+  if (smem_bytes) *smem_bytes = p.smem;
+  li4::clear_error();
+  return LI4_OK;
+}
+
 extern "C" int li4_int4_linear(const void* x, const void* packed, const void* scale, const void* zero, void* y,
                                int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t stride_xm,
                                int64_t stride_pn, int64_t stride_sn, int64_t stride_ym, void* workspace,

@@ -70,6 +70,8 @@ SIGNATURES = {
     "li4_version": (_INT, []),
     "li4_last_error": (ctypes.c_char_p, []),
     "li4_int4_linear_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _INT]),
+    "li4_int4_linear_plan": (_INT, [_I64, _I64, _I64, _I64, _INT, ctypes.POINTER(_INT), ctypes.POINTER(_INT),
+                                    ctypes.POINTER(_INT), ctypes.POINTER(_SZ)]),
     "li4_int4_linear": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "li4_int4_linear_ex": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
                                   _INT, _INT, _INT, _INT]),
@@ -149,6 +151,21 @@ def device_errors(reset: bool = True) -> int:
     flags = ctypes.c_uint(0)
     check(lib().li4_device_errors(ctypes.byref(flags), int(reset)), "device_errors")
     return flags.value
+
+
+KERNEL_NAMES = {KERNEL_CUDA_CORE: "cuda_core", KERNEL_MMA: "mma", KERNEL_STREAM: "stream", KERNEL_TILE: "tile",
+                KERNEL_BULK: "bulk", KERNEL_SLAB: "slab"}
+KERNEL_SYMBOLS = {KERNEL_CUDA_CORE: "gemv_cc_kernel", KERNEL_MMA: "gemv_mma_kernel", KERNEL_STREAM: "gemv_stream_kernel",
+                  KERNEL_TILE: "gemv_tile_kernel", KERNEL_BULK: "gemv_bulk_kernel", KERNEL_SLAB: "gemv_slab_kernel"}
+
+
+def plan(M: int, N: int, K: int, group_size: int = 128, sm_count: int = 0) -> dict:
+    """The launch plan li4_int4_linear picks for a contiguous problem (li4_int4_linear_plan)."""
+    k, sp, gx, sm = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    check(lib().li4_int4_linear_plan(M, N, K, group_size, sm_count, ctypes.byref(k), ctypes.byref(sp),
+                                     ctypes.byref(gx), ctypes.byref(sm)), "int4_linear_plan")
+    return {"kernel": KERNEL_NAMES.get(k.value, str(k.value)), "symbol": KERNEL_SYMBOLS.get(k.value, ""),
+            "split": sp.value, "grid_x": gx.value, "smem": sm.value}
 
 
 def stream_ptr(device: torch.device) -> int:
