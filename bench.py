@@ -341,11 +341,12 @@ def profile_shape(a):
     del w
     x = torch.randn(a.m, K, generator=gen, device=dev).half()
     y = torch.empty(a.m, N, dtype=torch.float16, device=dev)
+    kernel = {"auto": 0, "stream": 3, "tile": 4, "bulk": 5, "slab": 6}[a.kernel]
     for _ in range(a.launches):
-        int4_linear_out(x, p, s, z, y, GROUP)
+        int4_linear_out(x, p, s, z, y, GROUP, kernel=kernel)
     torch.cuda.synchronize(dev)
     print(json.dumps({"profile_shape": a.profile_shape, "N": N, "K": K, "M": a.m, "launches": a.launches,
-                      "bytes_per_launch": gemv_bytes(N, K, a.m)}))
+                      "kernel": a.kernel, "bytes_per_launch": gemv_bytes(N, K, a.m)}))
 
 
 def profile_attention(a):
@@ -691,6 +692,8 @@ def main():
     ap.add_argument("--profile-attention", type=int, default=0, metavar="BS",
                     help="only run --launches decode-attention launches at batch BS (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--kernel", default="auto", choices=["auto", "stream", "tile", "bulk", "slab"],
+                    help="kernel family for --profile-shape (default: the dispatcher's choice)")
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
     a = ap.parse_args()

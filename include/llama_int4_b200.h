@@ -54,9 +54,12 @@ typedef enum li4_kernel {
   LI4_KERNEL_TILE = 4,       /* tile-streaming warps: group 128, K ranges of 2048  */
   LI4_KERNEL_BULK = 5,       /* bulk-copy ring in shared memory: group 128,
                                 K % 1024 == 0, 16-byte aligned scale / zero rows   */
-  LI4_KERNEL_SLAB = 6        /* whole weight slice of a CTA resident in shared
+  LI4_KERNEL_SLAB = 6,       /* whole weight slice of a CTA resident in shared
                                 memory, K split across its warps: group 128, up to
                                 16 row tiles per CTA                              */
+  LI4_KERNEL_ROWS = 7        /* a warp's two rows unpacked in registers before the
+                                dependency wait: M = 1, group 128, K = 1024 or 2048,
+                                16-byte aligned x; no RMSNorm prologue or argmax  */
 } li4_kernel;
 
 /* Library version, (major << 16) | (minor << 8) | patch.  0.2: li4_fusion has the argmax_*

@@ -1133,8 +1133,11 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (sm <= 0) sm = 148;
 
   int kernel = kernel_req;
-  if (kernel == LI4_KERNEL_AUTO && group == 128 && K > 0 && slab_shape(M, N, K, sm, split_req, max_ctas, p))
-    kernel = LI4_KERNEL_SLAB;  // the problem fits the slab kernel (every decode layer shape)
+  // register rows at M = 1 while the tiles fill at most two CTAs per SM (q / k / v / o_proj; the
+  // caller re-plans when x is not 16-byte aligned or the fusion needs the RMSNorm prologue)
+  if (kernel == LI4_KERNEL_AUTO && M == 1 && group == 128 && (K == 1024 || K == 2048) && split_req <= 0 &&
+      max_ctas <= 0 && (N + 15) / 16 <= 2LL * sm)
+    kernel = LI4_KERNEL_ROWS;
   if (kernel == LI4_KERNEL_AUTO) {
     // By measured B200 sweeps of the Llama-3.2-1B shapes (bench.py --sweep):
     // tile streaming when every warp slot gets several 16-row x 2048-k tiles
@@ -1152,7 +1155,7 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
   }
   if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK &&
-      kernel != LI4_KERNEL_SLAB)
+      kernel != LI4_KERNEL_SLAB && kernel != LI4_KERNEL_ROWS)
     return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp, "
                      "tile, bulk-copy and slab kernels (group_size >= 128)");
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
@@ -1165,8 +1168,29 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (kernel == LI4_KERNEL_BULK && (group != 128 || K == 0 || (K / 128) % 8 != 0))
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the bulk-copy kernel needs group_size 128 and K a multiple "
                      "of 1024");
-  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_SLAB)
+  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_ROWS)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: unknown kernel %d", kernel);
+  if (kernel == LI4_KERNEL_ROWS) {
+    if (M != 1 || group != 128 || (K != 1024 && K != 2048))
+      return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the register-rows kernel takes M = 1, group_size 128 and "
+                       "K = 1024 or 2048 (M=%lld K=%lld)", (long long)M, (long long)K);
+    p->kernel = kernel;
+    p->rt = 1;
+    p->nt = 1;
+    p->scale_in_a = false;
+    p->n_ks = (int)(K / 128);
+    p->split = 1;
+    p->ks_per_split = p->n_ks;
+    p->n_tiles = (int)((N + 15) / 16);
+    p->grid_x = p->n_tiles;
+    p->auto_grid = false;
+    p->sm = sm;
+    p->smem = 0;
+    p->stream_ksplit = false;
+    p->ws_counters = 0;
+    p->ws_bytes = 0;
+    return LI4_OK;
+  }
   if (kernel == LI4_KERNEL_SLAB) {
     if (group != 128 || K == 0)
       return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the slab kernel needs group_size 128 and K > 0");
@@ -1445,6 +1469,7 @@ static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
   const bool fused = args.norm_w != nullptr || args.epi != LI4_EPI_STORE;
   if (p.kernel == LI4_KERNEL_SLAB)
     return launch_slab(args, p.nt, fused, p.grid_x, p.stages, p.slots, p.pitch, p.smem, s);
+  if (p.kernel == LI4_KERNEL_ROWS) return launch_rows(args, fused, s);
   if (p.kernel == LI4_KERNEL_BULK) {
     const int sel = (p.nt - 1) * 2 + (fused ? 1 : 0);
     switch (sel) {
@@ -1650,6 +1675,15 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
   const bool fused = f != nullptr && (f->norm_weight != nullptr || f->epilogue != LI4_EPI_STORE);
   int rc = make_plan(M, N, K, group, sm, kernel, rows_req, split_req, max_ctas, &p, fused);
   if (rc != LI4_OK) return rc;
+  if (p.kernel == LI4_KERNEL_ROWS &&
+      (!aligned16(x) || (f != nullptr && (f->norm_weight != nullptr || f->argmax_out != nullptr)))) {
+    // the register-rows kernel reads x in 16-byte pieces and has no RMSNorm prologue or argmax
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: the register-rows kernel needs a 16-byte aligned x and "
+                       "no RMSNorm prologue or fused argmax");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
   if (kernel == LI4_KERNEL_AUTO && f != nullptr && f->argmax_out != nullptr && p.kernel != LI4_KERNEL_TILE &&
       M <= 8) {
     // the fused greedy argmax runs on the tile kernel at M <= 8; where that does not take the
@@ -1704,7 +1738,7 @@ extern "C" size_t li4_int4_linear_workspace_bytes(int64_t M, int64_t N, int64_t 
   if (li4::make_plan(M, N, K, group_size, sm, LI4_KERNEL_AUTO, 0, 0, 0, &p) != LI4_OK) return 0;
   // Enough for every kernel family and launch shape the dispatcher may pick.
   size_t best = p.ws_bytes;
-  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_SLAB; ++kernel) {
+  for (int kernel = LI4_KERNEL_CUDA_CORE; kernel <= LI4_KERNEL_ROWS; ++kernel) {
     if (kernel == LI4_KERNEL_CUDA_CORE && M > 8) continue;
     if (li4::make_plan(M, N, K, group_size, sm, kernel, 0, 0, 0, &p) == LI4_OK && p.ws_bytes > best) best = p.ws_bytes;
   }

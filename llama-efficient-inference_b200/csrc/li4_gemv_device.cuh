@@ -562,6 +562,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` with the non-blocking test (a completed phase costs one
+// test), at most kBulkWaitLimit polls; a wait that runs out sets bit 0 of the device error word.
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, unsigned parity) {
+  for (unsigned i = 0; i < kBulkWaitLimit; ++i)
+    if (mbar_test_wait(bar, parity)) return true;
+  atomicOr(&g_li4_device_error, 1u);
+  return false;
+}
+
 // Wait for phase `parity` of `bar` to complete, at most kBulkWaitLimit rounds.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
   for (unsigned i = 0; i < kBulkWaitLimit; ++i)
@@ -612,6 +631,9 @@ size_t slab_smem_bytes(int M, int nt, int ks, int tiles_max, int slots, int pitc
 // Host: launch the slab kernel for a.ks_per_split ksteps per K range (a.split ranges on grid.y).
 int launch_slab(const GemvArgs& a, int nt, bool fused, int grid_x, int tiles_max, int slots, int pitch,
                 size_t smem, cudaStream_t stream);
+
+// Host: launch the register-rows kernel (li4_rows.cu): M = 1, K = 1024 or 2048, 16-byte aligned x.
+int launch_rows(const GemvArgs& a, bool fused, cudaStream_t stream);
 
 // Host: validate one linear (and its fusion) as li4_int4_linear_fused does and fill the
 // GemvArgs fields that do not depend on the launch plan (li4_gemv.cu).

@@ -51,8 +51,12 @@ struct SlabSum {
   const float* base;  // red + tile * slots * 16 * M
   int slots, M;
   __device__ __forceinline__ float operator()(int r, int m) const {
+    float p[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) p[s] = s < slots ? base[(s * 16 + r) * M + m] : 0.f;
     float v = 0.f;
-    for (int s = 0; s < slots; ++s) v += base[(s * 16 + r) * M + m];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) v += p[s];  // slot order (the zero tail adds nothing)
     return v;
   }
 };
@@ -63,25 +67,40 @@ struct SlabSum {
 template <int NT, bool NORM>
 __device__ __forceinline__ void slab_stage_x(const GemvArgs& a, int ks0, int nks, int M8, uint8_t* xs,
                                              const float* s_rstd) {
-  constexpr int U = 8;
+  constexpr int U = 4;
   const int rows = NT * M8;
   const int items = nks * 16 * rows;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
   for (int i0 = threadIdx.x; i0 < items; i0 += U * kSlabThreads) {
     uint4 v[U];
+    if (vec_ok) {
+      // every load of the round issued before any is used: out-of-range items read x[0][k0]
+      // (in bounds) and are zeroed afterwards, so there is no branch between the loads
+      const __half* src[U];
+      bool live[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int i = i0 + u * kSlabThreads;
-      v[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (i < items) {
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kSlabThreads;
         const int c = i / rows, j = i - c * rows;
         const int m = (j / M8) * 8 + (j % M8);
-        if (m < a.M) {
-          const long long k = (long long)ks0 * 128 + (long long)c * 8;
-          const __half* src = a.x + (long long)m * a.sxm + k;
-          if (vec_ok) {
-            v[u] = *reinterpret_cast<const uint4*>(src);
-          } else {
+        live[u] = i < items && m < a.M;
+        src[u] = live[u] ? a.x + (long long)m * a.sxm + (long long)ks0 * 128 + (long long)c * 8 : a.x;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = *reinterpret_cast<const uint4*>(src[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (!live[u]) v[u] = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kSlabThreads;
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (i < items) {
+          const int c = i / rows, j = i - c * rows;
+          const int m = (j / M8) * 8 + (j % M8);
+          if (m < a.M) {
+            const __half* src = a.x + (long long)m * a.sxm + (long long)ks0 * 128 + (long long)c * 8;
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -118,6 +137,73 @@ __device__ __forceinline__ void slab_stage_x(const GemvArgs& a, int ks0, int nks
   }
 }
 
+// The A fragments of one 16-row x 128-k unit (exact q - zero in fp16, mma.m16n8k16 order: word
+// 8w + {0..3} / {4..7} are the A registers of the unit's two MMAs on 16-byte chunk w) and the two
+// row scales.  Unpacking needs no x, so a warp builds its first units' fragments before the
+// dependency wait, while the preceding kernel still runs.
+struct SlabFrag {
+  uint32_t a[32];
+  float s_lo, s_hi;
+};
+
+__device__ __forceinline__ void slab_unpack(SlabFrag& f, const uint8_t* row_lo, const uint8_t* row_hi,
+                                            const unsigned short* sc, const unsigned short* ze, int grp, int ks,
+                                            int ks_n) {
+  const uint4 lo = lds128(row_lo + ks * 64), hi = lds128(row_hi + ks * 64);
+  const unsigned short zlo = ze[grp * ks_n + ks], zhi = ze[(grp + 8) * ks_n + ks];
+  f.s_lo = __half2float(__ushort_as_half(sc[grp * ks_n + ks]));
+  f.s_hi = __half2float(__ushort_as_half(sc[(grp + 8) * ks_n + ks]));
+  const ZeroConsts zl = make_zero_consts(__ushort_as_half(zlo)), zh = make_zero_consts(__ushort_as_half(zhi));
+  const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w}, wh[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    __half2 pl[4], ph[4];
+    unpack8_qz(wl[w], zl, pl);
+    unpack8_qz(wh[w], zh, ph);
+    f.a[8 * w + 0] = h2_as_u32(pl[0]);
+    f.a[8 * w + 1] = h2_as_u32(ph[0]);
+    f.a[8 * w + 2] = h2_as_u32(pl[1]);
+    f.a[8 * w + 3] = h2_as_u32(ph[1]);
+    f.a[8 * w + 4] = h2_as_u32(pl[2]);
+    f.a[8 * w + 5] = h2_as_u32(ph[2]);
+    f.a[8 * w + 6] = h2_as_u32(pl[3]);
+    f.a[8 * w + 7] = h2_as_u32(ph[3]);
+  }
+}
+
+// acc += s * (W[unit rows] . x[kstep]): the unit's 8 MMAs on four independent accumulators
+// (dependency depth 2), summed pairwise, then scaled per row in fp32.
+template <int NT>
+__device__ __forceinline__ void slab_mma(const SlabFrag& f, const uint8_t* xs_ks, int nt_stride, const int boff[4],
+                                         bool bvalid, float acc[NT][4]) {
+  float c[4][NT][4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[w][nt][e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      uint4 bq = make_uint4(0u, 0u, 0u, 0u);
+      if (bvalid) bq = lds128(xs_ks + nt * nt_stride + boff[w]);
+      mma_16816(c[w][nt], f.a[8 * w + 0], f.a[8 * w + 1], f.a[8 * w + 2], f.a[8 * w + 3], bq.x, bq.y);
+      mma_16816(c[w][nt], f.a[8 * w + 4], f.a[8 * w + 5], f.a[8 * w + 6], f.a[8 * w + 7], bq.z, bq.w);
+    }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = (c[0][nt][e] + c[1][nt][e]) + (c[2][nt][e] + c[3][nt][e]);
+    acc[nt][0] = fmaf(f.s_lo, v[0], acc[nt][0]);
+    acc[nt][1] = fmaf(f.s_lo, v[1], acc[nt][1]);
+    acc[nt][2] = fmaf(f.s_hi, v[2], acc[nt][2]);
+    acc[nt][3] = fmaf(f.s_hi, v[3], acc[nt][3]);
+  }
+}
+
 template <int NT, bool FUSED>
 __global__ void __launch_bounds__(kSlabThreads, 2) gemv_slab_kernel(const __grid_constant__ GemvArgs a,
                                                                    const __grid_constant__ SlabArgs sa) {
@@ -126,6 +212,7 @@ __global__ void __launch_bounds__(kSlabThreads, 2) gemv_slab_kernel(const __grid
   const int ks0 = blockIdx.y * ks_n;
   const int M8 = (NT == 1) ? a.M : 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 2, quad = lane & 3;
   const int t_begin = (int)((long long)blockIdx.x * a.n_tiles / gridDim.x);
   const int t_end = (int)((long long)(blockIdx.x + 1) * a.n_tiles / gridDim.x);
   const int my_tiles = t_end - t_begin;
@@ -170,7 +257,7 @@ __global__ void __launch_bounds__(kSlabThreads, 2) gemv_slab_kernel(const __grid
         const int r = min(tile * 16 + j, a.N - 1);
         bulk_g2s(sc + j * sz_row, a.scale + (long long)r * a.ssn + ks0, sz_row, &bars[t]);
         bulk_g2s(ze + j * sz_row, a.zero + (long long)r * a.ssn + ks0, sz_row, &bars[t]);
-      } else {  // rows not 16-byte aligned: plain loads (seen by the consumers through the barrier below)
+      } else {  // rows not 16-byte aligned: plain loads (seen by the other warps through the barrier below)
         const int j = lane - 16;
         const int r = min(tile * 16 + j, a.N - 1);
         const unsigned short* gs = reinterpret_cast<const unsigned short*>(a.scale) + (long long)r * a.ssn + ks0;
@@ -189,11 +276,47 @@ __global__ void __launch_bounds__(kSlabThreads, 2) gemv_slab_kernel(const __grid
     // was written long before.
     const int lines_per_row = (ks_n * 256 + 127) / 128;
     const int lines = lines_per_row * a.M;
-    for (int l = threadIdx.x - 32; l < lines; l += kSlabThreads - 32) {
+    for (int l = (int)threadIdx.x - 32; l < lines; l += kSlabThreads - 32) {
       const int m = l / lines_per_row, c = l - m * lines_per_row;
       asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint8_t*>(a.x + (long long)m * a.sxm +
                                                                                        (long long)ks0 * 128) + c * 128));
     }
+  }
+  if (sa.sz_mode == 2) __syncthreads();  // scale / zero rows written by plain stores above
+
+  // ---- this warp's units: tiles phase, phase + P, ...; ksteps slot, slot + S, ... of each
+  const int S = sa.slots, P = kSlabWarps / S;
+  const int slot = warp & (S - 1), phase = warp / S;
+  const int per_tile = ks_n / S;  // ksteps of one tile this warp takes (S divides ks_n)
+  const int warp_tiles = my_tiles > phase ? (my_tiles - phase + P - 1) / P : 0;
+  const int n_units = warp_tiles * per_tile;
+  const uint8_t* row_lo0 = stages + grp * sa.pitch + quad * 16;
+  auto unit_tile = [&](int u) { return phase + (u / per_tile) * P; };
+  auto unit_ks = [&](int u) { return slot + (u % per_tile) * S; };
+  auto unpack_unit = [&](SlabFrag& f, int u) {
+    const int t = unit_tile(u);
+    const uint8_t* st = stages + (size_t)t * sa.stage;
+    const unsigned short* sc = reinterpret_cast<const unsigned short*>(st + 16 * sa.pitch);
+    const uint8_t* rl = row_lo0 + (size_t)t * sa.stage;
+    slab_unpack(f, rl, rl + 8 * sa.pitch, sc, sc + 16 * ks_n, grp, unit_ks(u), ks_n);
+  };
+
+  // Before the dependency wait: every tile this warp reads has landed (its weights were
+  // requested at entry, so this overlaps the preceding kernel), and the first two units are
+  // unpacked into registers.
+  bool ok = true;
+  for (int t = phase; t < my_tiles && ok; t += P) ok = mbar_spin_bounded(&bars[t], 0);
+  SlabFrag f0, f1;
+  if (ok && n_units > 0) unpack_unit(f0, 0);
+  if (ok && n_units > 1) unpack_unit(f1, 1);
+  {
+    // Keep the unpack above the dependency wait (the compiler would sink it below to save
+    // registers): a branch on every unpacked word, taken only when N < 1 (never), must be
+    // evaluated before the wait.
+    uint32_t fold = 0u;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) fold ^= f0.a[i] ^ f1.a[i];
+    if (a.N < 1 && fold == 0u) atomicOr(&g_li4_device_error, 0u);
   }
 
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
@@ -211,49 +334,52 @@ __global__ void __launch_bounds__(kSlabThreads, 2) gemv_slab_kernel(const __grid
   __syncthreads();
 
   // ---- tensor-core work on the resident tiles
-  const int grp = lane >> 2, quad = lane & 3;
-  const int S = sa.slots, P = kSlabWarps / S;
-  const int slot = warp & (S - 1), phase = warp / S;
   const bool bvalid = grp < M8;
   int boff[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) boff[w] = (grp * 4 + quad) * 64 + ((w ^ xs_key(grp, quad)) << 4);
   const int nt_stride = M8 * 256;
   const int ks_stride = NT * nt_stride;
-  bool ok = true;
-  for (int t = phase; t < my_tiles; t += P) {
-    if (ok) ok = mbar_wait_bounded(&bars[t], 0);
-    float acc[NT][4];
+  float acc[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-    if (ok) {
-      const uint8_t* st = stages + (size_t)t * sa.stage;
-      const unsigned short* sc = reinterpret_cast<const unsigned short*>(st + 16 * sa.pitch);
-      const unsigned short* ze = sc + 16 * ks_n;
-      const uint8_t* row_lo = st + grp * sa.pitch + quad * 16;
-      const uint8_t* row_hi = row_lo + 8 * sa.pitch;
-#pragma unroll 2
-      for (int ks = slot; ks < ks_n; ks += S) {
-        StreamUnit u;
-        u.lo = lds128(row_lo + ks * 64);
-        u.hi = lds128(row_hi + ks * 64);
-        u.sz_lo = (uint32_t)sc[grp * ks_n + ks] | ((uint32_t)ze[grp * ks_n + ks] << 16);
-        u.sz_hi = (uint32_t)sc[(grp + 8) * ks_n + ks] | ((uint32_t)ze[(grp + 8) * ks_n + ks] << 16);
-        stream_compute<NT>(u, xs + ks * ks_stride, nt_stride, boff, bvalid, acc);
-      }
-    }
-    float* rb = red + (size_t)(t * S + slot) * 16 * a.M;
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+  // after unit u: a finished tile's partial goes to red[(t * S + slot) * 16 + r][m]
+  auto finish_unit = [&](int u) {
+    if (u % per_tile != per_tile - 1) return;
+    float* rb = red + (size_t)(unit_tile(u) * S + slot) * 16 * a.M;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = grp + 8 * (e >> 1), m = nt * 8 + 2 * quad + (e & 1);
         if (m < a.M) rb[r * a.M + m] = acc[nt][e];
+        acc[nt][e] = 0.f;
       }
+  };
+  if (ok) {
+    if (n_units > 0) {
+      slab_mma<NT>(f0, xs + unit_ks(0) * ks_stride, nt_stride, boff, bvalid, acc);
+      finish_unit(0);
+    }
+    if (n_units > 1) {
+      slab_mma<NT>(f1, xs + unit_ks(1) * ks_stride, nt_stride, boff, bvalid, acc);
+      finish_unit(1);
+    }
+    for (int u = 2; u < n_units; u += 2) {  // two units in flight: both unpacked, then both multiplied
+      const bool two = u + 1 < n_units;
+      unpack_unit(f0, u);
+      if (two) unpack_unit(f1, u + 1);
+      slab_mma<NT>(f0, xs + unit_ks(u) * ks_stride, nt_stride, boff, bvalid, acc);
+      finish_unit(u);
+      if (two) {
+        slab_mma<NT>(f1, xs + unit_ks(u + 1) * ks_stride, nt_stride, boff, bvalid, acc);
+        finish_unit(u + 1);
+      }
+    }
   }
-  __syncthreads();
+  const bool any_failed = __syncthreads_or(!ok);
 
   // ---- epilogue: warp w finishes tiles w, w + 8, ...
   for (int t = warp; t < my_tiles; t += kSlabWarps) {
@@ -282,11 +408,11 @@ __global__ void __launch_bounds__(kSlabThreads, 2) gemv_slab_kernel(const __grid
       if (lane == 0) a.counters[tile] = 0u;
     }
   }
-  // No copy may still be writing this CTA's shared memory when it exits: on the normal path
-  // every stage has completed (each was waited for above, so these polls return at once);
-  // after a failed wait this drains, bounded, what is left.
-  if (threadIdx.x == 0)
-    for (int t = 0; t < my_tiles; ++t) mbar_wait_bounded(&bars[t], 0);
+  // No copy may still be writing this CTA's shared memory when it exits.  On the normal path
+  // every stage was waited for (by the warps that read it, before the barrier above); after a
+  // failed wait this drains, bounded, what is left.
+  if (any_failed && threadIdx.x == 0)
+    for (int t = 0; t < my_tiles; ++t) mbar_spin_bounded(&bars[t], 0);
 }
 
 size_t slab_smem_bytes(int M, int nt, int ks, int tiles_max, int slots, int pitch) {

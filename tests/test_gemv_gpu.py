@@ -21,7 +21,7 @@ LLAMA_SHAPES = [  # (name, N = out_features, K = in_features)
     ("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
     ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192), ("lm_head", 128256, 2048),
 ]
-KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5, "slab": 6}
+KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5, "slab": 6, "rows": 7}
 
 
 def sm_count() -> int:
@@ -65,6 +65,8 @@ def supported(kernel: str, M: int, group: int = 128, K: int = 2048, N: int = 300
     """Which forced kernel families take the problem."""
     if kernel == "slab":
         return slab_fits(M, N, K, group)
+    if kernel == "rows":
+        return M == 1 and group == 128 and K in (1024, 2048)
     if kernel == "cuda_core":
         return M <= 8
     if kernel == "stream":
@@ -295,6 +297,37 @@ def test_slab_launch_shapes(M, split, max_ctas, N, K, g, cuda_device):
     assert native.device_errors() == 0
 
 
+@pytest.mark.parametrize("N,K", [(1, 2048), (17, 1024), (512, 2048), (2048, 2048), (3000, 1024), (4100, 2048)])
+def test_rows_launch_shapes(N, K, g, cuda_device):
+    """Register-rows kernel (M = 1): one partial tile, every row count modulo 16, K = 1024 / 2048;
+    deterministic."""
+    int4_gemv, _ = g
+    x, p, s, z, host = make_problem(N, K, 1, seed=N + K)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(1, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["rows"])
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["rows"])
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+def test_rows_rejects_misaligned_x(g, cuda_device):
+    """A forced register-rows launch refuses an x that is not 16-byte aligned; the dispatcher re-plans it."""
+    int4_gemv, native = g
+    N, K = 512, 2048
+    x, p, s, z, host = make_problem(N, K, 1, seed=5)
+    buf = torch.zeros(K + 8, dtype=torch.float16, device=cuda_device)
+    buf[1:K + 1] = x[0]
+    xm = buf[1:K + 1].view(1, K)  # 2 bytes past a 16-byte boundary
+    y = torch.empty(1, N, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(native.Li4Error, match="register-rows"):
+        int4_gemv.int4_linear_out(xm, p, s, z, y, 128, kernel=KERNELS["rows"])
+    int4_gemv.int4_linear_out(xm, p, s, z, y, 128)
+    y_ref, y32 = oracle.linear(*host)
+    check_close(y, y_ref, y32, host)
+
+
 def test_slab_rejects_what_does_not_fit(g, cuda_device):
     """A forced slab launch beyond its resident tiles (lm_head at M=1) fails with a clear error, no launch."""
     int4_gemv, native = g
@@ -308,13 +341,21 @@ def test_slab_rejects_what_does_not_fit(g, cuda_device):
         int4_gemv.int4_linear_out(x, p, s, s, y, 128, kernel=KERNELS["slab"])
 
 
-def test_auto_dispatch_matches_slab_rule(g, cuda_device):
-    """The dispatcher takes the slab kernel exactly where it fits (every Llama-3.2-1B layer shape at M <= 16)
-    and the tile / bulk kernels for lm_head: workspace needs follow the plan."""
+def test_slab_fits_every_layer_shape(g, cuda_device):
+    """The slab kernel takes every Llama-3.2-1B layer shape at M <= 16 (not lm_head)."""
     for name, N, K in LLAMA_SHAPES:
         for M in (1, 2, 4, 8, 16):
-            fits = slab_fits(M, N, K)
-            assert fits == (name != "lm_head"), (name, M)
+            assert slab_fits(M, N, K) == (name != "lm_head"), (name, M)
+
+
+def test_auto_dispatch_rows_at_m1(g, cuda_device):
+    """At M = 1 the dispatcher runs q / k / v / o_proj (K = 2048, at most two tiles per SM) on the
+    register-rows kernel, and not lm_head or gate / up / down."""
+    from llama import _native
+
+    for name, N, K in LLAMA_SHAPES:
+        k = _native.plan(1, N, K)["kernel"]
+        assert (k == "rows") == (name in ("q_proj", "k_proj", "v_proj", "o_proj")), (name, k)
 
 
 def test_split_counters_reset_across_launches(g, cuda_device):
