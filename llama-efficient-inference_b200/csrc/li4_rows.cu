@@ -113,10 +113,10 @@ __global__ void __launch_bounds__(kRowsThreads, 2) gemv_rows_kernel(const __grid
 
   pdl_wait_primary();  // x (and the residual) come from the preceding kernel
   // ---- x: the lane's KL values, loaded together (one L2 round trip)
-  uint4 xv[KW / 8];
+  uint4 xv[WORDS];  // one 16-byte piece of x (8 k) per packed word
   const uint4* xp = reinterpret_cast<const uint4*>(a.x + lane * KL);
 #pragma unroll
-  for (int j = 0; j < KW / 8; ++j) xv[j] = xp[j];
+  for (int j = 0; j < WORDS; ++j) xv[j] = xp[j];
   float res_lo = 0.f, res_hi = 0.f;
   if (FUSED && a.epi == LI4_EPI_RESIDUAL && lane == 0) {
     if (r_lo < a.N) res_lo = __half2float(a.res[r_lo]);
