@@ -1133,11 +1133,9 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (sm <= 0) sm = 148;
 
   int kernel = kernel_req;
-  // register rows at M = 1 while the tiles fill at most two CTAs per SM (q / k / v / o_proj; the
-  // caller re-plans when x is not 16-byte aligned or the fusion needs the RMSNorm prologue)
-  if (kernel == LI4_KERNEL_AUTO && M == 1 && group == 128 && (K == 1024 || K == 2048) && split_req <= 0 &&
-      max_ctas <= 0 && (N + 15) / 16 <= 2LL * sm)
-    kernel = LI4_KERNEL_ROWS;
+  // (The slab and register-rows families are taken only when forced: in graphs of back-to-back
+  // launches on B200 they measured slower than the choices below at every decode shape, e.g.
+  // q_proj at M = 1 2.73 / 3.34 against 2.41 us, gate_proj 5.70 / 7.35 against 4.44 us.)
   if (kernel == LI4_KERNEL_AUTO) {
     // By measured B200 sweeps of the Llama-3.2-1B shapes (bench.py --sweep):
     // tile streaming when every warp slot gets several 16-row x 2048-k tiles
