@@ -70,6 +70,16 @@ def gemv_bytes(N: int, K: int, M: int) -> int:
     return K * N // 2 + 4 * (K // GROUP) * N + 2 * M * K + 2 * M * N
 
 
+def workload_config(M: int, world: int) -> dict:
+    """The `config` of both arms' JSON lines (the same workload, the same keys)."""
+    shapes = stream_shapes()
+    return {"workload": "llama3.2-1b int4 g128 decode linears, 16 layers x 7 + lm_head, M=%d" % M,
+            "M": M, "gemvs_per_step": len(shapes), "bytes_per_step": sum(gemv_bytes(N, K, M) for _, N, K, _ in shapes),
+            "group_size": GROUP, "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
+            "l2": "no flush: 658 MB of distinct weights per step > 2x the 126 MB L2",
+            "timing": "one CUDA graph of the 113 int4_linear_out calls per step, CUDA events"}
+
+
 def measured_peak():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -283,47 +293,137 @@ def time_e2e(stream: Stream, steps: int, warmup: int, world: int, eager: bool = 
     return start.elapsed_time(end) / steps, hx.numel() * 2, hy.numel() * 2
 
 
-def per_shape_isolated(stream: Stream, reps: int = 5):
-    """Each distinct shape alone: a CUDA graph of back-to-back launches over rotating weight copies
-    totalling > 3x L2 (so weights stream from HBM), device time per launch, median of `reps` replays."""
+def _graph_us(run, copies: int, dev, reps: int = 7) -> float:
+    """Device time per launch of a CUDA graph of `copies` back-to-back launches (run() issues them),
+    median of `reps` replays, CUDA events on the replay stream."""
+    run()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        times.append(a.elapsed_time(b) / copies)
+    del g
+    return statistics.median(times) * 1e3
+
+
+SWEEP_M = (1, 2, 4, 8, 16)
+REFERENCE_M = (1, 8, 16)
+PER_SHAPE = LAYER_SHAPES + [LM_HEAD]
+
+
+def load_reference_int4_gemv():
+    """The reference's own llama/int4_gemv.py (Triton), from the unmodified copy that
+    baseline/stage_reference.py puts in baseline/_ref, loaded by file path as the reference's
+    int4_linear_fn does.  Returns (module, None) or (None, why)."""
+    import importlib.util
+
+    path = os.path.join(REPO, "baseline", "_ref", "llama", "int4_gemv.py")
+    if not os.path.exists(path):
+        return None, "baseline/_ref/llama/int4_gemv.py is absent (run baseline/stage_reference.py)"
+    try:
+        spec = importlib.util.spec_from_file_location("reference_int4_gemv", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod, None
+    except Exception as e:  # noqa: BLE001 -- reported, never substituted
+        return None, f"import failed: {type(e).__name__}: {e}"[:200]
+
+
+def per_shape(stream: Stream, peak: float, reference=None):
+    """Configuration 2: every distinct shape of the step (7 layer shapes + lm_head) at M in {1, 2, 4, 8, 16},
+    each a CUDA graph of back-to-back int4_linear_out launches over rotating weight copies totalling
+    > 3x L2 (weights stream from HBM), device time per launch: us, GB/s of the algorithmic bytes,
+    fraction of the measured HBM peak, and the kernel the dispatcher ran.  With the reference's own
+    Triton int4_linear (`reference`), the same graphs through it at M in {1, 8, 16}."""
+    from llama import _native
     from llama.int4_gemv import int4_linear_out
 
     dev = stream.device
     out = {}
-    seen = set()
-    for i, (name, N, K, _) in enumerate(stream.shapes):
-        short = name.split(".")[-1]
-        if short in seen:
-            continue
-        seen.add(short)
-        x, (p, s, z), y = stream.xs[i], stream.weights[i], stream.ys[i]
-        wbytes = gemv_bytes(N, K, 0)
-        copies = max(2, 3 * L2_BYTES // wbytes + 1)
+    for name, N, K in PER_SHAPE:
+        idx = next(i for i, sh in enumerate(stream.shapes) if sh[0].split(".")[-1] == name)
+        p, s, z = stream.weights[idx]
+        copies = max(2, 3 * L2_BYTES // gemv_bytes(N, K, 0) + 1)
         ws = [(p, s, z)] + [(p.clone(), s.clone(), z.clone()) for _ in range(copies - 1)]
+        gen = torch.Generator(device=dev).manual_seed(N + K)
+        rec = {"N": N, "K": K, "launches_per_graph": copies}
+        for M in SWEEP_M:
+            x = torch.randn(M, K, generator=gen, device=dev).half()
+            y = torch.empty(M, N, dtype=torch.float16, device=dev)
 
-        def run():
-            for pi, si, zi in ws:
-                int4_linear_out(x, pi, si, zi, y, GROUP)
+            def run():
+                for pi, si, zi in ws:
+                    int4_linear_out(x, pi, si, zi, y, GROUP)
 
-        run()
-        torch.cuda.synchronize(dev)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            run()
-        g.replay()
-        times = []
-        for _ in range(reps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            g.replay()
-            b.record()
-            torch.cuda.synchronize(dev)
-            times.append(a.elapsed_time(b) / copies)
-        us = statistics.median(times) * 1e3
-        out[short] = {"N": N, "K": K, "us": round(us, 2), "launches_per_graph": copies,
-                      "GBps": round(gemv_bytes(N, K, stream.M) / (us * 1e-6) / 1e9, 1)}
-        del g, ws
+            us = _graph_us(run, copies, dev)
+            gbps = gemv_bytes(N, K, M) / (us * 1e-6) / 1e9
+            plan = _native.plan(M, N, K, GROUP)
+            rec[f"M{M}"] = {"us": round(us, 2), "GBps": round(gbps, 1), "frac": round(gbps / peak, 4),
+                            "kernel": plan["kernel"], "split": plan["split"]}
+            if reference is not None and M in REFERENCE_M:
+                def run_ref():
+                    for pi, si, zi in ws:
+                        reference.int4_linear(x, pi, si, zi, GROUP)
+
+                try:
+                    rus = _graph_us(run_ref, copies, dev)
+                    rg = gemv_bytes(N, K, M) / (rus * 1e-6) / 1e9
+                    rec[f"M{M}"]["reference_gpu"] = {"us": round(rus, 2), "GBps": round(rg, 1),
+                                                     "frac": round(rg / peak, 4)}
+                except Exception as e:  # noqa: BLE001 -- recorded beside the number it replaces
+                    rec[f"M{M}"]["reference_gpu"] = {"error": f"{type(e).__name__}: {e}"[:160]}
+        out[name] = rec
+        del ws
         torch.cuda.empty_cache()
+    return out
+
+
+def reference_step(stream: Stream, reference, steps: int = 50) -> dict:
+    """The 113-GEMV step through the reference's Triton int4_linear (one CUDA graph of the 113 calls in
+    model order, as the repo's step): ms per step and GB/s, on the same B200 and the same weights."""
+    dev = stream.device
+
+    def run():
+        for x, (p, s, z) in zip(stream.xs, stream.weights):
+            reference.int4_linear(x, p, s, z, GROUP)
+
+    us = _graph_us(run, 1, dev, reps=steps)
+    return {"ms_per_step": round(us / 1e3, 4), "GBps": round(stream.bytes_per_step / (us * 1e-6) / 1e9, 1),
+            "impl": "reference llama/int4_gemv.py int4_linear (Triton), unmodified"}
+
+
+def per_kernel_roofline(stream: Stream, peak: float) -> dict:
+    """The step split by kernel: a graph of the step's launches of one kernel family (the layer GEMVs on
+    the streaming-warp kernel, lm_head on the tile kernel), device time per launch, algorithmic bytes per
+    launch, GB/s and fraction of the measured HBM peak."""
+    from llama import _native
+    from llama.int4_gemv import int4_linear_out
+
+    dev = stream.device
+    groups = {}
+    for i, (name, N, K, _) in enumerate(stream.shapes):
+        groups.setdefault(_native.plan(stream.M, N, K, GROUP)["symbol"], []).append(i)
+    out = {}
+    for sym, idx in groups.items():
+        def run():
+            for i in idx:
+                p, s, z = stream.weights[i]
+                int4_linear_out(stream.xs[i], p, s, z, stream.ys[i], GROUP)
+
+        us = _graph_us(run, len(idx), dev, reps=20)
+        nbytes = sum(gemv_bytes(stream.shapes[i][1], stream.shapes[i][2], stream.M) for i in idx) / len(idx)
+        gbps = nbytes / (us * 1e-6) / 1e9
+        out[sym] = {"launches_per_step": len(idx), "bytes_per_launch": int(nbytes), "us_per_launch": round(us, 3),
+                    "GBps": round(gbps, 1), "frac": round(gbps / peak, 4)}
     return out
 
 
@@ -371,14 +471,25 @@ def profile_attention(a):
     print(json.dumps({"profile_attention": bs, "launches": a.launches, "kv_bytes": 2 * bs * 513 * KV * HD * 2}))
 
 
-def roofline_traffic():
-    """DRAM bytes per step of the GEMV kernels from the committed ncu summary, if present (M=1 only)."""
-    path = os.path.join(REPO, "profiles", "gemv_step_m1_traffic.json")
+def roofline_traffic(stream: "Stream"):
+    """DRAM bytes per step: the sum over the step's launches of the per-launch DRAM bytes that ncu measured
+    for the same kernel on the same shape (profiles/gemv_dram_per_launch.json, one small capture per shape);
+    None when the file does not cover a kernel / shape the dispatcher now picks."""
+    from llama import _native
+
+    path = os.path.join(REPO, "profiles", "gemv_dram_per_launch.json")
     try:
         with open(path) as f:
-            return json.load(f).get("dram_bytes_per_step")
-    except (OSError, ValueError):
+            table = json.load(f)["launches"]
+    except (OSError, ValueError, KeyError):
         return None
+    total = 0
+    for _, N, K, _ in stream.shapes:
+        key = f"{_native.plan(stream.M, N, K, GROUP)['symbol']}/M{stream.M}/N{N}/K{K}"
+        if key not in table:
+            return None
+        total += table[key]
+    return int(total)
 
 
 # ---------------------------------------------------------------------------
@@ -443,6 +554,109 @@ def cpu_rate(cs: CpuStream, seconds: float):
     return nbytes / dt / 1e9, rows, nbytes, dt
 
 
+def reference_cpu_child(a):
+    """Child process (`--reference-cpu-child`): the reference's own CPU path, imported from the unmodified
+    copy in baseline/_ref (its package is also named `llama`, hence a process of its own).
+      gemv    QuantizedLinear.forward with the default DEQUANT_IMPL "v1" (dequantize_packed + fp16
+              F.linear, llama/quantize.py:128-147) on CPU tensors over the 113-GEMV step in model order,
+              on all host threads and on one; GB/s of algorithmic bytes over a bounded sample.
+      decode  one Llama-3.2-1B INT4 decode step of the reference model (llama/model.py) at batch 1,
+              position 512, with its .cuda() cache allocation (llama/model.py:205-220) stubbed to stay on
+              the host; its 113 linears are the reference's QuantizedLinear with zero buffers (the cost
+              of the v1 path does not depend on the values)."""
+    ref = os.path.join(REPO, "baseline", "_ref")
+    sys.path[:] = [ref] + [q for q in sys.path if os.path.abspath(q) not in (PKG_DIR, REPO)]
+    out = {}
+    try:
+        from llama import quantize as Q  # the reference's own module
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"unavailable": f"reference import failed: {type(e).__name__}: {e}"[:200]}), flush=True)
+        return
+    rng = torch.Generator().manual_seed(0)
+    mods = {}
+    for name, N, K in PER_SHAPE:
+        m = Q.QuantizedLinear(K, N, GROUP)
+        m.packed_weight.copy_(torch.randint(0, 256, (N, K // 2), generator=rng, dtype=torch.uint8))
+        m.scale.copy_((torch.rand(N, K // GROUP, generator=rng) * 0.002 + 0.002).half())
+        m.zero_point.copy_(torch.randint(0, 16, (N, K // GROUP), generator=rng).half())
+        mods[name] = m
+    xs = {K: torch.randn(1, K, generator=rng).half() for _, _, K in PER_SHAPE}
+    order = [sh[0].split(".")[-1] for sh in stream_shapes()]
+    Q.set_dequant_impl("v1")
+    all_threads = cpu_threads()
+    gemv = {}
+    for threads in (all_threads, 1):
+        torch.set_num_threads(threads)
+        with torch.no_grad():
+            mods["q_proj"](xs[2048])  # warm-up
+            t0, nbytes, calls = time.perf_counter(), 0, 0
+            while time.perf_counter() - t0 < a.ref_cpu_seconds:
+                name = order[calls % len(order)]
+                m = mods[name]
+                m(xs[m.in_features])
+                nbytes += gemv_bytes(m.out_features, m.in_features, 1)
+                calls += 1
+            dt = time.perf_counter() - t0
+        gemv[f"threads_{threads}"] = {"GBps": round(nbytes / dt / 1e9, 3), "cores": threads,
+                                      "sample": f"{calls} GEMV calls ({calls / len(order):.2f} decode steps) in "
+                                                f"{dt:.1f} s"}
+    out["gemv"] = gemv
+    torch.set_num_threads(all_threads)
+    try:
+        from torch import nn
+
+        from llama.model import Llama, ModelArgs
+        saved = (torch.Tensor.cuda, nn.Linear.reset_parameters, nn.Embedding.reset_parameters)
+        torch.Tensor.cuda = lambda self, *args, **kw: self
+        nn.Linear.reset_parameters = lambda self: None  # allocation only: every nn.Linear is replaced below
+        nn.Embedding.reset_parameters = lambda self: None
+        try:
+            torch.set_default_dtype(torch.float16)
+            model = Llama(ModelArgs(max_batch_size=1, max_seq_len=640))
+        finally:
+            torch.set_default_dtype(torch.float32)
+            torch.Tensor.cuda, nn.Linear.reset_parameters, nn.Embedding.reset_parameters = saved
+        model.eval()
+        nn.init.zeros_(model.tok_embeddings.weight)
+        # the 113 nn.Linear -> the reference's QuantizedLinear, as its quantize_model does, with the packed
+        # buffers left at zero instead of quantizing 1.2 B weights on the host first
+        for name, mod in [(n, m) for n, m in model.named_modules() if isinstance(m, nn.Linear)]:
+            parent, child = name.rsplit(".", 1) if "." in name else ("", name)
+            setattr(model.get_submodule(parent) if parent else model, child,
+                    Q.QuantizedLinear(mod.in_features, mod.out_features, GROUP))
+        tok = torch.randint(0, 128256, (1, 1), generator=rng)
+        times = []
+        with torch.no_grad():
+            for i in range(a.ref_cpu_decode_steps + 1):
+                t0 = time.perf_counter()
+                model(tok, 512 + i)
+                times.append(time.perf_counter() - t0)
+        ms = statistics.median(times[1:]) * 1e3
+        out["decode"] = {"bs": 1, "position": 512, "steps_timed": a.ref_cpu_decode_steps, "ms_per_step": round(ms, 1),
+                         "tok_s": round(1e3 / ms, 3), "cores": all_threads,
+                         "note": "KV cache rows 0..511 left zero (no prefill); the step's cost does not depend "
+                                 "on their values"}
+    except Exception as e:  # noqa: BLE001
+        out["decode"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    print(json.dumps(out), flush=True)
+
+
+def reference_cpu(a) -> dict:
+    """Run reference_cpu_child in a child process; its JSON, or why it is unavailable."""
+    import subprocess
+
+    if not os.path.exists(os.path.join(REPO, "baseline", "_ref", "llama", "quantize.py")):
+        return {"unavailable": "baseline/_ref/llama is absent (run baseline/stage_reference.py)"}
+    cmd = [sys.executable, os.path.abspath(__file__), "--reference-cpu-child", "--ref-cpu-seconds",
+           str(a.ref_cpu_seconds), "--ref-cpu-decode-steps", str(a.ref_cpu_decode_steps)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+        return json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+
 def run_reference(a):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -478,8 +692,7 @@ def run_reference(a):
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (random INT4 weights, N(0,1) x)",
-        "config": {"workload": "llama3.2-1b int4 g128 decode linears, 16 layers x 7 + lm_head, M=%d" % a.m,
-                   "M": a.m, "gemvs_per_step": len(cs.items), "group_size": GROUP},
+        "config": workload_config(a.m, world),
         "cpu_baseline": {"value": round(gbps, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbps, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -523,6 +736,29 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
     fused: the step as llama.fused kernels (five launches per block), else the module-by-module step."""
     from llama.generation import DecodeGraph
 
+    gen_t = torch.Generator(device=device).manual_seed(1)
+    tokens = torch.randint(0, 128256, (bs, prompt_len), generator=gen_t, device=device)
+    check_steps = min(16, gen - 1)
+    ref = None
+    if world > 1:
+        # the same seeded model unsharded (TP = 1) on this rank: its greedy tokens and first-step logits
+        # are what the sharded step must reproduce
+        model = build_decode_model(device, bs, prompt_len + gen)
+        if fused:
+            model.enable_fused_decode(program=program)
+        g1 = DecodeGraph(model, bs)
+        with torch.no_grad():
+            g1.start(tokens)
+            toks, logits1 = [], None
+            for i in range(check_steps):
+                g1.replay()
+                if i == 0:
+                    logits1 = g1.logits.float().clone()
+                toks.append(g1.tok.clone())
+        torch.cuda.synchronize(device)
+        ref = (torch.cat(toks, 1), logits1)
+        del g1, model
+        torch.cuda.empty_cache()
     model = build_decode_model(device, bs, prompt_len + gen)
     if world > 1:
         from llama.tp import shard_model
@@ -532,9 +768,27 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
         model.enable_fused_decode(program=program)
     torch.cuda.synchronize(device)
     graph = DecodeGraph(model, bs)
-    gen_t = torch.Generator(device=device).manual_seed(1)
-    tokens = torch.randint(0, model.params.vocab_size, (bs, prompt_len), generator=gen_t, device=device)
     steps, prefills, e2es = [], [], []
+    parity = None
+    if ref is not None:
+        with torch.no_grad():
+            graph.start(tokens)
+            toks, logits1 = [], None
+            for i in range(check_steps):
+                graph.replay()
+                if i == 0:
+                    logits1 = graph.logits.float().clone()
+                toks.append(graph.tok.clone())
+        torch.cuda.synchronize(device)
+        tp_toks = torch.cat(toks, 1)
+        agree = float((tp_toks == ref[0]).float().mean())
+        rel = float((logits1 - ref[1]).abs().max() / ref[1].abs().max())
+        import torch.distributed as dist
+
+        t = torch.tensor([agree, -rel], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)  # the worst rank
+        parity = {"tokens_match_tp1": bool(t[0].item() == 1.0), "tp1_token_agreement": round(float(t[0].item()), 4),
+                  "tp1_first_step_logits_rel_err": float(-t[1].item()), "steps_checked": check_steps}
     for rep in range(reps + 1):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(gen + 1)]
         barrier(world, device)
@@ -558,12 +812,15 @@ def run_decode(device, bs: int, prompt_len: int, gen: int, reps: int, world: int
     path = getattr(getattr(model, "_fused", None), "last_path", None)
     del graph, model
     torch.cuda.empty_cache()
-    return {"bs": bs, "prompt": prompt_len, "generated": gen, "tp": world, "reps": reps,
+    row = {"bs": bs, "prompt": prompt_len, "generated": gen, "tp": world, "reps": reps,
             "step": ("one-launch program (llama.program)" if path == "program" else "fused launches (llama.fused)")
             if fused else "unfused (module by module)",
             "decode_ms_per_step": round(step_ms, 4), "decode_p10_ms": round(q[0], 4), "decode_p90_ms": round(q[-1], 4),
             "decode_tok_s": round(bs / (step_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 3),
             "e2e_tok_s": round(bs * gen / (e2e_ms * 1e-3), 1)}
+    if parity is not None:
+        row.update(parity)
+    return row
 
 
 def log(msg: str) -> None:
@@ -612,8 +869,24 @@ def run_gpu(a):
                                      program=a.decode_program))
             if a.decode_unfused:
                 decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
-    log("per-shape isolated timing")
-    per_shape = per_shape_isolated(stream) if (rank == 0 and not a.no_per_shape) else None
+    peak, peak_kind = measured_peak()
+    kernels, shapes_cfg2, ref_step, ref_why = None, None, None, None
+    if rank == 0:
+        log("per-kernel timing of the step")
+        kernels = per_kernel_roofline(stream, peak)
+        reference = None
+        if not a.no_reference_gpu:
+            reference, ref_why = load_reference_int4_gemv()
+        if not a.no_per_shape:
+            log("configuration 2: every shape at M in 1, 2, 4, 8, 16" + (" (and the reference's Triton kernel)"
+                                                                          if reference else ""))
+            shapes_cfg2 = per_shape(stream, peak, reference)
+        if reference is not None:
+            log("the 113-GEMV step through the reference's Triton int4_linear")
+            try:
+                ref_step = reference_step(stream, reference)
+            except Exception as e:  # noqa: BLE001 -- recorded, never substituted
+                ref_why = f"{type(e).__name__}: {e}"[:200]
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         from oracle import oracle
@@ -627,29 +900,32 @@ def run_gpu(a):
         cpu = {"value": round(gbps, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{rows} output rows ({rows / total_rows:.2f} decode steps) of the 113-GEMV stream "
                          f"in {dt:.1f} s"}
+        if not a.no_reference_cpu:
+            log("the reference's own CPU path (torch v1 GEMVs, one reference-model decode step)")
+            cpu["reference_torch"] = reference_cpu(a)
     if rank != 0:
         return
-    peak, peak_kind = measured_peak()
     bps = stream.bytes_per_step
     value = world * bps / (ms_max * 1e-3) / 1e9
     achieved = bps / (ms * 1e-3) / 1e9
-    traffic = roofline_traffic() if a.m == 1 else None
+    counts = {}
+    for _, N, K, _ in stream.shapes:
+        sym = __import__("llama._native", fromlist=["plan"]).plan(a.m, N, K, GROUP)["symbol"]
+        counts[sym] = counts.get(sym, 0) + 1
+    kernel_desc = " + ".join(f"{n} {k}" for k, n in sorted(counts.items(), key=lambda kv: -kv[1]))
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (W ~ N(0,0.02) quantized INT4 g128 by the CUDA quantizer, x ~ N(0,1) fp16)",
-        "config": {"workload": "llama3.2-1b int4 g128 decode linears, 16 layers x 7 + lm_head, M=%d" % a.m,
-                   "M": a.m, "gemvs_per_step": len(stream.shapes), "bytes_per_step": bps, "group_size": GROUP,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
-                   "l2": "no flush: 658 MB of distinct weights per step > 2x the 126 MB L2",
-                   "timing": "one CUDA graph of the 113 int4_linear_out calls per step, CUDA events"},
+        "config": workload_config(a.m, world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "frac": round(achieved / peak, 4), "traffic": roofline_traffic(stream),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
-                     "kernel": "li4 fused INT4 GEMV: the 113 launches of one step (112 gemv_stream_kernel + "
-                               "1 gemv_tile_kernel); achieved and traffic are per step"},
+                     "kernel": f"the step's {len(stream.shapes)} launches ({kernel_desc}, the dispatcher's plans); "
+                               "achieved and traffic are per step",
+                     "per_kernel": kernels},
         "e2e": {"value": round(world * bps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
                 "path": "pinned H2D x -> graph of 113 int4_linear_out calls -> D2H y"},
@@ -659,7 +935,8 @@ def run_gpu(a):
         "gpu_launches": len(stream.shapes) * a.steps,
         "clocks": sampler.summary(),
         "cpu_baseline": cpu,
-        "per_shape_isolated": per_shape,
+        "per_shape": shapes_cfg2,
+        "reference_gpu": ref_step if ref_step is not None else {"unavailable": ref_why or "not run"},
         "decode": decode,
         "gpu": torch.cuda.get_device_name(dev),
     }
@@ -676,6 +953,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-shape", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's Triton int4_linear (baseline/_ref) on the same GPU")
+    ap.add_argument("--no-reference-cpu", action="store_true",
+                    help="skip the reference's own torch CPU path (baseline/_ref) in cpu_baseline")
+    ap.add_argument("--ref-cpu-seconds", type=float, default=6.0,
+                    help="seconds per thread count of the reference's CPU GEMV sample")
+    ap.add_argument("--ref-cpu-decode-steps", type=int, default=1,
+                    help="timed CPU decode steps of the reference model")
+    ap.add_argument("--reference-cpu-child", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--no-decode", action="store_true", help="skip the full-model decode measurement")
     ap.add_argument("--decode-bs", type=int, nargs="+", default=None,
                     help="decode batch sizes (default: 1, 8 and 16 on one GPU, 16 under tensor parallelism)")
@@ -697,6 +983,9 @@ def main():
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
     a = ap.parse_args()
+    if a.reference_cpu_child:
+        reference_cpu_child(a)
+        return
     if a.profile_shape:
         profile_shape(a)
         return

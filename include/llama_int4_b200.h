@@ -272,6 +272,16 @@ int li4_gather_rows(const void* table, int64_t table_rows, int64_t cols, int64_t
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);
 
+/* Test hook for the bounded device waits: the poll limit of li4_allreduce_add's
+ * peer-flag waits (allreduce_polls), the poll limit of the decode program's
+ * op-counter waits (program_polls) -- 0 restores each default (about a second
+ * of polling) -- and, when program_wait_extra > 0, a target no program counter
+ * wait can meet.  With a short limit a test can make a wait run out without a
+ * fault: the kernel sets its bit in li4_device_errors and returns.  Applies to
+ * the current device; synchronous.  No counterpart in the reference (it has no
+ * device waits). */
+int li4_debug_set_wait_limits(unsigned allreduce_polls, unsigned program_polls, unsigned program_wait_extra);
+
 /* ---------------------------------------------------------------------------
  * Tensor-parallel all-reduce over NVLink peer memory (one GPU per process).
  * Every rank allocates one communication buffer (li4_comm_alloc), exports it

@@ -37,6 +37,12 @@ int comm_device_errors(unsigned* flags, bool reset) {
 constexpr int kArThreads = 256;
 constexpr int kArMaxRanks = 8;
 constexpr unsigned kArWaitLimit = 1u << 22;  // polls of a peer flag before giving up (about a second)
+__device__ unsigned g_ar_wait_limit = kArWaitLimit;  // li4_debug_set_wait_limits shortens it for tests
+
+int comm_set_wait_limit(unsigned polls) {
+  const unsigned v = polls ? polls : kArWaitLimit;
+  return check_cuda(cudaMemcpyToSymbol(g_ar_wait_limit, &v, sizeof(v)), "debug_set_wait_limits: all-reduce");
+}
 
 struct ArArgs {
   const __half* slots[kArMaxRanks];  // this call's slot on every rank (peer pointers)
@@ -73,9 +79,10 @@ __global__ void __launch_bounds__(kArThreads) allreduce_add_kernel(const __grid_
     const int t = threadIdx.x;
     st_release_sys(a.flags[t] + c * a.world + a.rank, epoch);
     const unsigned* mine = a.flags[a.rank] + c * a.world + t;
+    const unsigned limit = g_ar_wait_limit;
     unsigned i = 0;
     while ((int)(ld_acquire_sys(mine) - epoch) < 0) {
-      if (++i == kArWaitLimit) {
+      if (++i == limit) {
         atomicOr(&g_comm_device_error, 2u);
         break;
       }

@@ -21,6 +21,10 @@ int current_sm_count();
 int comm_device_errors(unsigned* flags, bool reset);
 // Device error words of the decode program kernel (li4_program.cu); reset clears them.
 int program_device_errors(unsigned* flags, bool reset);
+// Poll limit of the all-reduce flag waits (li4_comm.cu); 0 restores the default.
+int comm_set_wait_limit(unsigned polls);
+// Poll limit of the program's counter waits and an unmeetable-target offset (li4_program.cu).
+int program_set_wait_limits(unsigned polls, unsigned extra);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }

@@ -118,6 +118,17 @@ __device__ unsigned g_prog_device_error;  // bits 0, 2, 3 of li4_device_errors (
 // Set with the error bit by a wait that runs out; cleared by the last CTA to leave the launch.
 __device__ unsigned g_prog_failing;
 
+__device__ unsigned g_prog_wait_limit = kProgWaitLimit;  // li4_debug_set_wait_limits shortens it for tests
+__device__ unsigned g_prog_wait_extra = 0u;  // > 0 (tests only): no counter wait can be met
+
+int program_set_wait_limits(unsigned polls, unsigned extra) {
+  const unsigned v = polls ? polls : kProgWaitLimit;
+  int rc = check_cuda(cudaMemcpyToSymbol(g_prog_wait_limit, &v, sizeof(v)), "debug_set_wait_limits: program");
+  if (rc == LI4_OK)
+    rc = check_cuda(cudaMemcpyToSymbol(g_prog_wait_extra, &extra, sizeof(extra)), "debug_set_wait_limits: program");
+  return rc;
+}
+
 int program_device_errors(unsigned* flags, bool reset) {
   unsigned a = 0;
   int rc = check_cuda(cudaMemcpyFromSymbol(&a, g_prog_device_error, sizeof(unsigned)), "device_errors: program");
@@ -725,10 +736,11 @@ __global__ void __launch_bounds__(prog_threads(NT), 1) decode_program_kernel(con
           reinterpret_cast<uint4*>(&s_op)[t] = reinterpret_cast<const uint4*>(&gop)[t];
         if (threadIdx.x == 0 && gop.wait >= 0) {
           // every CTA has finished op `wait`: its writes are visible after this acquire and the barrier below
-          const unsigned target = (unsigned)G + (unsigned)pa.ops[gop.wait].finalize;
+          const unsigned target = (unsigned)G + (unsigned)pa.ops[gop.wait].finalize + g_prog_wait_extra;
+          const unsigned limit = g_prog_wait_limit;
           unsigned it = 0;
           while (ld_acquire_gpu(&pa.done[gop.wait]) < target) {
-            if (++it == kProgWaitLimit) {
+            if (++it == limit) {
               prog_fail(4u);
               break;
             }
