@@ -266,13 +266,14 @@ class _Null:
 
 def time_concurrent(stream: Stream, n_streams: int = 4, reps: int = 50) -> dict:
     """The same 113 independent GEMVs issued round-robin on `n_streams` streams, one CUDA graph with
-    parallel branches (int4_linear_out unchanged; each stream has its own split-K workspace): device time
-    per step, GB/s, fraction of the measured HBM peak."""
+    parallel branches (int4_linear_out, each stream with a split-K workspace of its own): device time per
+    step, GB/s, fraction of the measured HBM peak."""
     from llama.int4_gemv import int4_linear_out
 
     dev = stream.device
     main = torch.cuda.current_stream(dev)
     sides = [torch.cuda.Stream(dev) for _ in range(n_streams)]
+    wss = [torch.zeros(16 << 20, dtype=torch.uint8, device=dev) for _ in range(n_streams)]
     order = sorted(range(len(stream.shapes)), key=lambda i: -gemv_bytes(*stream.shapes[i][1:3], stream.M))
 
     def run():
@@ -281,7 +282,7 @@ def time_concurrent(stream: Stream, n_streams: int = 4, reps: int = 50) -> dict:
         for j, i in enumerate(order):  # largest first, dealt round-robin
             with torch.cuda.stream(sides[j % n_streams]):
                 p, s, z = stream.weights[i]
-                int4_linear_out(stream.xs[i], p, s, z, stream.ys[i], GROUP)
+                int4_linear_out(stream.xs[i], p, s, z, stream.ys[i], GROUP, workspace=wss[j % n_streams])
         for s_ in sides:
             main.wait_stream(s_)
 

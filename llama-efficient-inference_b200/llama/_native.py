@@ -180,21 +180,18 @@ def ptr(t: torch.Tensor) -> int:
 
 
 # ---------------------------------------------------------------------------
-# Split-K workspace: one zero-initialised buffer per (device, stream), grown
-# outside CUDA-graph capture.  Kernels leave its counters at zero, so launches
-# that follow each other on a stream (eager or replayed) share it; launches on
-# other streams, which may overlap on the GPU, get their own.
+# Split-K workspace: one zero-initialised buffer per device, grown outside
+# CUDA-graph capture.  Kernels leave its counters at zero, so launches that
+# follow each other on a stream (eager or replayed) can share it; launches that
+# may overlap on the GPU (different streams) must not.
 # ---------------------------------------------------------------------------
-_ws: dict[tuple, torch.Tensor] = {}
+_ws: dict[int, torch.Tensor] = {}
 _WS_MIN = 8 << 20
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """The split-K workspace of (device, current stream): launches on different streams may overlap on
-    the GPU, so each stream has its own."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
-    buf = _ws.get(key)
+    buf = _ws.get(idx)
     if buf is None or buf.numel() < nbytes:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError(f"int4_linear needs a {nbytes}-byte split-K workspace on cuda:{idx} but a CUDA graph "
@@ -202,5 +199,5 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
                                f"call llama.int4_gemv.reserve_workspace() first")
         size = max(nbytes, _WS_MIN, 2 * (buf.numel() if buf is not None else 0))
         buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
-        _ws[key] = buf
+        _ws[idx] = buf
     return buf

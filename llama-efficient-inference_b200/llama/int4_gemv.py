@@ -62,11 +62,14 @@ def _check_operands(x2: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor,
 
 def int4_linear_out(x2: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, zp: torch.Tensor,
                     y: torch.Tensor, group_size: int = 128, kernel: int = 0, rows_per_cta: int = 0,
-                    split: int = 0, max_ctas: int = 0) -> torch.Tensor:
+                    split: int = 0, max_ctas: int = 0, workspace: torch.Tensor = None) -> torch.Tensor:
     """y[M, N] = x2[M, K] @ W^T into a caller-owned fp16 y (row stride y.stride(0)).
 
     For CUDA-graph capture with static buffers.  kernel / rows_per_cta /
     split / max_ctas force a launch shape (0 = automatic), for tuning sweeps.
+    workspace: a caller-owned zero-initialised uint8 split-K workspace (for
+    launches that may overlap on the GPU, e.g. on several streams); default:
+    the device's shared one.
     """
     M, K = x2.shape
     N = packed.shape[0]
@@ -80,7 +83,12 @@ def int4_linear_out(x2: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor,
     lib = _native.lib()
     dev = x2.device
     nbytes = lib.li4_int4_linear_workspace_bytes(M, N, K, group_size, 0)
-    ws = _native.workspace(dev, nbytes) if nbytes else None
+    if workspace is not None:
+        if workspace.dtype != torch.uint8 or workspace.device != dev or workspace.numel() < nbytes:
+            raise RuntimeError(f"int4_linear_out: the workspace must be a uint8 tensor of >= {nbytes} bytes on {dev}")
+        ws = workspace
+    else:
+        ws = _native.workspace(dev, nbytes) if nbytes else None
     ws_ptr, ws_len = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     stream = _native.stream_ptr(dev)
     if kernel or rows_per_cta or split or max_ctas:
