@@ -271,12 +271,12 @@ def time_concurrent(stream: Stream, n_streams: int = 4, reps: int = 50) -> dict:
     from llama.int4_gemv import int4_linear_out
 
     dev = stream.device
-    main = torch.cuda.current_stream(dev)
     sides = [torch.cuda.Stream(dev) for _ in range(n_streams)]
     wss = [torch.zeros(16 << 20, dtype=torch.uint8, device=dev) for _ in range(n_streams)]
     order = sorted(range(len(stream.shapes)), key=lambda i: -gemv_bytes(*stream.shapes[i][1:3], stream.M))
 
     def run():
+        main = torch.cuda.current_stream(dev)  # the capturing stream inside graph capture: the branches fork from it
         for s_ in sides:
             s_.wait_stream(main)
         for j, i in enumerate(order):  # largest first, dealt round-robin
