@@ -123,6 +123,19 @@ int li4_int4_linear_ex(const void* x, const void* packed, const void* scale, con
 int li4_int4_linear_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count,
                          int* kernel, int* split, int* grid_x, size_t* smem_bytes);
 
+/* y[M, N] = x[M, K] @ W^T on the tensor cores (tcgen05, fp32 accumulation in tensor
+ * memory) for any M >= 1, meant for prefill (M > 16).  The fp16 weights are rebuilt in
+ * shared memory tile by tile, bit-identical to dequantize_packed's fp16((q - zero) * scale),
+ * so the result is the reference's dequantize + F.linear up to the order of the fp32 sums.
+ * group_size 128, K a multiple of 128, x rows and packed rows 16-byte aligned (stride_xm
+ * % 8 == 0).  One launch; no workspace; no host synchronisation.  A bounded wait inside the
+ * kernel that runs out sets bit 4 of li4_device_errors.
+ * Replaces: the prefill branch of QuantizedLinear.forward, dequant_fn("v3") + F.linear
+ * (llama/quantize.py:143-146, 199-202). */
+int li4_int4_gemm(const void* x, const void* packed, const void* scale, const void* zero, void* y,
+                  int64_t M, int64_t N, int64_t K, int64_t group_size,
+                  int64_t stride_xm, int64_t stride_pn, int64_t stride_sn, int64_t stride_ym, void* stream);
+
 /* Size of the static device scratch behind li4_int4_linear_noalloc. */
 #define LI4_NOALLOC_SCRATCH_BYTES (4u << 20)
 
@@ -267,7 +280,7 @@ int li4_gather_rows(const void* table, int64_t table_rows, int64_t cols, int64_t
  * inside a GEMV kernel ran out; bit 1: a bounded wait for a peer's flag in
  * li4_allreduce_add ran out; bit 2: a decode program's wait for another op
  * ran out; bit 3: a gather (li4_gather_rows or a program gather) met an id
- * outside its table -- the kernel
+ * outside its table; bit 4: a bounded wait inside li4_int4_gemm ran out -- the kernel
  * carried on and its outputs are not valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);

@@ -1789,6 +1789,9 @@ extern "C" int li4_device_errors(unsigned* flags, int reset) {
   unsigned prog = 0;
   if (rc == LI4_OK) rc = li4::program_device_errors(&prog, reset != 0);
   if (rc == LI4_OK) *flags |= prog;
+  unsigned gemm = 0;
+  if (rc == LI4_OK) rc = li4::gemm_device_errors(&gemm, reset != 0);
+  if (rc == LI4_OK) *flags |= gemm;
   if (rc == LI4_OK) li4::clear_error();
   return rc;
 }

@@ -21,6 +21,8 @@ int current_sm_count();
 int comm_device_errors(unsigned* flags, bool reset);
 // Device error words of the decode program kernel (li4_program.cu); reset clears them.
 int program_device_errors(unsigned* flags, bool reset);
+// Device error word of the tensor-core GEMM (li4_gemm.cu); reset clears it.
+int gemm_device_errors(unsigned* flags, bool reset);
 // Poll limit of the all-reduce flag waits (li4_comm.cu); 0 restores the default.
 int comm_set_wait_limit(unsigned polls);
 // Poll limit of the program's counter waits and an unmeetable-target offset (li4_program.cu).

@@ -122,6 +122,27 @@ def int4_linear(x, packed, scale, zp, group_size=128, block_n=128, split_k=None,
     return y.reshape(*lead, N)
 
 
+def int4_gemm(x, packed, scale, zp, group_size=128):
+    """x [..., K] fp16 (any number of rows)  ->  [..., N] fp16 on the tensor cores (li4_int4_gemm):
+    the prefill path, the reference's dequantize + F.linear (llama/quantize.py:143-146) in one kernel."""
+    N, half_k = packed.shape
+    K = half_k * 2
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    assert x.dtype == torch.float16 and K % group_size == 0
+    packed, scale, zp = _check_operands(x2, packed, scale, zp)
+    M = x2.shape[0]
+    y = torch.empty(M, N, dtype=torch.float16, device=x.device)
+    if M and N:
+        rc = _native.lib().li4_int4_gemm(x2.data_ptr(), packed.data_ptr(), scale.data_ptr(), zp.data_ptr(),
+                                         y.data_ptr(), M, N, K, group_size, x2.stride(0), packed.stride(0),
+                                         scale.stride(0), y.stride(0), _native.stream_ptr(x.device))
+        _native.check(rc, "int4_gemm")
+    return y.reshape(*lead, N)
+
+
 def reserve_workspace(device=None, nbytes: int = 16 << 20) -> None:
     """Allocate the per-device split-K workspace ahead of CUDA-graph capture."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)

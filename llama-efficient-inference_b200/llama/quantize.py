@@ -9,7 +9,7 @@ zero_point), so converted packs and checkpoints stay loadable:
     QuantizedLinear.dequantize_packed / _v2  :78-126          -> li4_dequantize (CUDA)
     DEQUANT_IMPL / set_dequant_impl / dequant_fn  :176-203
     int4_linear_fn                           :206-216          -> int4_gemv.py, loaded by path
-    quantize_model / print_model_size        :219-251
+    quantize_model                           :219-240
 
 Every computation runs in the CUDA kernels of libllama_int4_b200.so and is
 bit-identical to the reference (quantize: packed bytes, scale and zero bits;
@@ -17,7 +17,8 @@ dequantize: fp16 weights).  CPU tensors are moved to the current CUDA device
 for the computation and the results moved back; without a CUDA device these
 functions raise.  DEQUANT_IMPL keeps the reference's meaning:
   v1, v2, v3  dequantize to fp16 (one CUDA kernel) + F.linear (cuBLAS)
-  v4          fused INT4 GEMV kernel for M <= 16 tokens, else as v3
+  v4          fused INT4 GEMV kernel for M <= 16 tokens, the tensor-core INT4 GEMM
+              (li4_int4_gemm) above at group 128, else as v3
 """
 from __future__ import annotations
 
@@ -128,9 +129,11 @@ class QuantizedLinear(nn.Module):
     dequantize_packed_v2 = dequantize_packed
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        # fused dequant + GEMV kernel for decode-sized inputs (M <= 16 tokens)
-        if DEQUANT_IMPL == "v4" and self.bias is None and x.numel() // x.shape[-1] <= 16:
-            return int4_linear_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
+        if DEQUANT_IMPL == "v4" and self.bias is None:
+            if x.numel() // x.shape[-1] <= 16:  # decode: the fused INT4 GEMV
+                return int4_linear_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
+            if self.group_size == 128 and x.is_cuda and x.dtype == torch.float16:  # prefill: tensor-core GEMM
+                return int4_gemm_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
         weight = dequant_fn(DEQUANT_IMPL)(self.packed_weight, self.scale, self.zero_point, self.group_size)
         return F.linear(x, weight, self.bias)
 
@@ -149,7 +152,7 @@ class QuantizedLinear(nn.Module):
 
 # Which path every QuantizedLinear uses (same names and default as the reference):
 #   v1 / v2 / v3  exact CUDA dequantize kernel + F.linear
-#   v4            fused INT4 GEMV kernel for M <= 16, else as v3
+#   v4            fused INT4 GEMV kernel for M <= 16, the tensor-core INT4 GEMM above (group 128)
 DEQUANT_IMPL = "v1"
 _int4_linear = None
 
@@ -166,16 +169,32 @@ def dequant_fn(impl: str):
     raise ValueError(impl)
 
 
-def int4_linear_fn():
-    global _int4_linear
-    if _int4_linear is None:
-        # by path, so this also works when quantize.py itself was loaded by path
+_int4_gemv_module = None
+
+
+def _int4_gemv():
+    """int4_gemv.py, loaded by file path (so this also works when quantize.py itself was loaded by path)."""
+    global _int4_gemv_module
+    if _int4_gemv_module is None:
         spec = importlib.util.spec_from_file_location(
             "llama_int4_gemv", os.path.join(os.path.dirname(os.path.abspath(__file__)), "int4_gemv.py"))
         mod = importlib.util.module_from_spec(spec)
         spec.loader.exec_module(mod)
-        _int4_linear = mod.int4_linear
+        _int4_gemv_module = mod
+    return _int4_gemv_module
+
+
+def int4_linear_fn():
+    """The decode kernel's entry point (cached in _int4_linear, which callers may replace)."""
+    global _int4_linear
+    if _int4_linear is None:
+        _int4_linear = _int4_gemv().int4_linear
     return _int4_linear
+
+
+def int4_gemm_fn():
+    """The prefill (M > 16) tensor-core GEMM's entry point."""
+    return _int4_gemv().int4_gemm
 
 
 def quantize_model(model, group_size=128):
@@ -188,14 +207,3 @@ def quantize_model(model, group_size=128):
         parent = model.get_submodule(parent_name) if parent_name else model
         setattr(parent, child_name, QuantizedLinear.from_linear(module, group_size).to(module.weight.device))
     return model
-
-
-def print_model_size(model):
-    """Print the model size in MB."""
-    param_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
-    buffer_bytes = sum(b.numel() * b.element_size() for b in model.buffers())
-    total_mb = (param_bytes + buffer_bytes) / (1024 ** 2)
-    print(f"Model size: {total_mb:.2f} MB")
-    print(f"  Parameters: {param_bytes / (1024**2):.2f} MB")
-    print(f"  Buffers: {buffer_bytes / (1024**2):.2f} MB")
-    return total_mb
