@@ -268,6 +268,16 @@ int li4_decode_attention(const void* q, int64_t stride_qb, const void* cache_k, 
 int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
                     int64_t* out, int64_t out_stride, void* stream);
 
+/* The row winners of li4_argmax_rows as keys for a vocabulary split over ranks:
+ * keys[r * keys_stride] = a signed 64-bit key of the winner of row r at global index
+ * index_offset + its column, ordered as torch.argmax orders candidates (larger value, NaN
+ * above all, then the smaller index).  The largest key over the ranks' shards (an int64 MAX
+ * all-reduce) is the winner over the whole row; its index is 0xFFFFFFFF - (key & 0xFFFFFFFF).
+ * Replaces: the all-gather of the vocabulary-sharded logits and the argmax over the
+ * gathered row at tensor-parallel decode (greedy step of llama/generation.py:59-60). */
+int li4_argmax_rows_keys(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
+                         int64_t index_offset, int64_t* keys, int64_t keys_stride, void* stream);
+
 /* out[r, :] = table[ids[r], :] for r < rows: fp16 rows of `cols` values (cols % 8 == 0,
  * 16-byte aligned rows; rows <= 65535).  An id outside [0, table_rows) is clamped and
  * sets bit 3 of li4_device_errors.  The ids may come from the preceding kernel on the

@@ -39,10 +39,30 @@ __device__ __forceinline__ void take(Best& best, float v, long long i) {
 // A cluster of kArgmaxCluster CTAs per row: CTA c scans columns [c*chunk, (c+1)*chunk) with
 // 16-byte loads unrolled so they are in flight together, and the cluster's first CTA picks
 // the winner among the CTAs' candidates through distributed shared memory.
+// The winner of a row as one signed 64-bit key whose order is torch.argmax's: the value's
+// order-preserving bits (NaN above every number, -0 as +0) above the complement of the global
+// index (the smaller index wins a tie), with the top bit flipped so that signed comparison (a
+// MAX reduction over int64) orders the keys as unsigned comparison would.
+__device__ __forceinline__ long long argmax_signed_key(float v, long long global_index) {
+  unsigned u = __float_as_uint(v), ord;
+  if (v != v) {
+    ord = 0xFFFFFFFFu;
+  } else {
+    if (v == 0.f) u = 0u;
+    ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  const unsigned long long key =
+      ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)global_index);
+  return (long long)(key ^ 0x8000000000000000ull);
+}
+
+// key_offset < 0: out[row] = the row's argmax index; otherwise out[row] = argmax_signed_key of the
+// row's winner at global index key_offset + index.
 template <bool F16>
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void* logits, long long cols,
                                                                      long long stride, long long* out,
-                                                                     long long out_stride, long long chunk) {
+                                                                     long long out_stride, long long chunk,
+                                                                     long long key_offset) {
   __shared__ Best s_best[kArgmaxThreads / 32];
   __shared__ Best s_cta;
   cg::cluster_group cluster = cg::this_cluster();
@@ -110,15 +130,15 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void*
       const Best other = *cluster.map_shared_rank(&s_cta, rk);
       if (better(other, win)) win = other;
     }
-    out[row * out_stride] = win.i;
+    out[row * out_stride] = key_offset < 0 ? win.i : argmax_signed_key(win.v, key_offset + win.i);
   }
   cluster.sync();  // every CTA's candidate stays in place until the first CTA has read it
 }
 
 }  // namespace li4
 
-extern "C" int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
-                               int64_t* out, int64_t out_stride, void* stream) {
+static int argmax_launch(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride, int64_t* out,
+                         int64_t out_stride, int64_t key_offset, void* stream) {
   using namespace li4;
   if (dtype != LI4_F16 && dtype != LI4_F32)
     return set_error(LI4_ERR_UNSUPPORTED, "argmax_rows: dtype %d (LI4_F16 or LI4_F32)", dtype);
@@ -146,13 +166,27 @@ extern "C" int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int6
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   long long* o = reinterpret_cast<long long*>(out);
+  const long long ko = (long long)key_offset;
   const int rc = dtype == LI4_F16
                      ? check_cuda(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<true>, logits, (long long)cols,
-                                                     (long long)stride, o, (long long)out_stride, chunk),
+                                                     (long long)stride, o, (long long)out_stride, chunk, ko),
                                   "argmax_rows: kernel launch")
                      : check_cuda(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<false>, logits, (long long)cols,
-                                                     (long long)stride, o, (long long)out_stride, chunk),
+                                                     (long long)stride, o, (long long)out_stride, chunk, ko),
                                   "argmax_rows: kernel launch");
   if (rc == LI4_OK) clear_error();
   return rc;
+}
+
+extern "C" int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
+                               int64_t* out, int64_t out_stride, void* stream) {
+  return argmax_launch(logits, dtype, rows, cols, stride, out, out_stride, -1, stream);
+}
+
+extern "C" int li4_argmax_rows_keys(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
+                                    int64_t index_offset, int64_t* keys, int64_t keys_stride, void* stream) {
+  if (index_offset < 0 || index_offset + cols > (int64_t(1) << 32) - 1)
+    return li4::set_error(LI4_ERR_INVALID_ARG, "argmax_rows_keys: index_offset=%lld cols=%lld (global indices "
+                          "below 2^32 - 1)", (long long)index_offset, (long long)cols);
+  return argmax_launch(logits, dtype, rows, cols, stride, keys, keys_stride, index_offset, stream);
 }

@@ -82,6 +82,7 @@ SIGNATURES = {
                                      ctypes.POINTER(Fusion), _P, _SZ, _P]),
     "li4_decode_attention": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "li4_argmax_rows": (_INT, [_P, _INT, _I64, _I64, _I64, _P, _I64, _P]),
+    "li4_argmax_rows_keys": (_INT, [_P, _INT, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "li4_device_errors": (_INT, [ctypes.POINTER(ctypes.c_uint), _INT]),
     "li4_debug_set_wait_limits": (_INT, [ctypes.c_uint, ctypes.c_uint, ctypes.c_uint]),
     "li4_comm_alloc": (_INT, [_SZ, ctypes.POINTER(_P)]),

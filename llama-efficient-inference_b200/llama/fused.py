@@ -130,6 +130,24 @@ def argmax_rows(logits: torch.Tensor, out: torch.Tensor) -> None:
     native.check(rc, "argmax_rows")
 
 
+def argmax_rows_keys(logits: torch.Tensor, index_offset: int, keys: torch.Tensor) -> None:
+    """keys[r] = the signed 64-bit key of the winner of logits[r] at global index index_offset + column
+    (li4_argmax_rows_keys): the largest key over every vocabulary shard is the row's argmax."""
+    codes = {torch.float16: native.LI4_F16, torch.float32: native.LI4_F32}
+    if logits.dtype not in codes or logits.stride(-1) != 1 or keys.dtype != torch.long:
+        raise RuntimeError("argmax_rows_keys: fp16 / fp32 logits with contiguous rows and an int64 output")
+    rows, cols = logits.shape
+    rc = native.lib().li4_argmax_rows_keys(logits.data_ptr(), codes[logits.dtype], rows, cols, logits.stride(0),
+                                           index_offset, keys.data_ptr(), keys.stride(0),
+                                           native.stream_ptr(logits.device))
+    native.check(rc, "argmax_rows_keys")
+
+
+def key_index(keys: torch.Tensor) -> torch.Tensor:
+    """The global index a key of argmax_rows_keys carries: 0xFFFFFFFF - (key & 0xFFFFFFFF)."""
+    return 0xFFFFFFFF - torch.bitwise_and(keys, 0xFFFFFFFF)
+
+
 class _Block:
     """Fused weights and fusion descriptors of one transformer block."""
 
@@ -374,11 +392,19 @@ class FusedDecoder:
                 f.argmax_out, f.argmax_stride, f.argmax_scratch = None, 0, None
         int4_linear_fused(h, *self.out, None, f, y_ptr=logits.data_ptr(), y_stride=logits.stride(0))
         if self.model.tp_group is not None:
+            # vocabulary-sharded logits: each rank's winner as an ordered key, one int64 MAX all-reduce,
+            # the winning global index -- instead of all-gathering bs x vocab fp32 logits
             import torch.distributed as dist
 
-            parts = [torch.empty_like(logits) for _ in range(self.model.tp_world)]
-            dist.all_gather(parts, logits, group=self.model.tp_group)
-            logits = torch.cat(parts, dim=-1)
+            if next_tokens is not None:
+                keys = self._bufs.get(("keys", bs))
+                if keys is None:
+                    keys = self._bufs[("keys", bs)] = torch.empty(bs, 1, dtype=torch.long, device=self.device)
+                shard = logits.shape[-1]
+                argmax_rows_keys(logits, dist.get_rank(self.model.tp_group) * shard, keys)
+                dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.model.tp_group)
+                next_tokens.view(bs, 1).copy_(key_index(keys))
+            return logits.view(bs, 1, -1)  # this rank's vocabulary shard
         if next_tokens is not None:
             argmax_rows(logits, next_tokens.view(bs, 1))
         return logits.view(bs, 1, -1)

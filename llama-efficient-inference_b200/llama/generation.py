@@ -1,5 +1,5 @@
-"""Generation loop with CUDA-graph decode (the reference's llama/generation.py:5-93 plus
-the graph capture its bench.py:103-151 does per position).
+"""Generation loop with CUDA-graph decode: the reference's interface (llama/generation.py:5-93)
+around one reusable decode graph (its bench.py:103-151 captures one graph per position).
 
 DecodeGraph captures ONE graph of the per-token step -- embedding, 16 blocks with the
 INT4 GEMV kernels, lm_head, greedy argmax, position increment -- and replays it for
@@ -87,66 +87,65 @@ def eager_tokens(model: nn.Module, tokens: torch.Tensor, n_steps: int) -> torch.
 
 
 class Generation(nn.Module):
+    """Text generation over the model's forward / decode step (the reference's interface,
+    llama/generation.py:5-82).
+
+    A batch of prompts is laid out in one token buffer, padded to the longest prompt plus
+    max_gen_len.  Decoding starts at the shortest prompt's length: each step produces the next
+    token of every sequence, but sequences still inside their prompt keep the prompt token
+    (teacher forcing), and a sequence stops contributing once it emits eos.  With the KV cache
+    each step feeds only the positions since the previous step; without it, the whole prefix.
+    cuda_graph=True (greedy only) runs the first step eagerly and every later one by replaying a
+    DecodeGraph, whose own greedy token is used directly."""
+
     def generate(self, tokenizer, prompts, max_gen_len, temperature, top_p, kv_caching, device, cuda_graph=False):
-        """The reference's generate (llama/generation.py:6-82).  cuda_graph=True replays the
-        decode steps from one captured graph (greedy: temperature must be 0)."""
-        prompt_tokens = [tokenizer.encode(x, bos=True, eos=False) for x in prompts]
-        bsz = len(prompt_tokens)
-        min_prompt_len = min(len(t) for t in prompt_tokens)
-        max_prompt_len = max(len(t) for t in prompt_tokens)
-        total_len = max_gen_len + max_prompt_len
-        tokens = torch.full((bsz, total_len), tokenizer.pad_id, dtype=torch.long, device=device)
-        for k, t in enumerate(prompt_tokens):
-            tokens[k, : len(t)] = torch.tensor(t, dtype=torch.long, device=device)
-        eos_reached = torch.tensor([False] * bsz, device=device)
-        input_text_mask = tokens != tokenizer.pad_id
-        graph = None
-        if cuda_graph:
-            if not kv_caching or temperature > 0:
-                raise ValueError("cuda_graph decode needs kv_caching=True and greedy sampling (temperature 0)")
-            graph = DecodeGraph(self, bsz)
-        prev_pos = 0
-        for cur_pos in range(min_prompt_len, total_len):
+        encoded = [tokenizer.encode(text, bos=True, eos=False) for text in prompts]
+        lengths = [len(t) for t in encoded]
+        first, total = min(lengths), max(lengths) + max_gen_len
+        buf = torch.full((len(encoded), total), tokenizer.pad_id, dtype=torch.long, device=device)
+        for row, toks in enumerate(encoded):
+            buf[row, :len(toks)] = torch.tensor(toks, dtype=torch.long, device=device)
+        in_prompt = buf != tokenizer.pad_id
+        finished = torch.zeros(len(encoded), dtype=torch.bool, device=device)
+        if cuda_graph and (not kv_caching or temperature > 0):
+            raise ValueError("cuda_graph decode needs kv_caching=True and greedy sampling (temperature 0)")
+        graph = DecodeGraph(self, len(encoded)) if cuda_graph else None
+        fed = 0  # positions already in the KV cache
+        for pos in range(first, total):
             with torch.no_grad():
-                if not kv_caching:
-                    # decoding without the cache: reprocess the whole prefix each step
-                    logits = self(tokens[:, :cur_pos], 0)
-                elif graph is not None and prev_pos > 0:
-                    graph.tok.copy_(tokens[:, prev_pos:cur_pos])
-                    graph.pos.fill_(prev_pos)
+                if graph is not None and fed > 0:  # one position since the last step: replay the graph
+                    graph.tok.copy_(buf[:, fed:pos])
+                    graph.pos.fill_(fed)
                     graph.replay()
-                    logits = graph.logits
+                    choice = graph.tok.view(-1).clone()
                 else:
-                    logits = self(tokens[:, prev_pos:cur_pos], prev_pos)
-            if temperature > 0:
-                probs = torch.softmax(logits[:, -1] / temperature, dim=-1)
-                next_token = sample_top_p(probs, top_p)
-            else:
-                next_token = torch.argmax(logits[:, -1], dim=-1)
-            next_token = next_token.reshape(-1)
-            next_token = torch.where(input_text_mask[:, cur_pos], tokens[:, cur_pos], next_token)
-            tokens[:, cur_pos] = next_token
-            eos_reached |= (~input_text_mask[:, cur_pos]) & (next_token == tokenizer.eos_id)
+                    logits = self(buf[:, fed:pos], fed) if kv_caching else self(buf[:, :pos], 0)
+                    last = logits[:, -1]
+                    if temperature > 0:
+                        choice = sample_top_p(torch.softmax(last / temperature, dim=-1), top_p).view(-1)
+                    else:
+                        choice = last.argmax(dim=-1)
+            choice = torch.where(in_prompt[:, pos], buf[:, pos], choice)
+            buf[:, pos] = choice
+            finished |= ~in_prompt[:, pos] & (choice == tokenizer.eos_id)
             if kv_caching:
-                prev_pos = cur_pos
-            if all(eos_reached):
+                fed = pos
+            if bool(finished.all()):
                 break
-        out_tokens = []
-        for i, toks in enumerate(tokens.tolist()):
-            start = len(prompt_tokens[i])
-            toks = toks[start: len(prompt_tokens[i]) + max_gen_len]
-            if tokenizer.eos_id in toks:
-                toks = toks[: toks.index(tokenizer.eos_id)]
-            out_tokens.append(toks)
-        return [{"generation": tokenizer.decode(t)} for t in out_tokens]
+        results = []
+        for row, n in enumerate(lengths):
+            gen = buf[row, n:n + max_gen_len].tolist()
+            if tokenizer.eos_id in gen:
+                gen = gen[:gen.index(tokenizer.eos_id)]
+            results.append({"generation": tokenizer.decode(gen)})
+        return results
 
 
 def sample_top_p(probs, p):
-    """Nucleus sampling (llama/generation.py:85-93)."""
-    probs_sort, probs_idx = torch.sort(probs, dim=-1, descending=True)
-    probs_sum = torch.cumsum(probs_sort, dim=-1)
-    mask = probs_sum - probs_sort > p
-    probs_sort[mask] = 0.0
-    probs_sort.div_(probs_sort.sum(dim=-1, keepdim=True))
-    next_token = torch.multinomial(probs_sort, num_samples=1)
-    return torch.gather(probs_idx, -1, next_token)
+    """Nucleus sampling (llama/generation.py:85-93): draw from the smallest set of most likely tokens
+    whose probability mass reaches p, renormalised; returns the drawn token ids [..., 1]."""
+    ranked, order = probs.sort(dim=-1, descending=True)
+    mass_above = ranked.cumsum(dim=-1) - ranked  # probability of the tokens ranked before each one
+    kept = ranked.masked_fill(mass_above > p, 0.0)
+    drawn = torch.multinomial(kept / kept.sum(dim=-1, keepdim=True), num_samples=1)
+    return order.gather(-1, drawn)

@@ -61,19 +61,18 @@ class ModelArgs:  # Llama 3.2-1B, llama/model.py:15-30
 
 
 class RMSNorm(torch.nn.Module):
-    """x * rsqrt(mean(x^2) + eps) in fp32, cast back, times weight (llama/model.py:32-75)."""
+    """Root-mean-square norm with the reference's fp16 / fp32 boundaries (llama/model.py:32-75): the
+    statistics and the scaling in fp32, the result cast back to the input dtype, then the weight."""
 
     def __init__(self, dim: int, eps: float = 1e-6):
         super().__init__()
         self.eps = eps
         self.weight = nn.Parameter(torch.ones(dim))
 
-    def _norm(self, x):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps)
-
     def forward(self, x):
-        output = self._norm(x.float()).type_as(x)
-        return output * self.weight
+        xf = x.float()
+        inv_rms = torch.rsqrt(xf.square().mean(-1, keepdim=True) + self.eps)
+        return (xf * inv_rms).type_as(x) * self.weight
 
 
 def apply_llama3_scaling(freqs: torch.Tensor, factor: float = 32.0, low_freq_factor: float = 1.0,
@@ -95,32 +94,42 @@ def apply_llama3_scaling(freqs: torch.Tensor, factor: float = 32.0, low_freq_fac
     return torch.tensor(out, dtype=freqs.dtype, device=freqs.device)
 
 
+def rope_frequencies(head_dim: int, theta: float, use_scaled: bool = False) -> torch.Tensor:
+    """Per-pair angular frequencies theta^(-2i / head_dim), i < head_dim / 2, in fp32 (computed as the
+    reciprocal of the power, the reference's rounding: llama/model.py:78-98)."""
+    exponents = torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim
+    freqs = 1.0 / (theta ** exponents)
+    return apply_llama3_scaling(freqs) if use_scaled else freqs
+
+
 def precompute_freqs_cis(dim: int, end: int, theta: float = 10000.0, use_scaled: bool = False):
-    """complex64 [end, dim/2] rotations (llama/model.py:78-98)."""
-    freqs = 1.0 / (theta ** (torch.arange(0, dim, 2)[: (dim // 2)].float() / dim))
-    if use_scaled:
-        freqs = apply_llama3_scaling(freqs)
-    t = torch.arange(end, device=freqs.device)
-    freqs = torch.outer(t, freqs).float()
-    return torch.polar(torch.ones_like(freqs), freqs)
+    """Unit complex rotations e^{i t f} (complex64 [end, dim/2]) for positions t < end."""
+    angles = torch.outer(torch.arange(end), rope_frequencies(dim, theta, use_scaled)).float()
+    return torch.polar(torch.ones_like(angles), angles)
 
 
-def reshape_for_broadcast(freqs_cis: torch.Tensor, x: torch.Tensor):
-    ndim = x.ndim
-    assert 0 <= 1 < ndim
-    assert freqs_cis.shape == (x.shape[1], x.shape[-1])
-    shape = [d if i == 1 or i == ndim - 1 else 1 for i, d in enumerate(x.shape)]
-    return freqs_cis.view(*shape)
+def _rotate(x: torch.Tensor, rot: torch.Tensor) -> torch.Tensor:
+    """x [b, s, heads, d] as d/2 complex (even, odd) pairs in fp32, times rot [s, d/2]."""
+    pairs = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+    rotated = pairs * rot[None, :, None, :]
+    return torch.view_as_real(rotated).flatten(3).type_as(x)
 
 
 def apply_rotary_emb(xq: torch.Tensor, xk: torch.Tensor, freqs_cis: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Rotate (even, odd) pairs as complex numbers in fp32 (llama/model.py:126-152)."""
-    xq_ = torch.view_as_complex(xq.float().reshape(*xq.shape[:-1], -1, 2))
-    xk_ = torch.view_as_complex(xk.float().reshape(*xk.shape[:-1], -1, 2))
-    freqs_cis = reshape_for_broadcast(freqs_cis, xq_)
-    xq_out = torch.view_as_real(xq_ * freqs_cis).flatten(3)
-    xk_out = torch.view_as_real(xk_ * freqs_cis).flatten(3)
-    return xq_out.type_as(xq), xk_out.type_as(xk)
+    """RoPE on queries and keys: pairs rotated as complex numbers in fp32, cast back
+    (llama/model.py:126-152)."""
+    if freqs_cis.shape != (xq.shape[1], xq.shape[-1] // 2):
+        raise ValueError(f"rotations {tuple(freqs_cis.shape)} do not match {tuple(xq.shape)}")
+    return _rotate(xq, freqs_cis), _rotate(xk, freqs_cis)
+
+
+def ffn_hidden_dim(dim: int, multiple_of: int, ffn_dim_multiplier: Optional[float]) -> int:
+    """SwiGLU width: 2/3 of 4*dim, times the multiplier, rounded up to multiple_of (8192 for
+    Llama-3.2-1B; llama/model.py:296-308)."""
+    hidden = int(2 * (4 * dim) / 3)
+    if ffn_dim_multiplier is not None:
+        hidden = int(ffn_dim_multiplier * hidden)
+    return -(-hidden // multiple_of) * multiple_of
 
 
 class Attention(nn.Module):
@@ -213,10 +222,7 @@ class Attention(nn.Module):
 class FeedForward(nn.Module):
     def __init__(self, dim: int, hidden_dim: int, multiple_of: int, ffn_dim_multiplier: Optional[float]):
         super().__init__()
-        hidden_dim = int(2 * hidden_dim / 3)
-        if ffn_dim_multiplier is not None:
-            hidden_dim = int(ffn_dim_multiplier * hidden_dim)
-        hidden_dim = multiple_of * ((hidden_dim + multiple_of - 1) // multiple_of)
+        hidden_dim = ffn_hidden_dim(hidden_dim // 4, multiple_of, ffn_dim_multiplier)
         self.w1 = nn.Linear(dim, hidden_dim, bias=False)
         self.w2 = nn.Linear(hidden_dim, dim, bias=False)
         self.w3 = nn.Linear(dim, hidden_dim, bias=False)

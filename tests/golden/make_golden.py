@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout exists (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference PATH_TO_REFERENCE_CHECKOUT
 
 It loads llama/quantize.py by file path (as the reference's own
 dequant_traffic.py:47-53 does, so no tokenizer or CUDA is needed), runs
@@ -95,7 +95,7 @@ def model_golden(ref_root, ref_quantize, arrays, meta):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout (the directory holding llama/)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))

@@ -106,7 +106,7 @@ def test_quantized_linear_prefill_routes_to_gemm(g, cuda_device):
     lin = torch.nn.Linear(2048, 1024, bias=False).to(cuda_device).half()
     with torch.no_grad():
         lin.weight.normal_(0, 0.02)
-    ql = QL.from_linear(lin, 128)
+    ql = QL.from_linear(lin, 128).to(cuda_device)
     x = torch.randn(2, 300, 2048, device=cuda_device).half()
     old = quantize.DEQUANT_IMPL
     try:

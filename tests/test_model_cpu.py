@@ -91,3 +91,46 @@ def test_llama3_rope_scaling_rule():
             assert s == pytest.approx(f / 32)
         else:
             assert f / 32 <= s <= f
+
+
+class _IdTokenizer:
+    """Token ids as text: encode('3 9 4') -> [bos, 3, 9, 4]; decode joins ids with spaces."""
+    bos_id, eos_id, pad_id = 1, 2, -1
+
+    def encode(self, text, bos, eos):
+        return ([self.bos_id] if bos else []) + [int(t) for t in text.split()] + ([self.eos_id] if eos else [])
+
+    def decode(self, ids):
+        return " ".join(str(i) for i in ids)
+
+
+def test_generate_greedy_matches_eager_loop(model):
+    """Generation.generate (greedy, with and without the KV cache, prompts of different lengths) gives the
+    tokens of the reference-style eager loop for each prompt on its own."""
+    from llama.generation import eager_tokens
+
+    tok = _IdTokenizer()
+    prompts = ["5 17 33 8", "40 41 42 43 44 45"]
+    steps = 4
+    for kv in (True, False):
+        for m in model.layers:
+            m.attention.cache_k = m.attention.cache_v = None
+        out = model.generate(tok, prompts, max_gen_len=steps, temperature=0.0, top_p=0.9, kv_caching=kv,
+                             device="cpu")
+        for p, o in zip(prompts, out):
+            model.reset_cache()
+            ids = torch.tensor([tok.encode(p, bos=True, eos=False)])
+            ref = eager_tokens(model, ids, steps - 1)[0].tolist()
+            if tok.eos_id in ref:
+                ref = ref[:ref.index(tok.eos_id)]
+            assert o["generation"] == tok.decode(ref), (kv, p, o, ref)
+
+
+def test_sample_top_p_keeps_the_nucleus():
+    """sample_top_p draws only tokens inside the smallest set whose mass reaches p."""
+    from llama.generation import sample_top_p
+
+    torch.manual_seed(0)
+    probs = torch.tensor([[0.05, 0.5, 0.1, 0.3, 0.05]]).repeat(2000, 1)
+    drawn = sample_top_p(probs, 0.75).view(-1)
+    assert set(drawn.tolist()) == {1, 3}  # 0.5 + 0.3 reaches 0.75; 0.1 starts above it
