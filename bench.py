@@ -431,6 +431,42 @@ def reference_step(stream: Stream, reference, steps: int = 50) -> dict:
             "impl": "reference llama/int4_gemv.py int4_linear (Triton), unmodified"}
 
 
+PREFILL_SHAPES = [("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("gate_proj", 8192, 2048), ("down_proj", 2048, 8192),
+                  ("lm_head", 128256, 2048)]
+
+
+def prefill_gemm(stream: Stream) -> dict:
+    """The tensor-core INT4 GEMM (li4_int4_gemm) on the prefill linears: M = 512 (a 512-token prompt at batch
+    1) and 8192 (batch 16), a CUDA graph of back-to-back launches per shape: us, TFLOP/s, fraction of the
+    measured dense bf16 peak, and beside it the path it replaces, the exact dequantize kernel + cuBLAS fp16
+    (F.linear), timed the same way."""
+    import torch.nn.functional as F
+
+    from llama.int4_gemv import int4_gemm
+    from llama.quantize import QuantizedLinear
+
+    dev = stream.device
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            tf_peak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        tf_peak = 1590.0
+    out = {"peak_tflops": tf_peak}
+    for M in (512, 8192):
+        for name, N, K in PREFILL_SHAPES:
+            if name == "lm_head" and M > 512:
+                continue
+            idx = next(i for i, sh in enumerate(stream.shapes) if sh[0].split(".")[-1] == name)
+            p, s, z = stream.weights[idx]
+            x = torch.randn(M, K, device=dev).half()
+            us = _graph_us(lambda: int4_gemm(x, p, s, z, GROUP), 1, dev, reps=10)
+            us_ref = _graph_us(lambda: F.linear(x, QuantizedLinear.dequantize_packed(p, s, z, GROUP)), 1, dev, reps=10)
+            tflops = 2 * M * N * K / (us * 1e-6) / 1e12
+            out[f"{name}/M{M}"] = {"us": round(us, 1), "TFLOPs": round(tflops, 1), "frac": round(tflops / tf_peak, 4),
+                                   "dequant_cublas_us": round(us_ref, 1)}
+    return out
+
+
 def per_kernel_roofline(stream: Stream, peak: float) -> dict:
     """The step split by kernel: a graph of the step's launches of one kernel family (the layer GEMVs on
     the streaming-warp kernel, lm_head on the tile kernel), device time per launch, algorithmic bytes per
@@ -477,6 +513,25 @@ def profile_shape(a):
     torch.cuda.synchronize(dev)
     print(json.dumps({"profile_shape": a.profile_shape, "N": N, "K": K, "M": a.m, "launches": a.launches,
                       "kernel": a.kernel, "bytes_per_launch": gemv_bytes(N, K, a.m)}))
+
+
+def profile_gemm(a):
+    """--profile-gemm M,N,K: `--launches` launches of the tensor-core INT4 GEMM on one weight set (a small
+    case for ncu captures of int4_gemm_kernel)."""
+    from llama.int4_gemv import int4_gemm
+    from llama.quantize import QuantizedLinear
+
+    M, N, K = (int(v) for v in a.profile_gemm.split(","))
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+    p, s, z = QuantizedLinear.quantize_tensor(w, GROUP)
+    del w
+    x = torch.randn(M, K, generator=gen, device=dev).half()
+    for _ in range(a.launches):
+        int4_gemm(x, p, s, z, GROUP)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_gemm": [M, N, K], "launches": a.launches, "flops_per_launch": 2 * M * N * K}))
 
 
 def profile_attention(a):
@@ -907,12 +962,14 @@ def run_gpu(a):
             if a.decode_unfused:
                 decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
     peak, peak_kind = measured_peak()
-    kernels, shapes_cfg2, ref_step, ref_why, concurrent = None, None, None, None, None
+    kernels, shapes_cfg2, ref_step, ref_why, concurrent, gemm = None, None, None, None, None, None
     if rank == 0:
         log("per-kernel timing of the step")
         kernels = per_kernel_roofline(stream, peak)
         log("the step's independent GEMVs on 4 streams")
         concurrent = time_concurrent(stream)
+        log("prefill GEMM (tensor cores) against dequantize + cuBLAS")
+        gemm = prefill_gemm(stream)
         reference = None
         if not a.no_reference_gpu:
             reference, ref_why = load_reference_int4_gemv()
@@ -972,6 +1029,7 @@ def run_gpu(a):
                       "ms_per_step": round(eager_ms, 5),
                       "path": "pinned H2D x -> 113 eager Python int4_linear_out calls -> D2H y"},
         "concurrent": concurrent,
+        "prefill_gemm": gemm,
         "gpu_launches": len(stream.shapes) * a.steps,
         "clocks": sampler.summary(),
         "cpu_baseline": cpu,
@@ -1017,6 +1075,8 @@ def main():
                     help="only run --launches launches of one shape (for ncu), no timing")
     ap.add_argument("--profile-attention", type=int, default=0, metavar="BS",
                     help="only run --launches decode-attention launches at batch BS (for ncu), no timing")
+    ap.add_argument("--profile-gemm", default=None, metavar="M,N,K",
+                    help="only run --launches tensor-core INT4 GEMM launches of one shape (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--kernel", default="auto", choices=["auto", "stream", "tile", "bulk", "slab"],
                     help="kernel family for --profile-shape (default: the dispatcher's choice)")
@@ -1031,6 +1091,9 @@ def main():
         return
     if a.profile_attention:
         profile_attention(a)
+        return
+    if a.profile_gemm:
+        profile_gemm(a)
         return
     if a.warmup < 3:
         a.warmup = 3

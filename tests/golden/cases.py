@@ -106,6 +106,9 @@ def make_quant_input(case) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 TINY_MODEL = dict(dim=256, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=1000, multiple_of=64,
                   ffn_dim_multiplier=1.5, norm_eps=1e-5, rope_theta=500000.0, max_batch_size=2, max_seq_len=24)
+# the same shape family with 8 KV heads and K shards of whole 128-groups at 2, 4 and 8 ranks
+TP_MODEL = dict(dim=1024, n_layers=2, n_heads=16, n_kv_heads=8, vocab_size=1024, multiple_of=1024,
+                ffn_dim_multiplier=1.5, norm_eps=1e-5, rope_theta=500000.0, max_batch_size=2, max_seq_len=24)
 TINY_PROMPT_LEN = 8
 TINY_DECODE_STEPS = 6
 TINY_SEED = 77

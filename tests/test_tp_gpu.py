@@ -1,8 +1,8 @@
-"""Tensor-parallel INT4 decode on 2 GPUs (NCCL): the sharded tiny model matches the
+"""Tensor-parallel INT4 decode on 2, 4 and 8 GPUs (NCCL): the sharded tiny model matches the
 unsharded one, and decode replayed from one CUDA graph (collectives inside the graph)
 gives the same greedy tokens as eager decoding, as does the fused step (llama.fused) on the
-shards.  Runs as child processes; skipped on
-machines with fewer than 2 GPUs."""
+shards (its vocabulary-sharded greedy step reduces per-rank argmax keys).  Runs as child
+processes; each case is skipped on machines with fewer GPUs than its ranks."""
 import json
 
 import pytest
@@ -13,10 +13,12 @@ from test_tp_cpu import launch
 pytestmark = pytest.mark.gpu
 
 
-def test_tp2_int4_model_matches_unsharded():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    outs = launch("gpu_parity", world=2, timeout_s=300, env_extra={"NCCL_NVLS_ENABLE": "0", "TP_TEST_TIMEOUT": "120"})
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_int4_model_matches_unsharded(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    outs = launch("gpu_parity", world=world, timeout_s=300,
+                  env_extra={"NCCL_NVLS_ENABLE": "0", "TP_TEST_TIMEOUT": "120"})
     for rc, out, err in outs:
         assert rc == 0, err[-3000:]
         rec = json.loads(out.strip().splitlines()[-1])
@@ -25,12 +27,14 @@ def test_tp2_int4_model_matches_unsharded():
         assert rec["fused_graph_tokens_equal"], rec
 
 
-def test_tp2_nvlink_allreduce_matches_nccl():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_nvlink_allreduce_matches_nccl(world):
     """li4_allreduce_add (one-shot over NVLink peer memory, GEMV partials written straight into the
     communication slots) against NCCL's all-reduce + residual, eager and replayed from a CUDA graph."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    outs = launch("gpu_allreduce", world=2, timeout_s=300, env_extra={"NCCL_NVLS_ENABLE": "0", "TP_TEST_TIMEOUT": "120"})
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    outs = launch("gpu_allreduce", world=world, timeout_s=300,
+                  env_extra={"NCCL_NVLS_ENABLE": "0", "TP_TEST_TIMEOUT": "120"})
     for rc, out, err in outs:
         assert rc == 0, err[-3000:]
         rec = json.loads(out.strip().splitlines()[-1])

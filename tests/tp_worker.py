@@ -62,8 +62,9 @@ def gpu_parity():
 
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", rank)
-    args = ModelArgs(**cases.TINY_MODEL)
-    sd = cases.tiny_state_dict(cases.TINY_MODEL)
+    cfg = cases.TINY_MODEL if world == 2 else cases.TP_MODEL  # 2 KV heads split 2 ways; 8 split up to 8
+    args = ModelArgs(**cfg)
+    sd = cases.tiny_state_dict(cfg)
 
     def build():
         torch.set_default_dtype(torch.float16)
@@ -79,7 +80,7 @@ def gpu_parity():
     quantize.set_dequant_impl("v4")
     full, part = build(), build()
     shard_model(part)
-    prompt = cases.tiny_prompt(cases.TINY_MODEL).to(dev)
+    prompt = cases.tiny_prompt(cfg).to(dev)
     steps = cases.TINY_DECODE_STEPS
     with torch.no_grad():
         a, b = full(prompt, 0), part(prompt, 0)
