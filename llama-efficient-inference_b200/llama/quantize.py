@@ -17,8 +17,8 @@ dequantize: fp16 weights).  CPU tensors are moved to the current CUDA device
 for the computation and the results moved back; without a CUDA device these
 functions raise.  DEQUANT_IMPL keeps the reference's meaning:
   v1, v2, v3  dequantize to fp16 (one CUDA kernel) + F.linear (cuBLAS)
-  v4          fused INT4 GEMV kernel for M <= 16 tokens, the tensor-core INT4 GEMM
-              (li4_int4_gemm) above at group 128, else as v3
+  v4          fused INT4 GEMV kernel for M <= 16 tokens; above, as v3, or with
+              set_prefill_gemm(True) the tensor-core INT4 GEMM (li4_int4_gemm, group 128)
 """
 from __future__ import annotations
 
@@ -132,7 +132,7 @@ class QuantizedLinear(nn.Module):
         if DEQUANT_IMPL == "v4" and self.bias is None:
             if x.numel() // x.shape[-1] <= 16:  # decode: the fused INT4 GEMV
                 return int4_linear_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
-            if self.group_size == 128 and x.is_cuda and x.dtype == torch.float16:  # prefill: tensor-core GEMM
+            if (PREFILL_GEMM and self.group_size == 128 and x.is_cuda and x.dtype == torch.float16):
                 return int4_gemm_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
         weight = dequant_fn(DEQUANT_IMPL)(self.packed_weight, self.scale, self.zero_point, self.group_size)
         return F.linear(x, weight, self.bias)
@@ -152,9 +152,18 @@ class QuantizedLinear(nn.Module):
 
 # Which path every QuantizedLinear uses (same names and default as the reference):
 #   v1 / v2 / v3  exact CUDA dequantize kernel + F.linear
-#   v4            fused INT4 GEMV kernel for M <= 16, the tensor-core INT4 GEMM above (group 128)
+#   v4            fused INT4 GEMV kernel for M <= 16; above, as v3 or (PREFILL_GEMM) the tensor-core INT4 GEMM
 DEQUANT_IMPL = "v1"
+# v4 prefill (M > 16) on the tensor-core INT4 GEMM (li4_int4_gemm) instead of dequantize + F.linear;
+# off by default while the GEMM measures slower than dequantize + cuBLAS (set_prefill_gemm).
+PREFILL_GEMM = False
 _int4_linear = None
+
+
+def set_prefill_gemm(enabled: bool) -> None:
+    """Route v4 prefill (M > 16, group 128, fp16 CUDA inputs) to the tensor-core INT4 GEMM."""
+    global PREFILL_GEMM
+    PREFILL_GEMM = bool(enabled)
 
 
 def set_dequant_impl(impl: str):

@@ -98,8 +98,8 @@ def test_gemm_strided_and_lm_head_tile(g, cuda_device):
 
 
 def test_quantized_linear_prefill_routes_to_gemm(g, cuda_device):
-    """QuantizedLinear.forward with the v4 implementation: M <= 16 on the GEMV, M > 16 on the tensor-core
-    GEMM; both agree with the reference's dequantize + F.linear (the v1 path) within the bound."""
+    """QuantizedLinear.forward with the v4 implementation and set_prefill_gemm(True): M > 16 on the
+    tensor-core GEMM, in agreement with the reference's dequantize + F.linear (the v1 path)."""
     _, _, QL = g
     from llama import quantize
 
@@ -108,13 +108,15 @@ def test_quantized_linear_prefill_routes_to_gemm(g, cuda_device):
         lin.weight.normal_(0, 0.02)
     ql = QL.from_linear(lin, 128).to(cuda_device)
     x = torch.randn(2, 300, 2048, device=cuda_device).half()
-    old = quantize.DEQUANT_IMPL
+    old, old_gemm = quantize.DEQUANT_IMPL, quantize.PREFILL_GEMM
     try:
         quantize.set_dequant_impl("v1")
         y1 = ql(x)
         quantize.set_dequant_impl("v4")
+        quantize.set_prefill_gemm(True)
         y4 = ql(x)
     finally:
         quantize.set_dequant_impl(old)
+        quantize.set_prefill_gemm(old_gemm)
     assert y4.shape == y1.shape
     assert float((y4.float() - y1.float()).abs().max()) <= 2e-3 * float(y1.float().abs().max())
