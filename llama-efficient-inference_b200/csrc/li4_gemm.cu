@@ -30,10 +30,9 @@
 
 namespace li4 {
 
-constexpr int kGemmThreads = 256;
 constexpr int kGemmBK = 64;       // k per step: one 128-byte swizzle row of fp16
 constexpr int kGemmStages = 4;    // shared-memory stages
-constexpr int kGemmAhead = 2;     // steps loaded ahead of the one being converted
+constexpr int kGemmAhead = 2;     // steps in flight ahead of the one being consumed (W registers, x copies)
 constexpr unsigned kGemmWaitLimit = 1u << 24;  // mbarrier polls before giving up
 
 __device__ unsigned g_gemm_device_error;  // bit 4 of li4_device_errors
@@ -126,18 +125,28 @@ __device__ __forceinline__ void dequant32(const uint4& w, __half z, __half s, ui
   }
 }
 
+// Warp roles of int4_gemm_kernel: 4 W warps (a feature row per thread), 2 x warps (cp.async),
+// 1 MMA warp (one thread issues the tensor-core work).
+constexpr int kGemmWWarps = 4, kGemmXWarps = 2;
+constexpr int kGemmMmaWarp = kGemmWWarps + kGemmXWarps;
+constexpr int kGemmWSThreads = (kGemmMmaWarp + 1) * 32;
+
 template <int BT>
-__global__ void __launch_bounds__(kGemmThreads, 1) int4_gemm_kernel(const __grid_constant__ GemmArgs a) {
+__global__ void __launch_bounds__(kGemmWSThreads, 1) int4_gemm_kernel(const __grid_constant__ GemmArgs a) {
   constexpr int A_BYTES = 128 * 128;                 // W tile: 128 features x 64 k fp16
   constexpr int B_BYTES = BT * 128;                  // x tile: BT tokens x 64 k fp16
   constexpr int STAGE = A_BYTES + B_BYTES;           // multiple of 1024 (BT % 8 == 0)
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;       // power of two >= 32
+  constexpr int S = kGemmStages;
+  constexpr int XA = kGemmAhead;                     // steps the x warps run ahead of their arrivals
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzle atoms are 1024 bytes: the stages start on a 1024-byte boundary
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + kGemmStages * STAGE);
-  uint64_t* drain = mma_done + kGemmStages;  // only after a wait ran out
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* full_w = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // W tile of the stage written (128 arrivals)
+  uint64_t* full_x = full_w + S;                                     // x tile landed (64 arrivals)
+  uint64_t* empty = full_x + S;                                      // the stage's MMAs have read it (commit)
+  uint64_t* done = empty + S;                                        // every MMA of the CTA has finished (commit)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * 128, m0 = blockIdx.y * BT;
@@ -149,132 +158,131 @@ __global__ void __launch_bounds__(kGemmThreads, 1) int4_gemm_kernel(const __grid
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (tid == 0) {
-    for (int s = 0; s < kGemmStages; ++s) mbar_init(&mma_done[s], 1);
-    mbar_init(drain, 1);
+  if (tid == 32) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_w[s], kGemmWWarps * 32);
+      mbar_init(&full_x[s], kGemmXWarps * 32);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_holder;
-
-  // this thread's W piece: feature row r, k half h (32 k) of each step
-  const int r = tid >> 1, h = tid & 1;
-  const int row = min(n0 + r, a.N - 1);  // rows past N repeat row N-1 (their outputs are not stored)
-  const uint8_t* wsrc = a.packed + (long long)row * a.spn + h * 16;
-  const unsigned short* ssrc = reinterpret_cast<const unsigned short*>(a.scale) + (long long)row * a.ssn;
-  const unsigned short* zsrc = reinterpret_cast<const unsigned short*>(a.zero) + (long long)row * a.ssn;
-
-  auto load_x = [&](int step) {  // cp.async of the x tile of `step` into its stage
-    uint8_t* bt = smem + (step % kGemmStages) * STAGE + A_BYTES;
-    const int k0 = step * kGemmBK;
-    for (int c = tid; c < BT * 8; c += kGemmThreads) {
-      const int t = c >> 3, ch = c & 7;
-      const int m = m0 + t;
-      const __half* src = a.x + (long long)min(m, a.M - 1) * a.sxm + k0 + ch * 8;
-      cp_async16(smem_addr(bt + t * 128 + ((ch ^ (t & 7)) << 4)), src, m < a.M ? 16 : 0);
-    }
-    cp_async_commit();
-  };
-  struct WPiece { uint4 w; unsigned short s, z; };
-  auto load_w = [&](int step, WPiece& p) {
-    p.w = ldg_stream_v4(wsrc + (long long)step * 32);
-    const int g = (step * kGemmBK) >> 7;  // one group of 128 covers two steps
-    p.s = __ldg(ssrc + g);
-    p.z = __ldg(zsrc + g);
-  };
-
-  static_assert(kGemmAhead == 2, "the W register ring below holds two steps ahead");
-  WPiece w0 = {}, w1 = {}, w2 = {};  // this step's W piece and the next two
-  for (int j = 0; j < kGemmAhead; ++j) {
-    if (j < nk) {
-      load_x(j);
-      load_w(j, j == 0 ? w0 : w1);
-    } else {
-      cp_async_commit();  // empty groups keep the wait count below uniform
-    }
-  }
   bool ok = true;
-  const uint32_t idesc = umma_idesc_f16(128, BT);
-  for (int step = 0; step < nk; ++step) {
-    const int s = step % kGemmStages;
-    // loads `kGemmAhead` steps ahead, into a stage whose previous MMAs have finished reading it
-    const int ahead = step + kGemmAhead;
-    if (ahead < nk) {
-      if (ahead >= kGemmStages && ok) ok = gemm_wait(&mma_done[ahead % kGemmStages], ((ahead / kGemmStages) - 1) & 1);
-      load_x(ahead);
-      load_w(ahead, w2);
-    } else {
-      cp_async_commit();  // an empty group keeps the wait count below uniform
+
+  if (warp < kGemmWWarps) {
+    // ---- W: thread r dequantizes feature row r (64 k = 32 packed bytes per step) into the A tile
+    const int r = tid;
+    const int row = min(n0 + r, a.N - 1);  // rows past N repeat row N-1 (their outputs are not stored)
+    const uint8_t* wsrc = a.packed + (long long)row * a.spn;
+    const unsigned short* ssrc = reinterpret_cast<const unsigned short*>(a.scale) + (long long)row * a.ssn;
+    const unsigned short* zsrc = reinterpret_cast<const unsigned short*>(a.zero) + (long long)row * a.ssn;
+    static_assert(XA == 2, "the W register ring below holds this step and the next two");
+    uint4 w0a = {}, w0b = {}, w1a = {}, w1b = {}, w2a = {}, w2b = {};  // packed bytes of steps t, t+1, t+2
+    if (nk > 0) {
+      w0a = ldg_stream_v4(wsrc);
+      w0b = ldg_stream_v4(wsrc + 16);
     }
-    // this step's W: unpack, scale, swizzled stores
-    {
-      uint4 q[4];
-      dequant32(w0.w, __ushort_as_half(w0.z), __ushort_as_half(w0.s), q);
+    if (nk > 1) {
+      w1a = ldg_stream_v4(wsrc + 32);
+      w1b = ldg_stream_v4(wsrc + 48);
+    }
+    for (int step = 0; step < nk; ++step) {
+      const int s = step % S;
+      if (step + XA < nk) {
+        w2a = ldg_stream_v4(wsrc + (long long)(step + XA) * 32);
+        w2b = ldg_stream_v4(wsrc + (long long)(step + XA) * 32 + 16);
+      }
+      const int g = (step * kGemmBK) >> 7;
+      const __half sc = __ushort_as_half(__ldg(ssrc + g)), ze = __ushort_as_half(__ldg(zsrc + g));
+      if (step >= S && ok) ok = gemm_wait(&empty[s], ((step / S) - 1) & 1);
+      uint4 q[8];
+      dequant32(w0a, ze, sc, q);
+      dequant32(w0b, ze, sc, q + 4);
+      w0a = w1a;
+      w0b = w1b;
+      w1a = w2a;
+      w1b = w2b;
       uint8_t* at = smem + s * STAGE + r * 128;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(at + (((h * 4 + j) ^ (r & 7)) << 4)) = q[j];
-      w0 = w1;
-      w1 = w2;
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) = q[c];
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> the tensor core
+      mbar_arrive(&full_w[s]);
     }
-    cp_async_wait<kGemmAhead>();  // this step's x has landed (this thread's copies)
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> the tensor core
-    __syncthreads();
-    if (tid == 0) {
+  } else if (warp < kGemmMmaWarp) {
+    // ---- x: the BT x 64 tile of each step by cp.async, XA steps in flight
+    const int xt = tid - kGemmWWarps * 32;  // 0 .. kGemmXWarps * 32 - 1
+    for (int step = 0; step < nk + XA; ++step) {
+      if (step < nk) {
+        const int s = step % S;
+        if (step >= S && ok) ok = gemm_wait(&empty[s], ((step / S) - 1) & 1);
+        uint8_t* bt = smem + s * STAGE + A_BYTES;
+        const int k0 = step * kGemmBK;
+        for (int c = xt; c < BT * 8; c += kGemmXWarps * 32) {
+          const int t = c >> 3, ch = c & 7;
+          const int m = m0 + t;
+          const __half* src = a.x + (long long)min(m, a.M - 1) * a.sxm + k0 + ch * 8;
+          cp_async16(smem_addr(bt + t * 128 + ((ch ^ (t & 7)) << 4)), src, m < a.M ? 16 : 0);
+        }
+      }
+      cp_async_commit();  // (empty groups past the end keep the wait count uniform)
+      const int landed = step - XA;  // the oldest step still in flight has landed after this wait
+      cp_async_wait<XA>();
+      if (landed >= 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&full_x[landed % S]);
+      }
+    }
+  } else if (lane == 0) {
+    // ---- MMA: one thread; a step's four MMAs read its stage, the commit frees it
+    const uint32_t idesc = umma_idesc_f16(128, BT);
+    for (int step = 0; step < nk && ok; ++step) {
+      const int s = step % S;
+      const unsigned ph = (step / S) & 1;
+      ok = gemm_wait(&full_w[s], ph) && gemm_wait(&full_x[s], ph);
+      if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t abase = smem_addr(smem + s * STAGE), bbase = abase + A_BYTES;
 #pragma unroll
       for (int kk = 0; kk < kGemmBK / 16; ++kk)  // K = 16 per MMA: 32 bytes further along the swizzled rows
         umma_f16(tmem, umma_desc_sw128(abase + kk * 32), umma_desc_sw128(bbase + kk * 32), idesc,
                  (step > 0 || kk > 0) ? 1u : 0u);
-      umma_commit(&mma_done[s]);
+      umma_commit(&empty[s]);
     }
+    umma_commit(done);  // completes once every MMA issued above has
   }
-  // every MMA has completed once the last step's commit has (commits track all earlier MMAs)
-  if (nk > 0 && ok) {
-    const int last = nk - 1;
-    ok = gemm_wait(&mma_done[last % kGemmStages], (last / kGemmStages) & 1);
-  }
-  const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;  // uniform: tcgen05.ld below is warp-collective
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-  // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (features), columns of its half of the tokens
-  if (all_ok && nk > 0) {
-    const int q = warp & 3, half = warp >> 2;
-    const int feat = n0 + q * 32 + lane;
-    constexpr int COLS = BT / 2;  // tokens per warp
-    constexpr int CHUNK = COLS < 16 ? COLS : 16;
-    for (int c0 = 0; c0 < COLS; c0 += CHUNK) {
+  // ---- epilogue (warps 0-3 = TMEM lane quarters): fp16 outputs, consecutive features per token
+  bool fin = ok;
+  if (warp < kGemmWWarps) fin = gemm_wait(done, 0) && ok;
+  const bool all_ok = __syncthreads_and(fin ? 1 : 0) != 0;  // uniform: tcgen05.ld is warp-collective
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (all_ok && nk > 0 && warp < kGemmWWarps) {
+    const int feat = n0 + warp * 32 + lane;
+    constexpr int CHUNK = BT < 16 ? BT : 16;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BT; c0 += CHUNK) {
       uint32_t v[CHUNK];
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * COLS + c0);
-      if constexpr (CHUNK == 16) {
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-            : "r"(taddr));
-      } else {
-        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                     : "r"(taddr));
-      }
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          : "r"(taddr));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       if (feat < a.N) {
 #pragma unroll
         for (int j = 0; j < CHUNK; ++j) {
-          const int m = m0 + half * COLS + c0 + j;
+          const int m = m0 + c0 + j;
           if (m < a.M) a.y[(long long)m * a.sym + feat] = __float2half_rn(__uint_as_float(v[j]));
         }
       }
     }
   }
-  if (!all_ok && tid == 0) {
-    // a wait ran out: wait (bounded) for whatever this CTA's MMAs (all issued by this thread) still
-    // do before their tensor memory is freed
-    umma_commit(drain);
-    gemm_wait(drain, 0);
-  }
+  if (!all_ok && warp == kGemmMmaWarp && lane == 0) gemm_wait(done, 0);  // MMAs finished before the memory goes
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
@@ -285,7 +293,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) int4_gemm_kernel(const __grid
 
 template <int BT>
 static size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kGemmStages * (128 * 128 + BT * 128) + (kGemmStages + 1) * 8 + 16;
+  return 1024 + (size_t)kGemmStages * (128 * 128 + BT * 128) + (3 * kGemmStages + 1) * 8 + 16;
 }
 
 template <int BT>
@@ -308,7 +316,7 @@ static int launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     }
   }
   dim3 grid((unsigned)((a.N + 127) / 128), (unsigned)((a.M + BT - 1) / BT), 1);
-  int4_gemm_kernel<BT><<<grid, kGemmThreads, smem, stream>>>(a);
+  int4_gemm_kernel<BT><<<grid, kGemmWSThreads, smem, stream>>>(a);
   return check_cuda(cudaGetLastError(), "int4_gemm: kernel launch");
 }
 
@@ -352,7 +360,8 @@ extern "C" int li4_int4_gemm(const void* x, const void* packed, const void* scal
   if (M <= 16) rc = launch_gemm<16>(a, s);
   else if (M <= 32) rc = launch_gemm<32>(a, s);
   else if (M <= 64) rc = launch_gemm<64>(a, s);
-  else rc = launch_gemm<128>(a, s);
+  else if (M <= 128) rc = launch_gemm<128>(a, s);
+  else rc = launch_gemm<256>(a, s);
   if (rc == LI4_OK) clear_error();
   return rc;
 }
