@@ -7,16 +7,18 @@
 //
 // One CTA computes a tile of 128 output features x BT tokens (BT = 128 for prefill, 16 / 32 / 64
 // for short batches), looping over K in steps of 64:
-//   * A operand = the W tile [128 features x 64 k] fp16, K-major, 128-byte swizzle.  Every thread
-//     loads 16 packed bytes (32 k of one feature row) two steps ahead into registers, and in its
-//     step unpacks them (the fp16 magic-number construction: exact q - zero), multiplies by the
-//     group scale in fp16 (the exact product rounded once: the reference's rounding), puts the k
-//     values back in order and stores four 16-byte chunks at their swizzled positions.
-//   * B operand = the x tile [BT tokens x 64 k] fp16, K-major, 128-byte swizzle, copied with
-//     cp.async two steps ahead (rows past M are zero-filled).
-//   * One thread issues the four tcgen05.mma (M = 128, N = BT, K = 16, fp32 accumulation in
-//     tensor memory) of a step and commits them to the stage's mbarrier; a stage is refilled only
-//     after that mbarrier says its MMAs have read it.
+//   * A operand = the W tile [128 features x 64 k] fp16, K-major, 128-byte swizzle, written by 8
+//     dequant warps: every thread loads 16 packed bytes (32 k of one feature row) four steps ahead
+//     into registers, and in its step unpacks them (the fp16 magic-number construction: exact
+//     q - zero), multiplies by the group scale in fp16 (the exact product rounded once: the
+//     reference's rounding), puts the k values back in order, stores four 16-byte chunks at their
+//     swizzled positions and arrives on the stage's "W full" mbarrier.
+//   * B operand = the x tile [BT tokens x 64 k] fp16, K-major, 128-byte swizzle, copied by 2 warps
+//     with cp.async three steps ahead (rows past M are zero-filled); "x full" mbarrier.
+//   * One thread of the MMA warp waits for both, issues the step's four tcgen05.mma (M = 128,
+//     N = BT, K = 16, fp32 accumulation in tensor memory) and commits them to the stage's "empty"
+//     mbarrier, which the producers wait for before refilling the stage.  No CTA-wide barrier
+//     inside the K loop.
 //   * Epilogue: tcgen05.ld of the accumulator (TMEM lane = feature, column = token), fp16
 //     rounding, stores of consecutive features per token.
 // Every mbarrier wait is bounded: one that runs out sets bit 4 of li4_device_errors, waits
@@ -32,7 +34,7 @@ namespace li4 {
 
 constexpr int kGemmBK = 64;       // k per step: one 128-byte swizzle row of fp16
 constexpr int kGemmStages = 4;    // shared-memory stages
-constexpr int kGemmAhead = 2;     // steps in flight ahead of the one being consumed (W registers, x copies)
+constexpr int kGemmAhead = 3;     // x tiles in flight ahead of the one being consumed
 constexpr unsigned kGemmWaitLimit = 1u << 24;  // mbarrier polls before giving up
 
 __device__ unsigned g_gemm_device_error;  // bit 4 of li4_device_errors
@@ -125,9 +127,10 @@ __device__ __forceinline__ void dequant32(const uint4& w, __half z, __half s, ui
   }
 }
 
-// Warp roles of int4_gemm_kernel: 4 W warps (a feature row per thread), 2 x warps (cp.async),
-// 1 MMA warp (one thread issues the tensor-core work).
-constexpr int kGemmWWarps = 4, kGemmXWarps = 2;
+// Warp roles of int4_gemm_kernel: 8 W warps (half a feature row's 64 k per thread), 2 x warps
+// (cp.async), 1 MMA warp (one thread issues the tensor-core work).
+constexpr int kGemmWWarps = 8, kGemmXWarps = 2;
+constexpr int kGemmWAhead = 4;  // steps of packed W in flight per thread (registers)
 constexpr int kGemmMmaWarp = kGemmWWarps + kGemmXWarps;
 constexpr int kGemmWSThreads = (kGemmMmaWarp + 1) * 32;
 
@@ -139,6 +142,7 @@ __global__ void __launch_bounds__(kGemmWSThreads, 1) int4_gemm_kernel(const __gr
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;       // power of two >= 32
   constexpr int S = kGemmStages;
   constexpr int XA = kGemmAhead;                     // steps the x warps run ahead of their arrivals
+  static_assert(XA < S, "the x warps may run at most S - 1 steps ahead of the MMAs");
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzle atoms are 1024 bytes: the stages start on a 1024-byte boundary
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -174,41 +178,33 @@ __global__ void __launch_bounds__(kGemmWSThreads, 1) int4_gemm_kernel(const __gr
   bool ok = true;
 
   if (warp < kGemmWWarps) {
-    // ---- W: thread r dequantizes feature row r (64 k = 32 packed bytes per step) into the A tile
-    const int r = tid;
+    // ---- W: threads 2r, 2r + 1 dequantize k halves 0 / 1 (32 k, 16 packed bytes) of feature row r
+    const int r = tid >> 1, h = tid & 1;
     const int row = min(n0 + r, a.N - 1);  // rows past N repeat row N-1 (their outputs are not stored)
-    const uint8_t* wsrc = a.packed + (long long)row * a.spn;
+    const uint8_t* wsrc = a.packed + (long long)row * a.spn + h * 16;
     const unsigned short* ssrc = reinterpret_cast<const unsigned short*>(a.scale) + (long long)row * a.ssn;
     const unsigned short* zsrc = reinterpret_cast<const unsigned short*>(a.zero) + (long long)row * a.ssn;
-    static_assert(XA == 2, "the W register ring below holds this step and the next two");
-    uint4 w0a = {}, w0b = {}, w1a = {}, w1b = {}, w2a = {}, w2b = {};  // packed bytes of steps t, t+1, t+2
-    if (nk > 0) {
-      w0a = ldg_stream_v4(wsrc);
-      w0b = ldg_stream_v4(wsrc + 16);
-    }
-    if (nk > 1) {
-      w1a = ldg_stream_v4(wsrc + 32);
-      w1b = ldg_stream_v4(wsrc + 48);
-    }
+    static_assert(kGemmWAhead == 4, "the W register ring below holds this step and the next four");
+    uint4 w0 = {}, w1 = {}, w2 = {}, w3 = {}, w4 = {};  // packed bytes of steps t .. t + 4
+    if (nk > 0) w0 = ldg_stream_v4(wsrc);
+    if (nk > 1) w1 = ldg_stream_v4(wsrc + 32);
+    if (nk > 2) w2 = ldg_stream_v4(wsrc + 64);
+    if (nk > 3) w3 = ldg_stream_v4(wsrc + 96);
     for (int step = 0; step < nk; ++step) {
       const int s = step % S;
-      if (step + XA < nk) {
-        w2a = ldg_stream_v4(wsrc + (long long)(step + XA) * 32);
-        w2b = ldg_stream_v4(wsrc + (long long)(step + XA) * 32 + 16);
-      }
+      if (step + kGemmWAhead < nk) w4 = ldg_stream_v4(wsrc + (long long)(step + kGemmWAhead) * 32);
       const int g = (step * kGemmBK) >> 7;
       const __half sc = __ushort_as_half(__ldg(ssrc + g)), ze = __ushort_as_half(__ldg(zsrc + g));
       if (step >= S && ok) ok = gemm_wait(&empty[s], ((step / S) - 1) & 1);
-      uint4 q[8];
-      dequant32(w0a, ze, sc, q);
-      dequant32(w0b, ze, sc, q + 4);
-      w0a = w1a;
-      w0b = w1b;
-      w1a = w2a;
-      w1b = w2b;
+      uint4 q[4];
+      dequant32(w0, ze, sc, q);
+      w0 = w1;
+      w1 = w2;
+      w2 = w3;
+      w3 = w4;
       uint8_t* at = smem + s * STAGE + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) = q[c];
+      for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(at + (((h * 4 + c) ^ (r & 7)) << 4)) = q[c];
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> the tensor core
       mbar_arrive(&full_w[s]);
     }
@@ -255,18 +251,22 @@ __global__ void __launch_bounds__(kGemmWSThreads, 1) int4_gemm_kernel(const __gr
     umma_commit(done);  // completes once every MMA issued above has
   }
 
-  // ---- epilogue (warps 0-3 = TMEM lane quarters): fp16 outputs, consecutive features per token
+  // ---- epilogue (warps 0-7: warp w reads TMEM lane quarter w % 4, the token half w / 4): fp16 outputs,
+  // consecutive features per token
   bool fin = ok;
   if (warp < kGemmWWarps) fin = gemm_wait(done, 0) && ok;
   const bool all_ok = __syncthreads_and(fin ? 1 : 0) != 0;  // uniform: tcgen05.ld is warp-collective
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (all_ok && nk > 0 && warp < kGemmWWarps) {
-    const int feat = n0 + warp * 32 + lane;
-    constexpr int CHUNK = BT < 16 ? BT : 16;
+    const int quarter = warp & 3;
+    const int feat = n0 + quarter * 32 + lane;
+    constexpr int CHUNK = 16;
+    constexpr int HALF = BT / 2;  // BT >= 32: two halves of whole 16-column chunks; BT = 16: warps 0-3 only
+    const int c_begin = BT >= 32 ? (warp >> 2) * HALF : 0, c_end = BT >= 32 ? c_begin + HALF : (warp < 4 ? BT : 0);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BT; c0 += CHUNK) {
+    for (int c0 = c_begin; c0 < c_end; c0 += CHUNK) {
       uint32_t v[CHUNK];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
       asm volatile(
           "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
           : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
@@ -360,7 +360,7 @@ extern "C" int li4_int4_gemm(const void* x, const void* packed, const void* scal
   if (M <= 16) rc = launch_gemm<16>(a, s);
   else if (M <= 32) rc = launch_gemm<32>(a, s);
   else if (M <= 64) rc = launch_gemm<64>(a, s);
-  else if (M <= 128) rc = launch_gemm<128>(a, s);
+  else if (M <= 2048) rc = launch_gemm<128>(a, s);  // more CTAs on the SMs
   else rc = launch_gemm<256>(a, s);
   if (rc == LI4_OK) clear_error();
   return rc;
