@@ -40,6 +40,7 @@ def _load_native():
 _native = _load_native()
 
 MAX_M = 16
+_ws_bytes: dict = {}  # (M, N, K, group_size, device) -> split-K workspace bytes
 
 
 def _check_operands(x2: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, zp: torch.Tensor):
@@ -82,7 +83,10 @@ def int4_linear_out(x2: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor,
         return y
     lib = _native.lib()
     dev = x2.device
-    nbytes = lib.li4_int4_linear_workspace_bytes(M, N, K, group_size, 0)
+    key = (M, N, K, group_size, dev.index)
+    nbytes = _ws_bytes.get(key)
+    if nbytes is None:  # the plan depends only on the shape and the device: ask the library once
+        nbytes = _ws_bytes[key] = lib.li4_int4_linear_workspace_bytes(M, N, K, group_size, 0)
     if workspace is not None:
         if workspace.dtype != torch.uint8 or workspace.device != dev or workspace.numel() < nbytes:
             raise RuntimeError(f"int4_linear_out: the workspace must be a uint8 tensor of >= {nbytes} bytes on {dev}")
@@ -141,6 +145,46 @@ def int4_gemm(x, packed, scale, zp, group_size=128):
                                          scale.stride(0), y.stride(0), _native.stream_ptr(x.device))
         _native.check(rc, "int4_gemm")
     return y.reshape(*lead, N)
+
+
+# ---------------------------------------------------------------------------
+# The kernel as a PyTorch operator (li4::int4_linear), with a shape-only fake kernel, so that
+# torch.compile / fake-tensor tracing pass through QuantizedLinear.forward without a graph break.
+# Eager callers keep the direct path above (no dispatcher overhead per call).
+# ---------------------------------------------------------------------------
+def _registered(name: str) -> bool:
+    try:
+        getattr(torch.ops.li4, name)
+        return True
+    except (AttributeError, RuntimeError):
+        return False
+
+
+# This file may be loaded twice (imported as llama.int4_gemv and by file path from quantize.py):
+# the operators are registered by whichever load comes first.
+if not _registered("int4_linear"):
+    @torch.library.custom_op("li4::int4_linear", mutates_args=())
+    def int4_linear_op(x: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, zp: torch.Tensor,
+                       group_size: int) -> torch.Tensor:
+        """int4_linear as an operator (decode sizes, prod(x.shape[:-1]) <= MAX_M)."""
+        return int4_linear(x, packed, scale, zp, group_size)
+
+    @int4_linear_op.register_fake
+    def _(x, packed, scale, zp, group_size):
+        torch._check(x.shape[-1] == packed.shape[1] * 2, lambda: "int4_linear: x's last dim must be 2 * packed.shape[1]")
+        return x.new_empty(*x.shape[:-1], packed.shape[0])
+
+if not _registered("int4_gemm"):
+    @torch.library.custom_op("li4::int4_gemm", mutates_args=())
+    def int4_gemm_op(x: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, zp: torch.Tensor,
+                     group_size: int) -> torch.Tensor:
+        """int4_gemm as an operator (any number of rows)."""
+        return int4_gemm(x, packed, scale, zp, group_size)
+
+    @int4_gemm_op.register_fake
+    def _(x, packed, scale, zp, group_size):
+        torch._check(x.shape[-1] == packed.shape[1] * 2, lambda: "int4_gemm: x's last dim must be 2 * packed.shape[1]")
+        return x.new_empty(*x.shape[:-1], packed.shape[0])
 
 
 def reserve_workspace(device=None, nbytes: int = 16 << 20) -> None:

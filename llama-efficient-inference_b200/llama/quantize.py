@@ -73,6 +73,7 @@ class QuantizedLinear(nn.Module):
             self.register_buffer("bias", torch.zeros(out_features, dtype=torch.float16))
         else:
             self.bias = None
+        _int4_gemv()  # registers the li4:: operators that traced forwards call
 
     @staticmethod
     def quantize_tensor(weight: torch.Tensor, group_size: int = 128):
@@ -130,10 +131,13 @@ class QuantizedLinear(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if DEQUANT_IMPL == "v4" and self.bias is None:
+            compiling = torch.compiler.is_compiling()  # traced: the registered operators (li4::...)
             if x.numel() // x.shape[-1] <= 16:  # decode: the fused INT4 GEMV
-                return int4_linear_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
+                fn = torch.ops.li4.int4_linear if compiling else int4_linear_fn()
+                return fn(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
             if (PREFILL_GEMM and self.group_size == 128 and x.is_cuda and x.dtype == torch.float16):
-                return int4_gemm_fn()(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
+                fn = torch.ops.li4.int4_gemm if compiling else int4_gemm_fn()
+                return fn(x, self.packed_weight, self.scale, self.zero_point, self.group_size)
         weight = dequant_fn(DEQUANT_IMPL)(self.packed_weight, self.scale, self.zero_point, self.group_size)
         return F.linear(x, weight, self.bias)
 

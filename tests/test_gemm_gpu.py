@@ -120,3 +120,26 @@ def test_quantized_linear_prefill_routes_to_gemm(g, cuda_device):
         quantize.set_prefill_gemm(old_gemm)
     assert y4.shape == y1.shape
     assert float((y4.float() - y1.float()).abs().max()) <= 2e-3 * float(y1.float().abs().max())
+
+
+def test_compiled_forward_runs_the_operators(g, cuda_device):
+    """torch.compile(fullgraph=True) of QuantizedLinear.forward traces through li4::int4_linear (decode) and
+    li4::int4_gemm (prefill) with no graph break, and gives the eager results."""
+    _, _, QL = g
+    from llama import quantize
+
+    lin = torch.nn.Linear(2048, 512, bias=False).to(cuda_device).half()
+    with torch.no_grad():
+        lin.weight.normal_(0, 0.02)
+    ql = QL.from_linear(lin, 128).to(cuda_device)
+    old, old_gemm = quantize.DEQUANT_IMPL, quantize.PREFILL_GEMM
+    try:
+        quantize.set_dequant_impl("v4")
+        quantize.set_prefill_gemm(True)
+        compiled = torch.compile(ql.forward, fullgraph=True, backend="aot_eager")
+        for rows in (3, 100):
+            x = torch.randn(rows, 2048, device=cuda_device).half()
+            assert torch.equal(compiled(x), ql(x))
+    finally:
+        quantize.set_dequant_impl(old)
+        quantize.set_prefill_gemm(old_gemm)

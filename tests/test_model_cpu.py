@@ -134,3 +134,20 @@ def test_sample_top_p_keeps_the_nucleus():
     probs = torch.tensor([[0.05, 0.5, 0.1, 0.3, 0.05]]).repeat(2000, 1)
     drawn = sample_top_p(probs, 0.75).view(-1)
     assert set(drawn.tolist()) == {1, 3}  # 0.5 + 0.3 reaches 0.75; 0.1 starts above it
+
+
+def test_int4_operators_trace_with_fake_tensors():
+    """li4::int4_linear and li4::int4_gemm are registered PyTorch operators whose fake kernels give the
+    output shape without running anything (what torch.compile traces through)."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    from llama.quantize import QuantizedLinear
+
+    QuantizedLinear(256, 64)  # constructing a layer registers the operators
+    with FakeTensorMode():
+        x = torch.empty(2, 3, 256, dtype=torch.float16)
+        p = torch.empty(64, 128, dtype=torch.uint8)
+        s = torch.empty(64, 2, dtype=torch.float16)
+        assert torch.ops.li4.int4_linear(x, p, s, s, 128).shape == (2, 3, 64)
+        xm = torch.empty(40, 256, dtype=torch.float16)
+        assert torch.ops.li4.int4_gemm(xm, p, s, s, 128).shape == (40, 64)
