@@ -174,7 +174,9 @@ def plan(M: int, N: int, K: int, group_size: int = 128, sm_count: int = 0) -> di
 
 
 def stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The current CUDA stream of `device` as a raw handle (cheap: no Stream object is built)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(idx)
 
 
 def ptr(t: torch.Tensor) -> int:
