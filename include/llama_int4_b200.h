@@ -151,8 +151,10 @@ int li4_int4_gemm(const void* x, const void* packed, const void* scale, const vo
  * the array are rejected with LI4_ERR_WORKSPACE (for example M=16, N=32768,
  * K=8192).  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress, which may load the module): make that first call
- * before any stream capture.  All calls share the array, so calls that may
- * overlap on the GPU (different streams) race; keep them on one stream.
+ * before any stream capture.  The address is cached per device ordinal for the
+ * life of the process: a device reset (cudaDeviceReset) between calls is not
+ * supported.  All calls share the array, so calls that may overlap on the GPU
+ * (different streams) race; keep them on one stream.
  * No counterpart in the reference: its int4_linear allocates its split-K
  * buffer with torch.zeros on every call. */
 int li4_int4_linear_noalloc(const void* x, const void* packed, const void* scale, const void* zero, void* y,
