@@ -189,8 +189,11 @@ typedef enum li4_epilogue_kind {
   LI4_EPI_SWIGLU = 2,    /* y = fp16(fp16(silu(g)) * u), g, u = fp16 outputs of pair  */
   LI4_EPI_QKV_ROPE = 3,  /* RoPE on q, k pairs at position *pos; q -> q_out,
                             k and v -> cache_k / cache_v at row *pos (y unused)       */
-  LI4_EPI_STORE_F32 = 4  /* y is fp32 [M, N] (row stride in fp32 elements):
+  LI4_EPI_STORE_F32 = 4, /* y is fp32 [M, N] (row stride in fp32 elements):
                             y = (float)fp16(x W^T), the reference's output(h).float() */
+  LI4_EPI_ALLREDUCE_RESIDUAL = 5  /* row-parallel linear under tensor parallelism:
+                            y = fp16(residual + fp16(sum_r P_r)), P_r = fp16(x W_r^T) of
+                            rank r, summed in fp32 in rank order (ar_* fields)          */
 } li4_epilogue_kind;
 
 typedef struct li4_fusion {
@@ -229,6 +232,22 @@ typedef struct li4_fusion {
   int64_t* argmax_out;
   int64_t argmax_stride;
   void* argmax_scratch;
+  /* LI4_EPI_ALLREDUCE_RESIDUAL (also needs residual / stride_rm; N % 16 == 0).  The launch
+   * pushes its fp16 partial P_rank to every rank as 8-byte words -- two outputs (rows j and
+   * j + 8 of a 16-row tile) and the call's epoch -- stored straight into each rank's receive
+   * buffer over NVLink, then waits (bounded) until its own buffer holds every rank's words of
+   * the same tiles and writes y.  Receive buffer layout: [world][N / 16][M][8] words of
+   * 8 bytes (sender outermost).  ar_recv: host array of ar_world device pointers, rank r's
+   * buffer at [r] (the peers' mapped through CUDA IPC), each ar_recv_bytes long;
+   * ar_epochs: this rank's uint32 call counts per 16-row tile [N / 16], zero before the
+   * first call and updated by the launch.  Every rank makes the same sequence of calls on a
+   * buffer; two calls in a row use different buffers (and epoch arrays), so a rank never
+   * overwrites words a peer is still reading.  Runs on the streaming-warp kernel.  A wait
+   * that runs out sets bit 5 of li4_device_errors and the launch finishes with what it read. */
+  void* const* ar_recv;
+  size_t ar_recv_bytes;
+  unsigned* ar_epochs;
+  int ar_world, ar_rank;
 } li4_fusion;
 
 /* li4_int4_linear with a fused prologue / epilogue (`fusion` NULL = plain).
@@ -292,13 +311,15 @@ int li4_gather_rows(const void* table, int64_t table_rows, int64_t cols, int64_t
  * inside a GEMV kernel ran out; bit 1: a bounded wait for a peer's flag in
  * li4_allreduce_add ran out; bit 2: a decode program's wait for another op
  * ran out; bit 3: a gather (li4_gather_rows or a program gather) met an id
- * outside its table; bit 4: a bounded wait inside li4_int4_gemm ran out -- the kernel
+ * outside its table; bit 4: a bounded wait inside li4_int4_gemm ran out; bit 5: an
+ * LI4_EPI_ALLREDUCE_RESIDUAL epilogue's wait for a peer's words ran out -- the kernel
  * carried on and its outputs are not valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);
 
 /* Test hook for the bounded device waits: the poll limit of li4_allreduce_add's
- * peer-flag waits (allreduce_polls), the poll limit of the decode program's
+ * peer-flag waits and of the LI4_EPI_ALLREDUCE_RESIDUAL epilogue's waits for the
+ * peers' words (allreduce_polls), the poll limit of the decode program's
  * op-counter waits (program_polls) -- 0 restores each default (about a second
  * of polling) -- and, when program_wait_extra > 0, a target no program counter
  * wait can meet.  With a short limit a test can make a wait run out without a

@@ -7,7 +7,8 @@
 // not bandwidth: NCCL's ring / tree steps each cross the switch.  Here every
 // rank's GEMV writes its partial straight into a buffer that all ranks have
 // mapped (CUDA IPC), and one kernel per rank
-//   1. raises its flag in every peer's flag array (system-scope release),
+//   1. raises its flag in every peer's flag array (system-scope release, which
+//      orders the partial the preceding kernel wrote before the flag),
 //   2. waits (bounded) until every peer's flag is up (system-scope acquire),
 //   3. reads all partials of its slice over NVLink, sums them in fp32 in rank
 //      order and writes fp16(residual + fp16(sum)).
@@ -69,10 +70,10 @@ __global__ void __launch_bounds__(kArThreads) allreduce_add_kernel(const __grid_
   const int c = blockIdx.x, C = gridDim.x;
   pdl_launch_dependents();
   pdl_wait_primary();  // this rank's partial was written by the preceding kernel
-  if (threadIdx.x == 0) {
-    s_epoch = a.counts[c] + 1;
-    __threadfence_system();  // the partial (and everything before) is visible system-wide first
-  }
+  // The partial was written by the preceding kernel, whose writes griddepcontrol.wait made visible
+  // to this grid; the flag's system-scope release below orders them before the flag for the peers.
+  // (A separate fence.sc.sys here measured 14.0 against 9.4 us per call on two B200s.)
+  if (threadIdx.x == 0) s_epoch = a.counts[c] + 1;
   __syncthreads();
   const unsigned epoch = s_epoch;
   if (threadIdx.x < a.world) {  // raise our flag in rank t's array, then wait for rank t's flag in ours

@@ -482,7 +482,167 @@ __device__ __forceinline__ void stream_load(const GemvArgs& a, StreamUnit& u, co
   u.sz_hi = ldg_u16(r.s_hi + g) | (ldg_u16(r.z_hi + g) << 16);
 }
 
-template <int NT, bool KSPLIT, bool FUSED>
+// ---------------------------------------------------------------------------
+// All-reduce + residual epilogue (LI4_EPI_ALLREDUCE_RESIDUAL), streaming-warp kernel only.
+//
+// Under tensor parallelism a row-parallel linear's output is the sum over ranks of
+// each rank's fp16 partial.  Here the GEMV that computes a tile also finishes it:
+// the tile's outputs go out as 8-byte words {fp16 row j, fp16 row j + 8, epoch},
+// stored straight into every peer's receive buffer over NVLink (one 8-byte store
+// is seen whole, so the epoch in a word vouches for its data: no flags, no fences),
+// and the same threads then poll their own receive buffer until every peer's word
+// of the same (tile, m, j) carries this call's epoch, sum the ranks' values in fp32
+// in rank order, round, add the residual and store -- exactly the arithmetic of
+// li4_allreduce_add after a plain GEMV.  The epoch of a tile is its call count on
+// this rank (ar_epochs, one atomic per tile and call); all ranks make the same calls,
+// so their counts agree.  A wait that runs out sets bit 5 and uses what it read; the
+// thread's later words then get one poll each, so a missing peer costs one poll limit.
+// ---------------------------------------------------------------------------
+constexpr unsigned kArEpiWaitLimit = 1u << 20;  // polls of one word before giving up
+__device__ unsigned g_ar_epi_wait_limit = kArEpiWaitLimit;  // li4_debug_set_wait_limits shortens it for tests
+
+int gemv_set_ar_wait_limit(unsigned polls) {
+  const unsigned v = polls ? polls : kArEpiWaitLimit;
+  return check_cuda(cudaMemcpyToSymbol(g_ar_epi_wait_limit, &v, sizeof(v)), "debug_set_wait_limits: fused all-reduce");
+}
+
+__device__ __forceinline__ unsigned long long ar_pack(float v0, float v1, unsigned epoch) {
+  const __half2 h = __floats2half2_rn(v0, v1);
+  return ((unsigned long long)epoch << 32) | *reinterpret_cast<const unsigned*>(&h);
+}
+
+__device__ __forceinline__ long long ar_index(const GemvArgs& a, int tile, int m, int j) {
+  return ((long long)tile * a.M + m) * 8 + j;
+}
+
+// This rank's word into every other rank's receive buffer (its own value stays in registers).
+__device__ __forceinline__ void ar_push(const GemvArgs& a, long long widx, unsigned long long w) {
+  for (int r = 0; r < a.ar_world; ++r) {
+    if (r == a.ar_rank) continue;
+    unsigned long long* dst = a.ar_recv[r] + (long long)a.ar_rank * a.ar_words + widx;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+  }
+}
+
+// Up to W words of this thread (live mask) summed over the ranks in rank order, and rows
+// row[i], row[i] + 8 of output row m[i] stored.  The residuals are requested first, and each
+// rank's W words are polled together, so a thread's words cost one round trip per rank.
+template <int W>
+__device__ __forceinline__ void ar_finish(const GemvArgs& a, const long long (&widx)[W], const int (&m)[W],
+                                          const int (&row)[W], unsigned live, const unsigned long long (&own)[W],
+                                          unsigned epoch) {
+  float rs0[W], rs1[W], s0[W], s1[W];
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    s0[i] = s1[i] = rs0[i] = rs1[i] = 0.f;
+    if (live >> i & 1u) {
+      const __half* res = a.res + (long long)m[i] * a.srm + row[i];
+      rs0[i] = __half2float(res[0]);
+      rs1[i] = __half2float(res[8]);
+    }
+  }
+  bool failed = false;
+  for (int r = 0; r < a.ar_world; ++r) {
+    unsigned long long w[W];
+#pragma unroll
+    for (int i = 0; i < W; ++i) w[i] = own[i];
+    if (r != a.ar_rank) {
+      const unsigned long long* base = a.ar_recv[a.ar_rank] + (long long)r * a.ar_words;
+      const unsigned limit = failed ? 1u : g_ar_epi_wait_limit;
+      unsigned pending = live;
+      for (unsigned it = 0; pending != 0u; ++it) {
+#pragma unroll
+        for (int i = 0; i < W; ++i)
+          if (pending >> i & 1u) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(base + widx[i]) : "memory");
+#pragma unroll
+        for (int i = 0; i < W; ++i)
+          if ((pending >> i & 1u) && (unsigned)(w[i] >> 32) == epoch) pending &= ~(1u << i);
+        if (pending != 0u && it + 1 >= limit) {
+          if (!failed) atomicOr(&g_li4_device_error, 32u);
+          failed = true;
+          break;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      const unsigned lo = (unsigned)w[i];
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+      s0[i] += f.x;
+      s1[i] += f.y;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    if (!(live >> i & 1u)) continue;
+    const float2 sum = __half22float2(__floats2half2_rn(s0[i], s1[i]));  // fp16 of the all-reduced partials
+    __half* y = a.y + (long long)m[i] * a.sym + row[i];
+    y[0] = __float2half_rn(rs0[i] + sum.x);
+    y[8] = __float2half_rn(rs1[i] + sum.y);
+  }
+}
+
+// A 16-row tile from a group of nthr threads that can all read value(r, m), W words per thread
+// (W * nthr >= 8 * M): every word is computed, then pushed, then finished.
+template <int W, typename F>
+__device__ __forceinline__ void emit_tile_ar(const GemvArgs& a, int tile, int tid, int nthr, F value, unsigned epoch) {
+  long long widx[W];
+  int mm[W], row[W];
+  unsigned long long own[W];
+  unsigned live = 0;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    const int idx = tid + i * nthr, m = idx >> 3, j = idx & 7;
+    mm[i] = m;
+    row[i] = tile * 16 + j;
+    widx[i] = ar_index(a, tile, m, j);
+    own[i] = 0ull;
+    if (idx < 8 * a.M) {
+      live |= 1u << i;
+      own[i] = ar_pack(value(j, m), value(j + 8, m), epoch);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < W; ++i)
+    if (live >> i & 1u) ar_push(a, widx[i], own[i]);
+  ar_finish<W>(a, widx, mm, row, live, own, epoch);
+}
+
+// Rows mode, split == 1: a warp's tile from its lanes' accumulators; lane (grp, quad) holds rows
+// grp and grp + 8 of columns nt*8 + 2*quad + {0, 1}, i.e. whole words.
+template <int NT>
+__device__ __forceinline__ void emit_warp_tile_ar(const GemvArgs& a, int tile, const float (&acc)[NT][4], int grp,
+                                                  int quad, unsigned epoch) {
+  constexpr int W = 2 * NT;
+  long long widx[W];
+  int mm[W], row[W];
+  unsigned long long own[W];
+  unsigned live = 0;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int i = 2 * nt + e, m = nt * 8 + 2 * quad + e;
+      mm[i] = m;
+      row[i] = tile * 16 + grp;
+      widx[i] = ar_index(a, tile, m, grp);
+      own[i] = ar_pack(acc[nt][e], acc[nt][e + 2], epoch);
+      if (m < a.M) live |= 1u << i;
+    }
+#pragma unroll
+  for (int i = 0; i < W; ++i)
+    if (live >> i & 1u) ar_push(a, widx[i], own[i]);
+  ar_finish<W>(a, widx, mm, row, live, own, epoch);
+}
+
+// The call's epoch of a tile, taken by lane 0 of the calling warp and shared with the warp.
+__device__ __forceinline__ unsigned ar_warp_epoch(const GemvArgs& a, int tile, int lane) {
+  unsigned e = 0;
+  if (lane == 0) e = atomicAdd(&a.ar_epochs[tile], 1u) + 1u;
+  return __shfl_sync(0xffffffffu, e, 0);
+}
+
+template <int NT, bool KSPLIT, bool FUSED, bool AR = false>
 __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int D = kStreamDepth;
@@ -517,6 +677,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
   if (KSPLIT) prefetch_residual<FUSED>(a, blockIdx.x, threadIdx.x);
   else prefetch_residual<FUSED>(a, blockIdx.x * kStreamWarps + warp, lane);
   __shared__ float s_rstd[LI4_MAX_M];
+  __shared__ unsigned s_ar_epoch[2];  // K-split mode, all-reduce epilogue: the tile's epoch (double-buffered as red)
   if (FUSED && a.norm_w != nullptr) {
     if (a.ssq_in != nullptr) rms_from_ssq<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
     else rms_factors<kStreamWarps>(a, s_rstd, threadIdx.x >> 5, threadIdx.x & 31);
@@ -562,7 +723,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
         const int rows = min(16, a.N - row0);
         if (!KSPLIT) {
           if (a.split == 1) {
-            emit_warp_tile<FUSED, NT>(a, tile, acc, grp, quad);
+            if constexpr (AR)
+              emit_warp_tile_ar<NT>(a, tile, acc, grp, quad, ar_warp_epoch(a, tile, lane));
+            else
+              emit_warp_tile<FUSED, NT>(a, tile, acc, grp, quad);
           } else {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
@@ -584,7 +748,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
               __threadfence();
-              if constexpr (NT == 2) emit_partial_tile<FUSED>(a, tile, lane, PartialSum{a.partial + row0, a.M, a.N, a.split});
+              if constexpr (AR)
+                emit_tile_ar<4>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split},
+                                ar_warp_epoch(a, tile, lane));
+              else if constexpr (NT == 2) emit_partial_tile<FUSED>(a, tile, lane, PartialSum{a.partial + row0, a.M, a.N, a.split});
               else emit_tile<FUSED>(a, tile, lane, 32, PartialSum{a.partial + row0, a.M, a.N, a.split});
               __syncwarp();
               if (lane == 0) a.counters[tile] = 0u;
@@ -599,10 +766,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
               rb[(warp * 16 + grp + 8 * (e >> 1)) * COLS + nt * 8 + 2 * quad + (e & 1)] = acc[nt][e];
               acc[nt][e] = 0.f;
             }
+          const bool ar = AR && a.split == 1;
+          if (ar && threadIdx.x == 0) s_ar_epoch[tiles_done & 1] = atomicAdd(&a.ar_epochs[tile], 1u) + 1u;
           __syncthreads();
           const WarpTileSum<COLS, kStreamWarps> tile_sum{rb};
           if (a.split == 1) {
-            emit_tile<FUSED>(a, tile, threadIdx.x, kStreamThreads, tile_sum);
+            if (ar) emit_tile_ar<1>(a, tile, threadIdx.x, kStreamThreads, tile_sum, s_ar_epoch[tiles_done & 1]);
+            else emit_tile<FUSED>(a, tile, threadIdx.x, kStreamThreads, tile_sum);
           } else {
             for (int idx = threadIdx.x; idx < rows * a.M; idx += kStreamThreads) {
               const int r = idx / a.M, m = idx - (idx / a.M) * a.M;
@@ -612,7 +782,21 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(const __
           if (a.split > 1) {
             __threadfence();  // every writer publishes its partials before the arrival count
             __syncthreads();
-            if (warp == 0) {
+            if constexpr (AR) {
+              // the last K range to arrive finishes the tile with the whole CTA (one word per thread)
+              if (threadIdx.x == 0) {
+                const bool last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1);
+                if (last) a.counters[tile] = 0u;
+                s_ar_epoch[tiles_done & 1] = last ? atomicAdd(&a.ar_epochs[tile], 1u) + 1u : 0u;
+              }
+              __syncthreads();
+              const unsigned ep = s_ar_epoch[tiles_done & 1];
+              if (ep != 0u) {
+                __threadfence();
+                emit_tile_ar<1>(a, tile, threadIdx.x, kStreamThreads, PartialSum{a.partial + row0, a.M, a.N, a.split},
+                                ep);
+              }
+            } else if (warp == 0) {
               unsigned last = 0;
               if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.split - 1)) ? 1u : 0u;
               last = __shfl_sync(0xffffffffu, last, 0);
@@ -1490,6 +1674,16 @@ static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
       default: return launch_stream_kernel(gemv_tile_kernel<2, 2, true>, p, args, s);
     }
   }
+  if (p.kernel == LI4_KERNEL_STREAM && args.epi == LI4_EPI_ALLREDUCE_RESIDUAL) {
+    // the all-reduce epilogue: its own instantiations, so the others keep their registers
+    const int sel = (p.nt - 1) * 2 + (p.stream_ksplit ? 1 : 0);
+    switch (sel) {
+      case 0: return launch_stream_kernel(gemv_stream_kernel<1, false, true, true>, p, args, s);
+      case 1: return launch_stream_kernel(gemv_stream_kernel<1, true, true, true>, p, args, s);
+      case 2: return launch_stream_kernel(gemv_stream_kernel<2, false, true, true>, p, args, s);
+      default: return launch_stream_kernel(gemv_stream_kernel<2, true, true, true>, p, args, s);
+    }
+  }
   if (p.kernel == LI4_KERNEL_STREAM) {
     const int sel = (p.nt - 1) * 4 + (p.stream_ksplit ? 2 : 0) + (fused ? 1 : 0);
     switch (sel) {
@@ -1560,6 +1754,27 @@ static int check_fusion(const li4_fusion& f, int64_t M, int64_t N, int64_t K) {
         return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: SwiGLU pairs need N %% 16 == 0 (N=%lld)",
                          (long long)N);
       return LI4_OK;
+    case LI4_EPI_ALLREDUCE_RESIDUAL: {
+      if (!f.residual || f.stride_rm < N || (reinterpret_cast<uintptr_t>(f.residual) & 1u) || N % 16 != 0)
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: the all-reduce epilogue needs a residual [M, N] "
+                         "(row stride >= N) and N %% 16 == 0 (N=%lld)", (long long)N);
+      if (f.ar_world < 1 || f.ar_world > 8 || f.ar_rank < 0 || f.ar_rank >= f.ar_world || !f.ar_recv ||
+          !f.ar_epochs || !aligned4(f.ar_epochs))
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: all-reduce epilogue: world=%d rank=%d (1..8 ranks), "
+                         "receive buffers and a 4-byte aligned epoch array", f.ar_world, f.ar_rank);
+      const size_t need = (size_t)f.ar_world * (size_t)(N / 16) * (size_t)M * 8 * sizeof(unsigned long long);
+      if (f.ar_recv_bytes < need)
+        return set_error(LI4_ERR_INVALID_ARG, "int4_linear_fused: all-reduce receive buffers of %zu bytes, %zu needed "
+                         "(world x N/16 x M x 8 words of 8 bytes)", f.ar_recv_bytes, need);
+      for (int r = 0; r < f.ar_world; ++r)
+        if (!f.ar_recv[r] || (reinterpret_cast<uintptr_t>(f.ar_recv[r]) & 7u))
+          return set_error(LI4_ERR_ALIGNMENT, "int4_linear_fused: all-reduce receive buffer %d is null or not 8-byte "
+                           "aligned", r);
+      if (f.sumsq_out != nullptr || f.argmax_out != nullptr)
+        return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: the all-reduce epilogue takes neither sumsq_out nor "
+                         "the fused argmax");
+      return LI4_OK;
+    }
     case LI4_EPI_QKV_ROPE: {
       const int64_t v_rows = N - f.q_rows - f.k_rows;
       if (f.head_dim < 2 || f.head_dim % 2 != 0 || f.q_rows < 0 || f.k_rows <= 0 || f.q_rows % 16 != 0 ||
@@ -1640,6 +1855,13 @@ int prepare_linear(const void* x, const void* packed, const void* scale, const v
     args.ssq_out = f->sumsq_out;
     args.ssq_in = f->sumsq_in;
     args.ssq_tiles = (int)f->sumsq_tiles;
+    if (epi == LI4_EPI_ALLREDUCE_RESIDUAL) {
+      for (int r = 0; r < f->ar_world; ++r) args.ar_recv[r] = static_cast<unsigned long long*>(f->ar_recv[r]);
+      args.ar_epochs = f->ar_epochs;
+      args.ar_words = (N / 16) * M * 8;
+      args.ar_world = f->ar_world;
+      args.ar_rank = f->ar_rank;
+    }
     if (f->argmax_out != nullptr) {
       args.am_keys = static_cast<unsigned long long*>(f->argmax_scratch);
       args.am_count = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(f->argmax_scratch) + 8 * M);
@@ -1679,6 +1901,14 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     if (kernel != LI4_KERNEL_AUTO)
       return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: the register-rows kernel needs a 16-byte aligned x and "
                        "no RMSNorm prologue or fused argmax");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
+  if (f != nullptr && f->epilogue == LI4_EPI_ALLREDUCE_RESIDUAL && p.kernel != LI4_KERNEL_STREAM) {
+    // the all-reduce epilogue runs on the streaming-warp kernel
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: the all-reduce epilogue runs on the streaming-warp "
+                       "kernel only");
     rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
     if (rc != LI4_OK) return rc;
   }
@@ -1792,6 +2022,14 @@ extern "C" int li4_device_errors(unsigned* flags, int reset) {
   unsigned gemm = 0;
   if (rc == LI4_OK) rc = li4::gemm_device_errors(&gemm, reset != 0);
   if (rc == LI4_OK) *flags |= gemm;
+  // the GEMV error words of the other translation units that run GEMV code
+  int (*const readers[])(unsigned*, bool) = {li4::slab_device_errors, li4::rows_device_errors,
+                                             li4::program_gemv_device_errors};
+  for (auto read : readers) {
+    unsigned f = 0;
+    if (rc == LI4_OK) rc = read(&f, reset != 0);
+    if (rc == LI4_OK) *flags |= f;
+  }
   if (rc == LI4_OK) li4::clear_error();
   return rc;
 }

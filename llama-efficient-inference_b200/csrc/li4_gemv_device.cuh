@@ -5,6 +5,7 @@
 #pragma once
 
 #include "li4_common.cuh"
+#include "li4_internal.h"
 #include "../../include/llama_int4_b200.h"
 
 namespace li4 {
@@ -51,6 +52,12 @@ struct GemvArgs {
   unsigned* am_count;            // then the CTA arrival count (li4_fusion.argmax_scratch)
   long long* am_out;
   long long am_stride;
+  // LI4_EPI_ALLREDUCE_RESIDUAL: every rank's receive buffer [world][ar_words] (peer pointers),
+  // this rank's per-tile call counts, words per sender (N / 16 * M * 8)
+  unsigned long long* ar_recv[8];
+  unsigned* ar_epochs;
+  long long ar_words;
+  int ar_world, ar_rank;
 };
 
 // ---------------------------------------------------------------------------
@@ -134,7 +141,8 @@ struct WarpTileSum {
 // the group prefetch one 32-byte segment each (rows tile*16 .. +16 of row m).
 template <bool FUSED>
 __device__ __forceinline__ void prefetch_residual(const GemvArgs& a, int tile16, int tid) {
-  if (FUSED && a.epi == LI4_EPI_RESIDUAL && tid < a.M && tile16 >= 0 && tile16 * 16 < a.N)
+  if (FUSED && (a.epi == LI4_EPI_RESIDUAL || a.epi == LI4_EPI_ALLREDUCE_RESIDUAL) && tid < a.M && tile16 >= 0 &&
+      tile16 * 16 < a.N)
     asm volatile("prefetch.global.L1 [%0];" ::"l"(a.res + (long long)tid * a.srm + tile16 * 16));
 }
 
@@ -533,9 +541,20 @@ __device__ __forceinline__ void stream_compute(const StreamUnit& u, const uint8_
 
 constexpr unsigned kBulkWaitLimit = 1u << 22;  // try_wait rounds: well under a second of polling, never forever
 
-// Device error word of the translation unit that includes this header (each has its own copy;
-// li4_device_errors collects them).  Bit 0: a bounded pipeline wait ran out.
+// Device error word of the translation unit that includes this header (each has its own copy,
+// read through tu_device_errors; li4_device_errors collects them).  Bit 0: a bounded pipeline
+// wait ran out; bit 5: a fused all-reduce epilogue's wait ran out.
 static __device__ unsigned g_li4_device_error;
+
+// Host side: this translation unit's copy of the device error word, cleared when reset.
+static inline int tu_device_errors(unsigned* flags, bool reset) {
+  int rc = check_cuda(cudaMemcpyFromSymbol(flags, g_li4_device_error, sizeof(unsigned)), "device_errors: reading");
+  if (rc == LI4_OK && reset) {
+    const unsigned zero = 0;
+    rc = check_cuda(cudaMemcpyToSymbol(g_li4_device_error, &zero, sizeof(unsigned)), "device_errors: clearing");
+  }
+  return rc;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

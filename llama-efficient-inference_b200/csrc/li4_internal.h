@@ -23,6 +23,12 @@ int comm_device_errors(unsigned* flags, bool reset);
 int program_device_errors(unsigned* flags, bool reset);
 // Device error word of the tensor-core GEMM (li4_gemm.cu); reset clears it.
 int gemm_device_errors(unsigned* flags, bool reset);
+// The GEMV device error words of the slab, register-rows and program translation units.
+int slab_device_errors(unsigned* flags, bool reset);
+int rows_device_errors(unsigned* flags, bool reset);
+int program_gemv_device_errors(unsigned* flags, bool reset);
+// Poll limit of the LI4_EPI_ALLREDUCE_RESIDUAL epilogue's waits (0 = default).
+int gemv_set_ar_wait_limit(unsigned polls);
 // Poll limit of the all-reduce flag waits (li4_comm.cu); 0 restores the default.
 int comm_set_wait_limit(unsigned polls);
 // Poll limit of the program's counter waits and an unmeetable-target offset (li4_program.cu).

@@ -793,6 +793,8 @@ __global__ void __launch_bounds__(prog_threads(NT), 1) decode_program_kernel(con
   }
 }
 
+int program_gemv_device_errors(unsigned* flags, bool reset) { return tu_device_errors(flags, reset); }
+
 }  // namespace li4
 
 namespace li4 {

@@ -189,4 +189,6 @@ int launch_rows(const GemvArgs& a, bool fused, cudaStream_t stream) {
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, a), "int4_linear: register-rows kernel launch");
 }
 
+int rows_device_errors(unsigned* flags, bool reset) { return tu_device_errors(flags, reset); }
+
 }  // namespace li4

@@ -474,4 +474,6 @@ int launch_slab(const GemvArgs& a, int nt, bool fused, int grid_x, int tiles_max
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, a, sa), "int4_linear: slab kernel launch");
 }
 
+int slab_device_errors(unsigned* flags, bool reset) { return tu_device_errors(flags, reset); }
+
 }  // namespace li4

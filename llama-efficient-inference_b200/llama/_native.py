@@ -33,6 +33,7 @@ _SZ = ctypes.c_size_t
 _INT = ctypes.c_int
 
 LI4_EPI_STORE, LI4_EPI_RESIDUAL, LI4_EPI_SWIGLU, LI4_EPI_QKV_ROPE, LI4_EPI_STORE_F32 = 0, 1, 2, 3, 4
+LI4_EPI_ALLREDUCE_RESIDUAL = 5
 
 
 class Fusion(ctypes.Structure):
@@ -63,6 +64,11 @@ class Fusion(ctypes.Structure):
         ("argmax_out", ctypes.c_void_p),
         ("argmax_stride", ctypes.c_int64),
         ("argmax_scratch", ctypes.c_void_p),
+        ("ar_recv", ctypes.c_void_p),
+        ("ar_recv_bytes", ctypes.c_size_t),
+        ("ar_epochs", ctypes.c_void_p),
+        ("ar_world", ctypes.c_int),
+        ("ar_rank", ctypes.c_int),
     ]
 
 

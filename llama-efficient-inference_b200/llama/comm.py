@@ -10,6 +10,12 @@ GEMV writes its fp16 partial straight into this rank's slot (`slot_ptr`), then
 `all_reduce_add` sums the slots of all ranks over NVLink and adds the residual
 in one launch.  Calls alternate the two slots; every rank must make the same
 sequence of calls.
+
+The same buffer also holds two receive buffers for the fused form
+(`push_fusion`): the row-parallel GEMV itself stores its fp16 partial, as
+8-byte words that carry the call's epoch, into every peer's receive buffer
+and finishes the sum and the residual in its own launch
+(LI4_EPI_ALLREDUCE_RESIDUAL), with no separate all-reduce kernel.
 """
 from __future__ import annotations
 
@@ -39,7 +45,10 @@ class NvlinkAllReduce:
         self.device, self.ctas, self.max_elems = device, ctas, max_elems
         lib = native.lib()
         self.slot_bytes = _round_up(2 * max_elems)
-        total = 2 * self.slot_bytes + _round_up(4 * ctas * self.world)
+        self.flag_bytes = _round_up(4 * ctas * self.world)
+        # fused form: per receive buffer, every rank's words [world][max_elems / 2] of 8 bytes
+        self.recv_bytes = _round_up(self.world * ((max_elems + 1) // 2) * 8)
+        total = 2 * self.slot_bytes + self.flag_bytes + 2 * self.recv_bytes
         with torch.cuda.device(device):
             base = ctypes.c_void_p()
             native.check(lib.li4_comm_alloc(total, ctypes.byref(base)), "comm_alloc")
@@ -63,6 +72,10 @@ class NvlinkAllReduce:
         self._slots = [arr(*[b + s * self.slot_bytes for b in bases]) for s in (0, 1)]
         self._flags = arr(*[b + 2 * self.slot_bytes for b in bases])
         self.counts = torch.zeros(ctas, dtype=torch.int32, device=device)
+        recv0 = 2 * self.slot_bytes + self.flag_bytes
+        self._recv = [arr(*[b + recv0 + s * self.recv_bytes for b in bases]) for s in (0, 1)]
+        # per receive buffer, this rank's call count of every 16-row output tile
+        self.epochs = torch.zeros(2, (max_elems + 15) // 16, dtype=torch.int32, device=device)
 
     def slot_ptr(self, slot: int) -> int:
         """Device address of this rank's partial slot `slot` (0 or 1), fp16, max_elems values."""
@@ -77,6 +90,17 @@ class NvlinkAllReduce:
                                            self.world, self.rank, n, residual.data_ptr(), out.data_ptr(),
                                            native.stream_ptr(out.device))
         native.check(rc, "allreduce_add")
+
+    def push_fusion(self, slot: int, residual: torch.Tensor) -> native.Fusion:
+        """The li4_fusion of a row-parallel GEMV that finishes its own all-reduce + residual add
+        (LI4_EPI_ALLREDUCE_RESIDUAL) through receive buffer `slot` (0 or 1): y = fp16(residual +
+        fp16(sum over ranks of their fp16 partials)), the same values as all_reduce_add."""
+        if residual.numel() > self.max_elems or residual.stride(-1) != 1:
+            raise RuntimeError(f"push_fusion: a row-major residual of at most {self.max_elems} values")
+        return native.Fusion(epilogue=native.LI4_EPI_ALLREDUCE_RESIDUAL, residual=residual.data_ptr(),
+                             stride_rm=residual.stride(0), ar_recv=ctypes.cast(self._recv[slot], ctypes.c_void_p),
+                             ar_recv_bytes=self.recv_bytes, ar_epochs=self.epochs[slot].data_ptr(),
+                             ar_world=self.world, ar_rank=self.rank)
 
     def close(self) -> None:
         lib = native.lib()

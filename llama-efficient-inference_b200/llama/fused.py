@@ -19,10 +19,13 @@ adds.  Here a block is:
 
 and the step ends with lm_head with the final RMSNorm fused into its staging.  The embedding rows
 come from li4_gather_rows and the greedy tokens from li4_argmax_rows.
-Under tensor parallelism the wo / w2 outputs are partial sums: each rank's GEMV
-writes its partial into a buffer every rank has mapped, and one kernel sums the
-ranks' partials over NVLink and adds the residual (llama.comm; NCCL plus a torch
-add with nvlink_allreduce=False).
+Under tensor parallelism the wo / w2 outputs are partial sums.  By default the
+row-parallel GEMV finishes them itself: it stores its fp16 partial into every
+rank's receive buffer over NVLink and sums the ranks' partials with the residual
+in the same launch (LI4_EPI_ALLREDUCE_RESIDUAL, llama.comm.push_fusion).  With
+fused_allreduce=False the GEMV writes its partial into a buffer every rank has
+mapped and a second kernel sums the partials (li4_allreduce_add); with
+nvlink_allreduce=False NCCL all-reduces and torch adds the residual.
 
 The fused epilogues pair two GEMV outputs in one thread.  They take weights
 whose rows are rearranged once, at construction (pair_permutation,
@@ -187,9 +190,10 @@ class FusedDecoder:
     # batch 4 it is even (0.7372 vs 0.7363 ms).
     sumsq_handoff_max_batch = 4
 
-    def __init__(self, model, nvlink_allreduce: bool = True, program: bool = False):
+    def __init__(self, model, nvlink_allreduce: bool = True, program: bool = False, fused_allreduce: bool = True):
         self.model = model
         self.nvlink_allreduce = nvlink_allreduce
+        self.fused_allreduce = fused_allreduce
         # single GPU: the whole step as one persistent launch (llama.program) where it applies
         self.use_program = program
         self._programs = {}
@@ -240,8 +244,9 @@ class FusedDecoder:
 
     def _row_parallel(self, x: torch.Tensor, w, residual: torch.Tensor, out: torch.Tensor, part: torch.Tensor,
                       group, slot: int) -> None:
-        """out = residual + allreduce(x @ w^T) for a row-parallel INT4 linear: the partial goes straight
-        into this rank's NVLink communication slot and one kernel sums the ranks' slots (or NCCL)."""
+        """out = residual + allreduce(x @ w^T) for a row-parallel INT4 linear: in the GEMV's own launch
+        (fused_allreduce), or the partial goes straight into this rank's NVLink communication slot and
+        one kernel sums the ranks' slots (or NCCL)."""
         E = native
         if self.nvlink_allreduce:
             if self._ar is None:
@@ -249,6 +254,9 @@ class FusedDecoder:
 
                 self._ar = NvlinkAllReduce(group, max_elems=self.model.params.max_batch_size * self.dim,
                                            device=self.device)
+            if self.fused_allreduce:
+                int4_linear_fused(x, *w, out, self._ar.push_fusion(slot, residual))
+                return
             int4_linear_fused(x, *w, None, E.Fusion(epilogue=E.LI4_EPI_STORE),
                               y_ptr=self._ar.slot_ptr(slot), y_stride=out.stride(0))
             self._ar.all_reduce_add(slot, residual, out)

@@ -322,15 +322,18 @@ class Llama(Generation):
         h = self.norm(h)
         return self._logits(h)
 
-    def enable_fused_decode(self, enabled: bool = True, nvlink_allreduce: bool = True, program: bool = False):
+    def enable_fused_decode(self, enabled: bool = True, nvlink_allreduce: bool = True, program: bool = False,
+                            fused_allreduce: bool = True):
         """Run decode_step as the fused INT4 kernels of llama.fused (five launches per block, or with
         program=True the whole step as one persistent launch, llama.program, on a single GPU).
         Needs a quantized fp16 model on a CUDA device; shares this model's KV caches.  Under tensor
-        parallelism the row-parallel sums go over NVLink peer memory (llama.comm), or NCCL."""
+        parallelism the row-parallel sums go over NVLink peer memory (llama.comm) inside the GEMV's
+        launch (fused_allreduce) or in a kernel of their own, or through NCCL."""
         if enabled:
             from .fused import FusedDecoder
 
-            self._fused = FusedDecoder(self, nvlink_allreduce=nvlink_allreduce, program=program)
+            self._fused = FusedDecoder(self, nvlink_allreduce=nvlink_allreduce, program=program,
+                                       fused_allreduce=fused_allreduce)
         else:
             self._fused = None
         return self

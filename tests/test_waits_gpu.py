@@ -1,8 +1,8 @@
 """The bounded device waits run out without a fault, report it, and leave the context usable.
 
-Two kernels here spin on memory that another agent writes: li4_allreduce_add waits for
-every peer's flag, and a decode program's op waits for the completion counter of the op it
-depends on.  Each wait gives up after a poll limit, sets its bit in li4_device_errors and
+Three kernels here spin on memory that another agent writes: li4_allreduce_add waits for
+every peer's flag, a row-parallel GEMV with the all-reduce epilogue waits for every peer's
+words, and a decode program's op waits for the completion counter of the op it depends on.  Each wait gives up after a poll limit, sets its bit in li4_device_errors and
 returns.  li4_debug_set_wait_limits shortens the limits so a test can make the waits run out
 on one GPU, with nothing faulting or hanging: the peer is a local buffer that nobody writes,
 and the program's counter target is one no op can meet.  Every test restores the defaults.
@@ -60,6 +60,49 @@ def test_allreduce_peer_wait_runs_out(native, cuda_device):
     torch.cuda.synchronize()
     assert native.device_errors(reset=True) == 0
     assert torch.equal(out, torch.full_like(out, 1.5))
+
+
+def test_fused_allreduce_wait_runs_out(native, cuda_device):
+    """Rank 0 of a 2-rank row-parallel GEMV that finishes its own all-reduce (LI4_EPI_ALLREDUCE_RESIDUAL),
+    with a "peer" whose words never arrive: every wait gives up after the short limit, sets bit 5, and
+    the launch still writes fp16(residual + fp16(own partial + the zeros it read)), which is the
+    residual epilogue's output; with the defaults back, a 1-rank call reports nothing."""
+    from llama import fused
+
+    lib = native.lib()
+    native.check(lib.li4_debug_set_wait_limits(SHORT, 0, 0), "debug_set_wait_limits")
+    M, N, K, world = 1, 2048, 1024, 2
+    gen = torch.Generator().manual_seed(5)
+    w = (torch.randn(N, K, generator=gen) * 0.02).half()
+    packed, scale, zero = oracle.quantize(w.numpy(), 128)
+    p, s, z = (torch.from_numpy(a).to(cuda_device) for a in (packed, scale, zero))
+    x = torch.randn(M, K, generator=gen).half().to(cuda_device)
+    res = torch.randn(M, N, generator=gen).half().to(cuda_device)
+    words = N // 16 * M * 8
+    recv = [torch.zeros(world * words, dtype=torch.int64, device=cuda_device) for _ in range(world)]
+    epochs = torch.zeros(N // 16, dtype=torch.int32, device=cuda_device)
+    ptrs = (ctypes.c_void_p * world)(*[r.data_ptr() for r in recv])
+    f = native.Fusion(epilogue=native.LI4_EPI_ALLREDUCE_RESIDUAL, residual=res.data_ptr(), stride_rm=N,
+                      ar_recv=ctypes.cast(ptrs, ctypes.c_void_p), ar_recv_bytes=world * words * 8,
+                      ar_epochs=epochs.data_ptr(), ar_world=world, ar_rank=0)
+    out = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    fused.int4_linear_fused(x, p, s, z, out, f)
+    torch.cuda.synchronize()
+    assert native.device_errors(reset=True) & 32, "the fused all-reduce wait did not report running out"
+    want = torch.empty_like(out)
+    fused.int4_linear_fused(x, p, s, z, want, native.Fusion(epilogue=native.LI4_EPI_RESIDUAL, residual=res.data_ptr(),
+                                                            stride_rm=N))
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    assert int(epochs.min()) == 1 and int(epochs.max()) == 1  # one call counted on every tile
+    # our words went into the "peer's" buffer with epoch 1; nothing arrived in ours
+    assert int((recv[1][:words] >> 32).min()) == 1 and int(recv[0].abs().max()) == 0
+    native.check(lib.li4_debug_set_wait_limits(0, 0, 0), "debug_set_wait_limits")
+    f.ar_world, f.ar_rank = 1, 0
+    fused.int4_linear_fused(x, p, s, z, out, f)
+    torch.cuda.synchronize()
+    assert native.device_errors(reset=True) == 0
+    assert torch.equal(out, want)
 
 
 def test_program_counter_wait_runs_out(native, cuda_device):

@@ -94,78 +94,105 @@ def gpu_parity():
         torch.cuda.synchronize(dev)
         del graph
         # the fused step (llama.fused) on the shards: row-parallel partial sums all-reduced in the graph
+        # (the wo / w2 GEMVs finish their own all-reduce; then with a separate all-reduce kernel)
         part.enable_fused_decode()
         fgraph = DecodeGraph(part, prompt.shape[0])
         t_fused = fgraph.tokens(prompt, steps)
         torch.cuda.synchronize(dev)
         del fgraph
+        part.enable_fused_decode(fused_allreduce=False)
+        sgraph = DecodeGraph(part, prompt.shape[0])
+        t_sep = sgraph.tokens(prompt, steps)
+        torch.cuda.synchronize(dev)
+        del sgraph
     same_eager = bool(torch.equal(t_full, t_part))
     same_graph = bool(torch.equal(t_part, t_graph))
     same_fused = bool(torch.equal(t_full, t_fused))
+    same_sep = bool(torch.equal(t_full, t_sep))
     print(json.dumps({"rank": rank, "world": world, "prefill_rel_err": prefill_err, "eager_tokens_equal": same_eager,
-                      "graph_tokens_equal": same_graph, "fused_graph_tokens_equal": same_fused}), flush=True)
+                      "graph_tokens_equal": same_graph, "fused_graph_tokens_equal": same_fused,
+                      "separate_allreduce_graph_tokens_equal": same_sep}), flush=True)
 
 
 def gpu_allreduce():
-    """li4_allreduce_add over NVLink peer memory against NCCL: each rank's INT4 GEMV writes its
-    partial into its communication slot; sum over ranks + residual, eager and replayed in a graph."""
+    """The row-parallel sum over NVLink peer memory against the same sum taken through NCCL, bit for bit:
+    li4_allreduce_add after a GEMV that writes its partial into this rank's slot, and the GEMV that
+    finishes the all-reduce in its own launch (LI4_EPI_ALLREDUCE_RESIDUAL); eager and replayed in a
+    graph, alternating the two buffers as the decode step does, over the streaming kernel's modes
+    (K-split and rows mode, with and without a split-K reduction)."""
     from llama import _native, fused
     from llama.comm import NvlinkAllReduce
     from llama.quantize import QuantizedLinear
 
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", rank)
-    M, N, K = 16, 2048, 1024  # a row-parallel down_proj shard at batch 16
-    gen = torch.Generator(device=dev).manual_seed(100 + rank)
-    w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
-    p, s, z = QuantizedLinear.quantize_tensor(w, 128)
-    ar = NvlinkAllReduce(dist.group.WORLD, max_elems=M * N, device=dev)
-    xs = [torch.randn(M, K, generator=gen, device=dev).half() for _ in range(4)]
-    res = torch.randn(M, N, generator=torch.Generator(device=dev).manual_seed(7), device=dev).half()
-    outs = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(4)]
     E = _native
-
-    def run():
-        for i, x in enumerate(xs):  # alternate the two slots as the decode step does
-            fused.int4_linear_fused(x, p, s, z, None, E.Fusion(epilogue=E.LI4_EPI_STORE),
-                                    y_ptr=ar.slot_ptr(i % 2), y_stride=N)
-            ar.all_reduce_add(i % 2, res, outs[i])
-
+    shapes = [(1, 2048, 2048 // world), (16, 2048, 2048 // world), (1, 2048, 8192 // world),
+              (16, 2048, 8192 // world), (1, 9472, 2048), (16, 9472, 4096)]
+    ar = NvlinkAllReduce(dist.group.WORLD, max_elems=max(m * n for m, n, _ in shapes), device=dev)
+    bitwise_sep = bitwise_fused = True
     worst = 0.0
     with torch.no_grad():
-        for _ in range(3):
-            run()
-        torch.cuda.synchronize(dev)
-        refs = []
-        for x in xs:
-            part = torch.empty(M, N, dtype=torch.float16, device=dev)
-            fused.int4_linear_fused(x, p, s, z, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
-            tot = part.float()
-            dist.all_reduce(tot)
-            refs.append((res.float() + tot.half().float()).half())
-        for o, r in zip(outs, refs):
-            worst = max(worst, float((o.float() - r.float()).abs().max() / r.float().abs().max()))
-        g = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            run()
-        torch.cuda.current_stream(dev).wait_stream(side)
-        torch.cuda.synchronize(dev)
-        with torch.cuda.graph(g):
-            run()
-        for o in outs:
-            o.zero_()
-        for _ in range(5):
-            g.replay()
-        torch.cuda.synchronize(dev)
-        for o, r in zip(outs, refs):
-            worst = max(worst, float((o.float() - r.float()).abs().max() / r.float().abs().max()))
-        del g
+        for M, N, K in shapes:
+            gen = torch.Generator(device=dev).manual_seed(100 + rank)
+            w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+            p, s, z = QuantizedLinear.quantize_tensor(w, 128)
+            xs = [torch.randn(M, K, generator=gen, device=dev).half() for _ in range(4)]
+            res = torch.randn(M, N, generator=torch.Generator(device=dev).manual_seed(7), device=dev).half()
+            sep = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(4)]
+            fus = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(4)]
+
+            def run():
+                for i, x in enumerate(xs):
+                    fused.int4_linear_fused(x, p, s, z, None, E.Fusion(epilogue=E.LI4_EPI_STORE),
+                                            y_ptr=ar.slot_ptr(i % 2), y_stride=N)
+                    ar.all_reduce_add(i % 2, res, sep[i])
+                for i, x in enumerate(xs):
+                    fused.int4_linear_fused(x, p, s, z, fus[i], ar.push_fusion(i % 2, res))
+
+            refs = []  # every rank's partial gathered, summed in fp32 in rank order, + residual
+            for x in xs:
+                part = torch.empty(M, N, dtype=torch.float16, device=dev)
+                fused.int4_linear_fused(x, p, s, z, part, E.Fusion(epilogue=E.LI4_EPI_STORE))
+                parts = [torch.empty_like(part) for _ in range(world)]
+                dist.all_gather(parts, part)
+                acc = torch.zeros(M, N, dtype=torch.float32, device=dev)
+                for t in parts:
+                    acc += t.float()
+                refs.append((res.float() + acc.half().float()).half())
+
+            def check():
+                nonlocal bitwise_sep, bitwise_fused, worst
+                for a, b, r in zip(sep, fus, refs):
+                    bitwise_sep &= bool(torch.equal(a, r))
+                    bitwise_fused &= bool(torch.equal(b, r))
+                    worst = max(worst, float((b.float() - r.float()).abs().max() / r.float().abs().max()))
+
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize(dev)
+            check()
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                run()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(g):
+                run()
+            for o in sep + fus:
+                o.zero_()
+            for _ in range(5):
+                g.replay()
+            torch.cuda.synchronize(dev)
+            check()
+            del g
     errors = _native.device_errors()
     dist.barrier()
     ar.close()
-    print(json.dumps({"rank": rank, "world": world, "max_rel_err": worst, "device_errors": errors}), flush=True)
+    print(json.dumps({"rank": rank, "world": world, "bitwise_separate": bitwise_sep, "bitwise_fused": bitwise_fused,
+                      "max_rel_err": worst, "device_errors": errors}), flush=True)
 
 
 def dead_peer():
