@@ -299,6 +299,22 @@ int li4_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t cols, i
 int li4_argmax_rows_keys(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
                          int64_t index_offset, int64_t* keys, int64_t keys_stride, void* stream);
 
+/* The greedy step of a vocabulary-sharded lm_head under tensor parallelism, in one launch:
+ * every rank finds the winner of its shard (columns index_offset .. index_offset + cols - 1 of
+ * the full vocabulary) as li4_argmax_rows_keys does, stores its key into every rank's receive
+ * buffer over NVLink as two 8-byte words that carry the call's epoch, waits (bounded) for every
+ * rank's key of the row in its own buffer, and writes out[r * out_stride] = the global index of
+ * the largest key -- torch.argmax over the gathered logits.  Receive buffer layout:
+ * [2][world][rows][2] words of 8 bytes (the epoch's parity picks the half); recv: host array of
+ * world device pointers, rank r's buffer at [r] (the peers' through CUDA IPC), each recv_bytes
+ * long; epochs: this rank's uint32 call counts per row, zero before the first call.  Every rank
+ * makes the same calls with the same rows.  A wait that runs out sets bit 6 of
+ * li4_device_errors.  Replaces: the reference's greedy logits[:, -1].argmax(-1) (bench.py:154-161)
+ * over logits that tensor parallelism would all-gather first. */
+int li4_argmax_rows_allreduce(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
+                              int64_t index_offset, void* const* recv, size_t recv_bytes, unsigned* epochs,
+                              int world, int rank, int64_t* out, int64_t out_stride, void* stream);
+
 /* out[r, :] = table[ids[r], :] for r < rows: fp16 rows of `cols` values (cols % 8 == 0,
  * 16-byte aligned rows; rows <= 65535).  An id outside [0, table_rows) is clamped and
  * sets bit 3 of li4_device_errors.  The ids may come from the preceding kernel on the
@@ -312,14 +328,16 @@ int li4_gather_rows(const void* table, int64_t table_rows, int64_t cols, int64_t
  * li4_allreduce_add ran out; bit 2: a decode program's wait for another op
  * ran out; bit 3: a gather (li4_gather_rows or a program gather) met an id
  * outside its table; bit 4: a bounded wait inside li4_int4_gemm ran out; bit 5: an
- * LI4_EPI_ALLREDUCE_RESIDUAL epilogue's wait for a peer's words ran out -- the kernel
+ * LI4_EPI_ALLREDUCE_RESIDUAL epilogue's wait for a peer's words ran out; bit 6: a wait of
+ * li4_argmax_rows_allreduce for a peer's key ran out -- the kernel
  * carried on and its outputs are not valid).  Synchronising: copies the flags to the host; reset != 0 clears them.
  * A diagnostic for tests and health checks, not for the decode loop. */
 int li4_device_errors(unsigned* flags, int reset);
 
 /* Test hook for the bounded device waits: the poll limit of li4_allreduce_add's
- * peer-flag waits and of the LI4_EPI_ALLREDUCE_RESIDUAL epilogue's waits for the
- * peers' words (allreduce_polls), the poll limit of the decode program's
+ * peer-flag waits, of the LI4_EPI_ALLREDUCE_RESIDUAL epilogue's waits for the
+ * peers' words and of li4_argmax_rows_allreduce's waits for the peers' keys
+ * (allreduce_polls), the poll limit of the decode program's
  * op-counter waits (program_polls) -- 0 restores each default (about a second
  * of polling) -- and, when program_wait_extra > 0, a target no program counter
  * wait can meet.  With a short limit a test can make a wait run out without a

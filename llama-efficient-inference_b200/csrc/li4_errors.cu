@@ -52,6 +52,7 @@ extern "C" int li4_debug_set_wait_limits(unsigned allreduce_polls, unsigned prog
                                          unsigned program_wait_extra) {
   int rc = li4::comm_set_wait_limit(allreduce_polls);
   if (rc == LI4_OK) rc = li4::gemv_set_ar_wait_limit(allreduce_polls);
+  if (rc == LI4_OK) rc = li4::sample_set_wait_limit(allreduce_polls);
   if (rc == LI4_OK) rc = li4::program_set_wait_limits(program_polls, program_wait_extra);
   if (rc == LI4_OK) li4::clear_error();
   return rc;

@@ -2022,9 +2022,9 @@ extern "C" int li4_device_errors(unsigned* flags, int reset) {
   unsigned gemm = 0;
   if (rc == LI4_OK) rc = li4::gemm_device_errors(&gemm, reset != 0);
   if (rc == LI4_OK) *flags |= gemm;
-  // the GEMV error words of the other translation units that run GEMV code
+  // the error words of the other translation units (GEMV code, the argmax key exchange)
   int (*const readers[])(unsigned*, bool) = {li4::slab_device_errors, li4::rows_device_errors,
-                                             li4::program_gemv_device_errors};
+                                             li4::program_gemv_device_errors, li4::sample_device_errors};
   for (auto read : readers) {
     unsigned f = 0;
     if (rc == LI4_OK) rc = read(&f, reset != 0);

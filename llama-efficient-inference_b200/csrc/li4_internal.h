@@ -27,6 +27,9 @@ int gemm_device_errors(unsigned* flags, bool reset);
 int slab_device_errors(unsigned* flags, bool reset);
 int rows_device_errors(unsigned* flags, bool reset);
 int program_gemv_device_errors(unsigned* flags, bool reset);
+// Device error word of the argmax kernels (bit 6) and the poll limit of their key exchange.
+int sample_device_errors(unsigned* flags, bool reset);
+int sample_set_wait_limit(unsigned polls);
 // Poll limit of the LI4_EPI_ALLREDUCE_RESIDUAL epilogue's waits (0 = default).
 int gemv_set_ar_wait_limit(unsigned polls);
 // Poll limit of the all-reduce flag waits (li4_comm.cu); 0 restores the default.

@@ -56,13 +56,81 @@ __device__ __forceinline__ long long argmax_signed_key(float v, long long global
   return (long long)(key ^ 0x8000000000000000ull);
 }
 
+// Exchange of the shards' winners between tensor-parallel ranks (li4_argmax_rows_allreduce): the
+// row's key goes to every rank as two 8-byte words {key half, epoch} stored straight into each
+// rank's receive buffer over NVLink (one 8-byte store is seen whole); the rank then polls its own
+// buffer (bounded) for every rank's two words of the row, and the largest key names the token.
+// The epoch is the row's call count on this rank (every rank makes the same calls), and its
+// parity picks one of two buffer halves, so call k + 1 never overwrites words of call k that a
+// slower rank may still be reading.
+struct KeyExchange {
+  unsigned long long* recv[8];  // every rank's receive buffer [2][world][rows][2] words
+  unsigned* epochs;             // this rank's call count per row
+  long long rows;
+  int world, rank;
+};
+
+__device__ unsigned g_sample_device_error;  // bit 6 of li4_device_errors
+constexpr unsigned kKeyWaitLimit = 1u << 20;
+__device__ unsigned g_key_wait_limit = kKeyWaitLimit;
+
+int sample_device_errors(unsigned* flags, bool reset) {
+  int rc = check_cuda(cudaMemcpyFromSymbol(flags, g_sample_device_error, sizeof(unsigned)), "device_errors: argmax");
+  if (rc == LI4_OK && reset) {
+    const unsigned zero = 0;
+    rc = check_cuda(cudaMemcpyToSymbol(g_sample_device_error, &zero, sizeof(unsigned)), "device_errors: clearing");
+  }
+  return rc;
+}
+
+int sample_set_wait_limit(unsigned polls) {
+  const unsigned v = polls ? polls : kKeyWaitLimit;
+  return check_cuda(cudaMemcpyToSymbol(g_key_wait_limit, &v, sizeof(v)), "debug_set_wait_limits: argmax exchange");
+}
+
+__device__ __forceinline__ long long exchange_key(const KeyExchange& x, long long row, long long key) {
+  const unsigned epoch = atomicAdd(&x.epochs[row], 1u) + 1u;
+  const long long half = (long long)(epoch & 1u) * x.world * x.rows * 2;
+  const unsigned long long hi = ((unsigned long long)epoch << 32) | (unsigned)((unsigned long long)key >> 32);
+  const unsigned long long lo = ((unsigned long long)epoch << 32) | (unsigned)((unsigned long long)key);
+  for (int r = 0; r < x.world; ++r) {
+    if (r == x.rank) continue;
+    unsigned long long* dst = x.recv[r] + half + ((long long)x.rank * x.rows + row) * 2;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(hi) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + 1), "l"(lo) : "memory");
+  }
+  long long best = key;
+  bool failed = false;
+  for (int r = 0; r < x.world; ++r) {
+    if (r == x.rank) continue;
+    const unsigned long long* src = x.recv[x.rank] + half + ((long long)r * x.rows + row) * 2;
+    unsigned long long w0 = 0, w1 = 0;
+    const unsigned limit = failed ? 1u : g_key_wait_limit;
+    for (unsigned it = 0;; ++it) {
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w0) : "l"(src) : "memory");
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w1) : "l"(src + 1) : "memory");
+      if ((unsigned)(w0 >> 32) == epoch && (unsigned)(w1 >> 32) == epoch) break;
+      if (it + 1 >= limit) {
+        if (!failed) atomicOr(&g_sample_device_error, 64u);
+        failed = true;
+        break;
+      }
+    }
+    const long long k = (long long)(((w0 & 0xFFFFFFFFull) << 32) | (w1 & 0xFFFFFFFFull));
+    if (k > best) best = k;
+  }
+  return best;
+}
+
 // key_offset < 0: out[row] = the row's argmax index; otherwise out[row] = argmax_signed_key of the
-// row's winner at global index key_offset + index.
+// row's winner at global index key_offset + index, or, with an exchange (x.world > 0), the global
+// index of the winner over every rank's shard.
 template <bool F16>
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void* logits, long long cols,
                                                                      long long stride, long long* out,
                                                                      long long out_stride, long long chunk,
-                                                                     long long key_offset) {
+                                                                     long long key_offset,
+                                                                     const __grid_constant__ KeyExchange x) {
   __shared__ Best s_best[kArgmaxThreads / 32];
   __shared__ Best s_cta;
   cg::cluster_group cluster = cg::this_cluster();
@@ -130,7 +198,14 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void*
       const Best other = *cluster.map_shared_rank(&s_cta, rk);
       if (better(other, win)) win = other;
     }
-    out[row * out_stride] = key_offset < 0 ? win.i : argmax_signed_key(win.v, key_offset + win.i);
+    if (key_offset < 0) {
+      out[row * out_stride] = win.i;
+    } else if (x.world == 0) {
+      out[row * out_stride] = argmax_signed_key(win.v, key_offset + win.i);
+    } else {
+      const long long best = exchange_key(x, row, argmax_signed_key(win.v, key_offset + win.i));
+      out[row * out_stride] = 0xFFFFFFFFLL - (best & 0xFFFFFFFFLL);
+    }
   }
   cluster.sync();  // every CTA's candidate stays in place until the first CTA has read it
 }
@@ -138,7 +213,8 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const void*
 }  // namespace li4
 
 static int argmax_launch(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride, int64_t* out,
-                         int64_t out_stride, int64_t key_offset, void* stream) {
+                         int64_t out_stride, int64_t key_offset, void* stream,
+                         const li4::KeyExchange& x = li4::KeyExchange{}) {
   using namespace li4;
   if (dtype != LI4_F16 && dtype != LI4_F32)
     return set_error(LI4_ERR_UNSUPPORTED, "argmax_rows: dtype %d (LI4_F16 or LI4_F32)", dtype);
@@ -169,10 +245,10 @@ static int argmax_launch(const void* logits, int dtype, int64_t rows, int64_t co
   const long long ko = (long long)key_offset;
   const int rc = dtype == LI4_F16
                      ? check_cuda(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<true>, logits, (long long)cols,
-                                                     (long long)stride, o, (long long)out_stride, chunk, ko),
+                                                     (long long)stride, o, (long long)out_stride, chunk, ko, x),
                                   "argmax_rows: kernel launch")
                      : check_cuda(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<false>, logits, (long long)cols,
-                                                     (long long)stride, o, (long long)out_stride, chunk, ko),
+                                                     (long long)stride, o, (long long)out_stride, chunk, ko, x),
                                   "argmax_rows: kernel launch");
   if (rc == LI4_OK) clear_error();
   return rc;
@@ -189,4 +265,33 @@ extern "C" int li4_argmax_rows_keys(const void* logits, int dtype, int64_t rows,
     return li4::set_error(LI4_ERR_INVALID_ARG, "argmax_rows_keys: index_offset=%lld cols=%lld (global indices "
                           "below 2^32 - 1)", (long long)index_offset, (long long)cols);
   return argmax_launch(logits, dtype, rows, cols, stride, keys, keys_stride, index_offset, stream);
+}
+
+extern "C" int li4_argmax_rows_allreduce(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t stride,
+                                         int64_t index_offset, void* const* recv, size_t recv_bytes,
+                                         unsigned* epochs, int world, int rank, int64_t* out, int64_t out_stride,
+                                         void* stream) {
+  using namespace li4;
+  if (index_offset < 0 || index_offset + cols > (int64_t(1) << 32) - 1)
+    return set_error(LI4_ERR_INVALID_ARG, "argmax_rows_allreduce: index_offset=%lld cols=%lld (global indices "
+                     "below 2^32 - 1)", (long long)index_offset, (long long)cols);
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || !recv || !epochs ||
+      (reinterpret_cast<uintptr_t>(epochs) & 3u))
+    return set_error(LI4_ERR_INVALID_ARG, "argmax_rows_allreduce: world=%d rank=%d (1..8 ranks), receive buffers "
+                     "and a 4-byte aligned epoch array", world, rank);
+  const size_t need = (size_t)2 * world * (size_t)(rows > 0 ? rows : 0) * 2 * sizeof(unsigned long long);
+  if (recv_bytes < need)
+    return set_error(LI4_ERR_INVALID_ARG, "argmax_rows_allreduce: receive buffers of %zu bytes, %zu needed "
+                     "(2 x world x rows x 2 words of 8 bytes)", recv_bytes, need);
+  KeyExchange x = {};
+  for (int r = 0; r < world; ++r) {
+    if (!recv[r] || (reinterpret_cast<uintptr_t>(recv[r]) & 7u))
+      return set_error(LI4_ERR_ALIGNMENT, "argmax_rows_allreduce: receive buffer %d is null or not 8-byte aligned", r);
+    x.recv[r] = static_cast<unsigned long long*>(recv[r]);
+  }
+  x.epochs = epochs;
+  x.rows = rows;
+  x.world = world;
+  x.rank = rank;
+  return argmax_launch(logits, dtype, rows, cols, stride, out, out_stride, index_offset, stream, x);
 }

@@ -82,6 +82,7 @@ SIGNATURES = {
     "li4_int4_linear": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "li4_int4_linear_ex": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
                                   _INT, _INT, _INT, _INT]),
+    "li4_argmax_rows_allreduce": (_INT, [_P, _INT, _I64, _I64, _I64, _I64, _P, _SZ, _P, _INT, _INT, _P, _I64, _P]),
     "li4_int4_linear_noalloc": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_int4_gemm": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_int4_linear_fused": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,

@@ -36,7 +36,7 @@ def _round_up(v: int, a: int = _ALIGN) -> int:
 class NvlinkAllReduce:
     """One communication buffer per rank of `group`, mapped by every other rank."""
 
-    def __init__(self, group, max_elems: int, device: torch.device, ctas: int = 16):
+    def __init__(self, group, max_elems: int, device: torch.device, ctas: int = 16, key_rows: int = 64):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -48,7 +48,10 @@ class NvlinkAllReduce:
         self.flag_bytes = _round_up(4 * ctas * self.world)
         # fused form: per receive buffer, every rank's words [world][max_elems / 2] of 8 bytes
         self.recv_bytes = _round_up(self.world * ((max_elems + 1) // 2) * 8)
-        total = 2 * self.slot_bytes + self.flag_bytes + 2 * self.recv_bytes
+        # greedy step (argmax_allreduce): every rank's key words [2][world][key_rows][2] of 8 bytes
+        self.key_rows = key_rows
+        self.key_bytes = _round_up(2 * self.world * key_rows * 2 * 8)
+        total = 2 * self.slot_bytes + self.flag_bytes + 2 * self.recv_bytes + self.key_bytes
         with torch.cuda.device(device):
             base = ctypes.c_void_p()
             native.check(lib.li4_comm_alloc(total, ctypes.byref(base)), "comm_alloc")
@@ -76,6 +79,8 @@ class NvlinkAllReduce:
         self._recv = [arr(*[b + recv0 + s * self.recv_bytes for b in bases]) for s in (0, 1)]
         # per receive buffer, this rank's call count of every 16-row output tile
         self.epochs = torch.zeros(2, (max_elems + 15) // 16, dtype=torch.int32, device=device)
+        self._keys = arr(*[b + recv0 + 2 * self.recv_bytes for b in bases])
+        self.key_epochs = torch.zeros(key_rows, dtype=torch.int32, device=device)
 
     def slot_ptr(self, slot: int) -> int:
         """Device address of this rank's partial slot `slot` (0 or 1), fp16, max_elems values."""
@@ -101,6 +106,21 @@ class NvlinkAllReduce:
                              stride_rm=residual.stride(0), ar_recv=ctypes.cast(self._recv[slot], ctypes.c_void_p),
                              ar_recv_bytes=self.recv_bytes, ar_epochs=self.epochs[slot].data_ptr(),
                              ar_world=self.world, ar_rank=self.rank)
+
+    def argmax_allreduce(self, logits: torch.Tensor, index_offset: int, out: torch.Tensor) -> None:
+        """out[r] = torch.argmax of row r of the full logits, of which this rank holds the columns
+        index_offset .. index_offset + logits.shape[1] - 1 (li4_argmax_rows_allreduce: each rank's key
+        goes to every rank over NVLink, no NCCL).  fp16 / fp32 logits with contiguous rows."""
+        codes = {torch.float16: native.LI4_F16, torch.float32: native.LI4_F32}
+        rows, cols = logits.shape
+        if logits.dtype not in codes or logits.stride(-1) != 1 or out.dtype != torch.long or rows > self.key_rows:
+            raise RuntimeError(f"argmax_allreduce: fp16 / fp32 logits of at most {self.key_rows} contiguous rows, "
+                               "an int64 output")
+        rc = native.lib().li4_argmax_rows_allreduce(
+            logits.data_ptr(), codes[logits.dtype], rows, cols, logits.stride(0), index_offset,
+            ctypes.cast(self._keys, ctypes.c_void_p), self.key_bytes, self.key_epochs.data_ptr(), self.world,
+            self.rank, out.data_ptr(), out.stride(0), native.stream_ptr(logits.device))
+        native.check(rc, "argmax_rows_allreduce")
 
     def close(self) -> None:
         lib = native.lib()

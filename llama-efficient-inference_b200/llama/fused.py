@@ -25,7 +25,10 @@ rank's receive buffer over NVLink and sums the ranks' partials with the residual
 in the same launch (LI4_EPI_ALLREDUCE_RESIDUAL, llama.comm.push_fusion).  With
 fused_allreduce=False the GEMV writes its partial into a buffer every rank has
 mapped and a second kernel sums the partials (li4_allreduce_add); with
-nvlink_allreduce=False NCCL all-reduces and torch adds the residual.
+nvlink_allreduce=False NCCL all-reduces and torch adds the residual.  The
+greedy step over the vocabulary-sharded lm_head likewise exchanges each rank's
+winner over NVLink inside the argmax launch (li4_argmax_rows_allreduce), or
+through an NCCL MAX all-reduce of ordered keys.
 
 The fused epilogues pair two GEMV outputs in one thread.  They take weights
 whose rows are rearranged once, at construction (pair_permutation,
@@ -253,7 +256,7 @@ class FusedDecoder:
                 from .comm import NvlinkAllReduce
 
                 self._ar = NvlinkAllReduce(group, max_elems=self.model.params.max_batch_size * self.dim,
-                                           device=self.device)
+                                           device=self.device, key_rows=max(64, self.model.params.max_batch_size))
             if self.fused_allreduce:
                 int4_linear_fused(x, *w, out, self._ar.push_fusion(slot, residual))
                 return
@@ -405,13 +408,18 @@ class FusedDecoder:
             import torch.distributed as dist
 
             if next_tokens is not None:
-                keys = self._bufs.get(("keys", bs))
-                if keys is None:
-                    keys = self._bufs[("keys", bs)] = torch.empty(bs, 1, dtype=torch.long, device=self.device)
                 shard = logits.shape[-1]
-                argmax_rows_keys(logits, dist.get_rank(self.model.tp_group) * shard, keys)
-                dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.model.tp_group)
-                next_tokens.view(bs, 1).copy_(key_index(keys))
+                offset = dist.get_rank(self.model.tp_group) * shard
+                if self._ar is not None and self.fused_allreduce:
+                    # the keys cross NVLink inside the argmax launch (li4_argmax_rows_allreduce)
+                    self._ar.argmax_allreduce(logits, offset, next_tokens.view(bs, 1))
+                else:
+                    keys = self._bufs.get(("keys", bs))
+                    if keys is None:
+                        keys = self._bufs[("keys", bs)] = torch.empty(bs, 1, dtype=torch.long, device=self.device)
+                    argmax_rows_keys(logits, offset, keys)
+                    dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.model.tp_group)
+                    next_tokens.view(bs, 1).copy_(key_index(keys))
             return logits.view(bs, 1, -1)  # this rank's vocabulary shard
         if next_tokens is not None:
             argmax_rows(logits, next_tokens.view(bs, 1))

@@ -31,7 +31,8 @@ def test_tp_int4_model_matches_unsharded(world):
 def test_tp_nvlink_allreduce_matches_nccl(world):
     """The row-parallel sum over NVLink peer memory -- li4_allreduce_add after the GEMV, and the GEMV
     that finishes the all-reduce in its own launch -- bit for bit against every rank's partial gathered
-    through NCCL and summed in rank order, eager and replayed from a CUDA graph."""
+    through NCCL and summed in rank order, eager and replayed from a CUDA graph; and the greedy step over
+    vocabulary shards with the keys exchanged over NVLink against torch.argmax of the gathered logits."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     outs = launch("gpu_allreduce", world=world, timeout_s=300,
@@ -40,4 +41,5 @@ def test_tp_nvlink_allreduce_matches_nccl(world):
         assert rc == 0, err[-3000:]
         rec = json.loads(out.strip().splitlines()[-1])
         assert rec["bitwise_separate"] and rec["bitwise_fused"], rec
+        assert rec["argmax_exchange_equal"], rec
         assert rec["device_errors"] == 0, rec

@@ -1,8 +1,9 @@
 """The bounded device waits run out without a fault, report it, and leave the context usable.
 
-Three kernels here spin on memory that another agent writes: li4_allreduce_add waits for
+Four kernels here spin on memory that another agent writes: li4_allreduce_add waits for
 every peer's flag, a row-parallel GEMV with the all-reduce epilogue waits for every peer's
-words, and a decode program's op waits for the completion counter of the op it depends on.  Each wait gives up after a poll limit, sets its bit in li4_device_errors and
+words, li4_argmax_rows_allreduce waits for every peer's key, and a decode program's op waits
+for the completion counter of the op it depends on.  Each wait gives up after a poll limit, sets its bit in li4_device_errors and
 returns.  li4_debug_set_wait_limits shortens the limits so a test can make the waits run out
 on one GPU, with nothing faulting or hanging: the peer is a local buffer that nobody writes,
 and the program's counter target is one no op can meet.  Every test restores the defaults.
@@ -103,6 +104,36 @@ def test_fused_allreduce_wait_runs_out(native, cuda_device):
     torch.cuda.synchronize()
     assert native.device_errors(reset=True) == 0
     assert torch.equal(out, want)
+
+
+def test_argmax_exchange_wait_runs_out(native, cuda_device):
+    """Rank 0 of a 2-rank greedy step over vocabulary shards (li4_argmax_rows_allreduce) whose peer never
+    sends its keys: the wait gives up after the short limit, sets bit 6, and the launch still writes a
+    token -- this shard's winner, since the zero words it read make a key below any positive maximum."""
+    lib = native.lib()
+    native.check(lib.li4_debug_set_wait_limits(SHORT, 0, 0), "debug_set_wait_limits")
+    rows, cols, world = 4, 3000, 2
+    logits = torch.randn(rows, cols, generator=torch.Generator().manual_seed(9)).abs().to(cuda_device)
+    recv = [torch.zeros(2 * world * rows * 2, dtype=torch.int64, device=cuda_device) for _ in range(world)]
+    epochs = torch.zeros(rows, dtype=torch.int32, device=cuda_device)
+    ptrs = (ctypes.c_void_p * world)(*[r.data_ptr() for r in recv])
+    out = torch.full((rows, 1), -1, dtype=torch.long, device=cuda_device)
+    rc = lib.li4_argmax_rows_allreduce(logits.data_ptr(), native.LI4_F32, rows, cols, cols, 0,
+                                       ctypes.cast(ptrs, ctypes.c_void_p), recv[0].numel() * 8, epochs.data_ptr(),
+                                       world, 0, out.data_ptr(), 1, native.stream_ptr(cuda_device))
+    native.check(rc, "argmax_rows_allreduce")
+    torch.cuda.synchronize()
+    assert native.device_errors(reset=True) & 64, "the key exchange wait did not report running out"
+    assert torch.equal(out.view(-1), logits.argmax(-1))
+    assert torch.equal(epochs, torch.ones_like(epochs))
+    native.check(lib.li4_debug_set_wait_limits(0, 0, 0), "debug_set_wait_limits")
+    rc = lib.li4_argmax_rows_allreduce(logits.data_ptr(), native.LI4_F32, rows, cols, cols, 0,
+                                       ctypes.cast(ptrs, ctypes.c_void_p), recv[0].numel() * 8, epochs.data_ptr(),
+                                       1, 0, out.data_ptr(), 1, native.stream_ptr(cuda_device))
+    native.check(rc, "argmax_rows_allreduce")
+    torch.cuda.synchronize()
+    assert native.device_errors(reset=True) == 0
+    assert torch.equal(out.view(-1), logits.argmax(-1))
 
 
 def test_program_counter_wait_runs_out(native, cuda_device):

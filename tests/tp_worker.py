@@ -188,11 +188,43 @@ def gpu_allreduce():
             torch.cuda.synchronize(dev)
             check()
             del g
+        # the greedy step over vocabulary shards (li4_argmax_rows_allreduce) against torch.argmax of the
+        # gathered logits: random rows, a row whose maximum every shard shares (the first index wins)
+        # and fp16 logits; eager calls and graph replays
+        rows, shard = 16, 1000
+        lg = torch.Generator(device=dev).manual_seed(55 + rank)
+        keys_ok = True
+        for dtype in (torch.float32, torch.float16):
+            for trial in range(3):
+                logits = torch.randn(rows, shard, generator=lg, device=dev).to(dtype)
+                logits[3, 17] = 50.0  # the same maximum in every shard: rank 0's column 17 wins
+                full = [torch.empty_like(logits) for _ in range(world)]
+                dist.all_gather(full, logits)
+                want = torch.cat(full, 1).float().argmax(-1)
+                out = torch.full((rows, 1), -1, dtype=torch.long, device=dev)
+                ar.argmax_allreduce(logits, rank * shard, out)
+                torch.cuda.synchronize(dev)
+                keys_ok &= bool(torch.equal(out.view(-1), want))
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                ar.argmax_allreduce(logits, rank * shard, out)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(g):
+                ar.argmax_allreduce(logits, rank * shard, out)
+            for _ in range(3):
+                out.fill_(-1)
+                g.replay()
+                torch.cuda.synchronize(dev)
+                keys_ok &= bool(torch.equal(out.view(-1), want))
+            del g
     errors = _native.device_errors()
     dist.barrier()
     ar.close()
     print(json.dumps({"rank": rank, "world": world, "bitwise_separate": bitwise_sep, "bitwise_fused": bitwise_fused,
-                      "max_rel_err": worst, "device_errors": errors}), flush=True)
+                      "argmax_exchange_equal": keys_ok, "max_rel_err": worst, "device_errors": errors}), flush=True)
 
 
 def dead_peer():
