@@ -1321,17 +1321,24 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   // launches on B200 they measured slower than the choices below at every decode shape, e.g.
   // q_proj at M = 1 2.73 / 3.34 against 2.41 us, gate_proj 5.70 / 7.35 against 4.44 us.)
   if (kernel == LI4_KERNEL_AUTO) {
-    // By measured B200 sweeps of the Llama-3.2-1B shapes (bench.py --sweep):
-    // tile streaming when every warp slot gets several 16-row x 2048-k tiles
-    // (lm_head-sized N) at M <= 8; the bulk-copy ring for 2 <= M <= 8, at M > 8
-    // for lm_head-sized N too (41.6 against 47.7 us for lm_head at M = 16), and
-    // otherwise when each SM gets about four tiles or more (fused gate/up;
-    // down_proj at M > 8); streaming warps below that; CUDA-core / MMA kernels for
-    // groups below 128.
-    const int64_t tiles_2048 = ((N + 15) / 16) * std::max<int64_t>(1, K / 2048);
+    // By a measured B200 sweep of every family and split over the Llama-3.2-1B shapes at
+    // M = 1..16 (graphs of back-to-back launches, weights streaming from HBM): tile
+    // streaming when every warp slot gets several 16-row x 2048-k tiles (lm_head-sized N)
+    // at M <= 8; the bulk-copy ring when the 16-row tiles alone give each SM two or more
+    // at M >= 2 (gate / up / fused gate-up, lm_head at M = 16) or four or more at M = 1
+    // (fused gate-up: 6.47 against 8.91 us); streaming warps for everything narrower
+    // (q / k / v / o / fused qkv / down at every M: k_proj at M = 8 3.82 against 6.85 us
+    // on the bulk ring, down_proj at M = 2 7.0 against 10.9 us); CUDA-core / MMA kernels
+    // for groups below 128.  Launches with a prologue or epilogue keep the bulk ring for
+    // 2 <= M <= 8 and, at M > 8, wherever the 2048-k tiles give each SM two or more: the
+    // streaming kernel's fused variants spill at M > 8, and the fused decode step at batch
+    // 16 measured 0.97 ms with these choices against 1.04 ms with the plain ones.
+    const int64_t tiles = (N + 15) / 16;
+    const int64_t tiles_2048 = tiles * std::max<int64_t>(1, K / 2048);
+    const bool bulk_plain = (M >= 2 && tiles >= 2LL * sm) || tiles >= 4LL * sm;
+    const bool bulk_fused = (M >= 2 && M <= 8) || tiles_2048 >= 4LL * sm || (M > 8 && tiles_2048 >= 2LL * sm);
     if (group == 128 && K > 0 && K % 2048 == 0 && tiles_2048 >= 32LL * sm && M <= 8) kernel = LI4_KERNEL_TILE;
-    else if (group == 128 && K > 0 && K % 1024 == 0 &&
-             ((M >= 2 && M <= 8) || tiles_2048 >= 4LL * sm || (M > 8 && tiles_2048 >= 2LL * sm)))
+    else if (group == 128 && K > 0 && K % 1024 == 0 && (fused ? bulk_fused : bulk_plain))
       kernel = LI4_KERNEL_BULK;
     else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;

@@ -126,6 +126,66 @@ def test_fused_rejects_bad_epilogues(native):
     assert call(native.Fusion(epilogue=native.LI4_EPI_STORE_F32), y=18) == native.LI4_ERR_ALIGNMENT
 
 
+def test_fused_allreduce_epilogue_validates(native):
+    """LI4_EPI_ALLREDUCE_RESIDUAL checks its rank, buffers and sizes before any launch."""
+    lib = native.lib()
+    N, K, M = 64, 256, 1
+    need = 2 * (N // 16) * M * 8 * 8  # world x tiles x M x 8 words of 8 bytes
+    ptrs = (ctypes.c_void_p * 2)(256, 512)
+
+    def call(N=N, world=2, rank=0, recv=ptrs, nbytes=need, epochs=1024, residual=2048):
+        f = native.Fusion(epilogue=native.LI4_EPI_ALLREDUCE_RESIDUAL, residual=residual, stride_rm=N,
+                          ar_recv=ctypes.cast(recv, ctypes.c_void_p), ar_recv_bytes=nbytes, ar_epochs=epochs,
+                          ar_world=world, ar_rank=rank)
+        return lib.li4_int4_linear_fused(16, 16, 16, 16, 16, M, N, K, 128, K, K // 2, K // 128, N,
+                                         ctypes.byref(f), None, 0, None)
+
+    assert call(world=9) == native.LI4_ERR_INVALID_ARG
+    assert call(rank=2) == native.LI4_ERR_INVALID_ARG
+    assert call(nbytes=need - 8) == native.LI4_ERR_INVALID_ARG
+    assert call(N=40) == native.LI4_ERR_INVALID_ARG  # N % 16
+    assert call(residual=0) == native.LI4_ERR_INVALID_ARG
+    assert call(epochs=1026) == native.LI4_ERR_INVALID_ARG  # epoch array not 4-byte aligned
+    assert call(recv=(ctypes.c_void_p * 2)(256, 516)) == native.LI4_ERR_ALIGNMENT
+
+
+def test_argmax_allreduce_validates(native):
+    lib = native.lib()
+    rows, world = 4, 2
+    need = 2 * world * rows * 2 * 8
+    ptrs = (ctypes.c_void_p * 2)(256, 512)
+
+    def call(world=world, rank=0, recv=ptrs, nbytes=need, offset=0):
+        return lib.li4_argmax_rows_allreduce(256, native.LI4_F32, rows, 1000, 1000, offset,
+                                             ctypes.cast(recv, ctypes.c_void_p), nbytes, 1024, world, rank, 256, 1,
+                                             None)
+
+    assert call(world=0) == native.LI4_ERR_INVALID_ARG
+    assert call(rank=3) == native.LI4_ERR_INVALID_ARG
+    assert call(nbytes=need - 8) == native.LI4_ERR_INVALID_ARG
+    assert call(offset=-1) == native.LI4_ERR_INVALID_ARG
+    assert call(recv=(ctypes.c_void_p * 2)(256, 514)) == native.LI4_ERR_ALIGNMENT
+
+
+def test_dispatch_plans_b200(native):
+    """The automatic kernel choice on a 148-SM B200 for the Llama-3.2-1B decode shapes (from a measured
+    sweep of every family and split at M = 1..16): streaming warps for the narrow shapes at every M,
+    the bulk-copy ring for gate / up at M >= 2 and the fused gate-up at every M, the tile kernel for
+    lm_head at M <= 8 and the bulk ring at M = 16."""
+    want = {
+        (2048, 2048): ["stream"] * 5,                        # q / o
+        (512, 2048): ["stream"] * 5,                         # k / v
+        (3072, 2048): ["stream"] * 5,                        # fused qkv
+        (2048, 8192): ["stream"] * 5,                        # down
+        (8192, 2048): ["stream"] + ["bulk"] * 4,             # gate / up
+        (16384, 2048): ["bulk"] * 5,                         # fused gate-up
+        (128256, 2048): ["tile"] * 4 + ["bulk"],             # lm_head
+    }
+    for (N, K), kernels in want.items():
+        got = [native.plan(M, N, K, 128, 148)["kernel"] for M in (1, 2, 4, 8, 16)]
+        assert got == kernels, (N, K, got)
+
+
 def test_attention_and_argmax_validate(native):
     lib = native.lib()
     # head_dim 48 unsupported; GQA ratio 3 unsupported; misaligned cache
