@@ -328,6 +328,31 @@ def test_decode_attention_cluster_shapes(B, max_seq, pos, fz, cuda_device):
     close(out, attention_ref(q, ck, cv, pos, n_heads, n_kv_heads, head_dim), what="attention")
 
 
+@pytest.mark.parametrize("B,max_seq,old,new", [(1, 640, 100, 517), (4, 640, 517, 30), (16, 576, 200, 575)])
+def test_decode_attention_position_written_by_preceding_kernel(B, max_seq, old, new, fz, cuda_device):
+    """The position is written by the kernel right before the attention (li4_argmax_rows storing its
+    index into *pos): the attention reads the position before its dependency wait to start copying
+    cache rows, so it may see the old value and must then copy again (the "moved" path).  Whichever
+    way each launch goes, the result attends rows 0..new."""
+    fused, _ = fz
+    n_heads, n_kv_heads, head_dim = 32, 8, 64
+    q = randn((B, n_heads * head_dim), cuda_device, 71 + B)
+    ck = randn((B, max_seq, n_kv_heads, head_dim), cuda_device, 72)
+    cv = randn((B, max_seq, n_kv_heads, head_dim), cuda_device, 73)
+    logits = torch.zeros(1, max_seq, device=cuda_device)
+    logits[0, new] = 1.0
+    want = attention_ref(q, ck, cv, new, n_heads, n_kv_heads, head_dim)
+    out = torch.empty_like(q)
+    for _ in range(20):
+        pos_t = torch.tensor([old], dtype=torch.long, device=cuda_device)
+        out.zero_()
+        fused.argmax_rows(logits, pos_t.view(1, 1))  # *pos = new, written by the preceding kernel
+        fused.decode_attention(q, ck, cv, pos_t, out, n_heads, n_kv_heads)
+        torch.cuda.synchronize()
+        assert pos_t.item() == new
+        close(out, want, what="attention")
+
+
 @pytest.mark.parametrize("M", [1, 16])
 @pytest.mark.parametrize("N,K", [(128256, 2048), (1000, 256), (2048, 8192)])
 def test_store_f32_epilogue(M, N, K, fz, cuda_device):
