@@ -294,6 +294,29 @@ def time_concurrent(stream: Stream, n_streams: int = 4, reps: int = 50) -> dict:
                    f"{n_streams} streams of one CUDA graph"}
 
 
+def time_grouped(stream: Stream, reps: int = 50) -> dict:
+    """The same 113 independent GEMVs as one persistent launch (llama.int4_gemv.GroupedGemv,
+    li4_int4_linear_grouped): device time per step, GB/s, fraction of the measured HBM peak, and the
+    largest difference from the 113-launch step's outputs (the order of the fp32 sums differs)."""
+    from llama.int4_gemv import GroupedGemv
+
+    dev = stream.device
+    if any(stream.M * K * 2 > 32768 for _, _, K, _ in stream.shapes):
+        return {"unavailable": f"M={stream.M}: x of a problem above the grouped kernel's 32 KB staging"}
+    stream.graph.replay()
+    torch.cuda.synchronize(dev)
+    y_step = stream.y_flat.clone()
+    grouped = GroupedGemv([(stream.xs[i], *stream.weights[i], stream.ys[i]) for i in range(len(stream.shapes))])
+    us = _graph_us(grouped, 1, dev, reps=reps)
+    torch.cuda.synchronize(dev)
+    diff = float((stream.y_flat.float() - y_step.float()).abs().max())
+    gbps = stream.bytes_per_step / (us * 1e-6) / 1e9
+    return {"ms_per_step": round(us / 1e3, 4), "GBps": round(gbps, 1), "frac": round(gbps / measured_peak()[0], 4),
+            "units": grouped.units, "max_abs_diff_vs_step": diff,
+            "how": "the step's 113 GEMVs are independent (each its own x): one persistent launch streams them all "
+                   "from a work queue of 128-row units, largest K first"}
+
+
 def time_e2e(stream: Stream, steps: int, warmup: int, world: int, eager: bool = False):
     """H2D x (pinned) -> 113 calls -> D2H y (pinned), every step inside the timed region."""
     dev = stream.device
@@ -969,11 +992,15 @@ def run_gpu(a):
                 decode.append(run_decode(dev, bs, a.decode_prompt, a.decode_gen, a.decode_reps, world, fused=False))
     peak, peak_kind = measured_peak()
     kernels, shapes_cfg2, ref_step, ref_why, concurrent, gemm = None, None, None, None, None, None
+    grouped = None
     if rank == 0:
         log("per-kernel timing of the step")
         kernels = per_kernel_roofline(stream, peak)
         log("the step's independent GEMVs on 4 streams")
         concurrent = time_concurrent(stream)
+        if a.m <= 8:
+            log("the step's independent GEMVs as one grouped launch")
+            grouped = time_grouped(stream)
         log("prefill GEMM (tensor cores) against dequantize + cuBLAS")
         gemm = prefill_gemm(stream)
         reference = None
@@ -1035,6 +1062,7 @@ def run_gpu(a):
                       "ms_per_step": round(eager_ms, 5),
                       "path": "pinned H2D x -> 113 eager Python int4_linear_out calls -> D2H y"},
         "concurrent": concurrent,
+        "grouped": grouped,
         "prefill_gemm": gemm,
         "gpu_launches": len(stream.shapes) * a.steps,
         "clocks": sampler.summary(),

@@ -123,6 +123,35 @@ int li4_int4_linear_ex(const void* x, const void* packed, const void* scale, con
 int li4_int4_linear_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int sm_count,
                          int* kernel, int* split, int* grid_x, size_t* smem_bytes);
 
+/* One problem of a grouped launch: y[M, N] = x[M, K] @ W^T with this problem's own x, packed
+ * weights, scales, zeros and y (fp16; strides as li4_int4_linear's). */
+typedef struct li4_gemv_problem {
+  const void* x;
+  const void* packed;
+  const void* scale;
+  const void* zero;
+  void* y;
+  int64_t N, K;
+  int64_t stride_xm, stride_pn, stride_sn, stride_ym;
+} li4_gemv_problem;
+
+/* Many independent INT4 GEMVs in one persistent launch.  The work is cut into units of one
+ * problem's 128 output rows over its whole K; the launch's CTAs take units from a queue in
+ * the device table (largest K first), so the weight stream of every problem runs in one
+ * kernel with no launch boundary between problems.  Same math and rounding as li4_int4_linear.
+ * M in 1..8, group_size 128, K a multiple of 128 with M * K * 2 <= 32768 bytes, packed rows
+ * 16-byte aligned.  li4_int4_linear_grouped_table_bytes gives the size of the device table
+ * (0 for an invalid list) and the number of units; li4_int4_linear_grouped_build validates the
+ * list and writes the table (a synchronous host-to-device copy: build once, launch many);
+ * li4_int4_linear_grouped launches (no host data: capturable in a CUDA graph).  Launches that
+ * may overlap need their own tables.
+ * Replaces: a sequence of the reference's int4_linear calls (llama/int4_gemv.py:105-140) on
+ * independent inputs, one kernel launch each. */
+size_t li4_int4_linear_grouped_table_bytes(const li4_gemv_problem* problems, int n, int64_t M, int* units);
+int li4_int4_linear_grouped_build(const li4_gemv_problem* problems, int n, int64_t M, int64_t group_size,
+                                  void* table, size_t table_bytes);
+int li4_int4_linear_grouped(const void* table, int n, int units, int64_t M, void* stream);
+
 /* y[M, N] = x[M, K] @ W^T on the tensor cores (tcgen05, fp32 accumulation in tensor
  * memory) for any M >= 1, meant for prefill (M > 16).  The fp16 weights are rebuilt in
  * shared memory tile by tile, bit-identical to dequantize_packed's fp16((q - zero) * scale),

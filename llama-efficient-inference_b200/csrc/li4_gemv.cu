@@ -442,45 +442,6 @@ __device__ __forceinline__ void stream_advance(StreamCursor& c, int units_per_ti
   }
 }
 
-// Base pointers of a warp-thread for one tile (rows grp, grp + 8).
-struct StreamRows {
-  const uint8_t* p_lo;
-  const uint8_t* p_hi;
-  const unsigned short* s_lo;
-  const unsigned short* s_hi;
-  const unsigned short* z_lo;
-  const unsigned short* z_hi;
-};
-
-__device__ __forceinline__ StreamRows stream_rows(const GemvArgs& a, int tile, int ks0, int grp, int quad) {
-  int r0 = tile * 16 + grp, r1 = r0 + 8;
-  r0 = r0 < a.N ? r0 : a.N - 1;
-  r1 = r1 < a.N ? r1 : a.N - 1;
-  const long long off = (long long)ks0 * 64 + quad * 16;
-  const int g0 = (ks0 * 128) >> a.log2_group;
-  StreamRows r;
-  r.p_lo = a.packed + (long long)r0 * a.spn + off;
-  r.p_hi = a.packed + (long long)r1 * a.spn + off;
-  r.s_lo = reinterpret_cast<const unsigned short*>(a.scale) + (long long)r0 * a.ssn + g0;
-  r.s_hi = reinterpret_cast<const unsigned short*>(a.scale) + (long long)r1 * a.ssn + g0;
-  r.z_lo = reinterpret_cast<const unsigned short*>(a.zero) + (long long)r0 * a.ssn + g0;
-  r.z_hi = reinterpret_cast<const unsigned short*>(a.zero) + (long long)r1 * a.ssn + g0;
-  return r;
-}
-
-__device__ __forceinline__ uint32_t ldg_u16(const unsigned short* p) {
-  unsigned short r;
-  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
-  return r;
-}
-
-__device__ __forceinline__ void stream_load(const GemvArgs& a, StreamUnit& u, const StreamRows& r, int ks) {
-  u.lo = ldg_stream_v4(r.p_lo + ks * 64);
-  u.hi = ldg_stream_v4(r.p_hi + ks * 64);
-  const int g = (ks * 128) >> a.log2_group;
-  u.sz_lo = ldg_u16(r.s_lo + g) | (ldg_u16(r.z_lo + g) << 16);
-  u.sz_hi = ldg_u16(r.s_hi + g) | (ldg_u16(r.z_hi + g) << 16);
-}
 
 // ---------------------------------------------------------------------------
 // All-reduce + residual epilogue (LI4_EPI_ALLREDUCE_RESIDUAL), streaming-warp kernel only.

@@ -36,6 +36,15 @@ LI4_EPI_STORE, LI4_EPI_RESIDUAL, LI4_EPI_SWIGLU, LI4_EPI_QKV_ROPE, LI4_EPI_STORE
 LI4_EPI_ALLREDUCE_RESIDUAL = 5
 
 
+class GemvProblem(ctypes.Structure):
+    """struct li4_gemv_problem (include/llama_int4_b200.h): one GEMV of a grouped launch."""
+
+    _fields_ = [("x", ctypes.c_void_p), ("packed", ctypes.c_void_p), ("scale", ctypes.c_void_p),
+                ("zero", ctypes.c_void_p), ("y", ctypes.c_void_p), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+                ("stride_xm", ctypes.c_int64), ("stride_pn", ctypes.c_int64), ("stride_sn", ctypes.c_int64),
+                ("stride_ym", ctypes.c_int64)]
+
+
 class Fusion(ctypes.Structure):
     """struct li4_fusion (include/llama_int4_b200.h): fused prologue / epilogue of one GEMV."""
 
@@ -83,6 +92,9 @@ SIGNATURES = {
     "li4_int4_linear_ex": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
                                   _INT, _INT, _INT, _INT]),
     "li4_argmax_rows_allreduce": (_INT, [_P, _INT, _I64, _I64, _I64, _I64, _P, _SZ, _P, _INT, _INT, _P, _I64, _P]),
+    "li4_int4_linear_grouped_table_bytes": (_SZ, [_P, _INT, _I64, ctypes.POINTER(_INT)]),
+    "li4_int4_linear_grouped_build": (_INT, [_P, _INT, _I64, _I64, _P, _SZ]),
+    "li4_int4_linear_grouped": (_INT, [_P, _INT, _INT, _I64, _P]),
     "li4_int4_linear_noalloc": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_int4_gemm": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "li4_int4_linear_fused": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,

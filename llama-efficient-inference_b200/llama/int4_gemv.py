@@ -19,6 +19,7 @@ like the reference), so it locates its sibling _native.py by path too.
 """
 from __future__ import annotations
 
+import ctypes
 import importlib.util
 import os
 import sys
@@ -124,6 +125,42 @@ def int4_linear(x, packed, scale, zp, group_size=128, block_n=128, split_k=None,
     y = torch.empty(M, N, dtype=torch.float16, device=x.device)
     int4_linear_out(x2, packed, scale, zp, y, group_size)
     return y.reshape(*lead, N)
+
+
+class GroupedGemv:
+    """Many independent INT4 GEMVs in one persistent launch (li4_int4_linear_grouped).
+
+    problems: (x [M, K] fp16, packed, scale, zp, y [M, N] fp16) tuples on one device, every x with
+    the same M (1..8).  The device table is built once here; each call launches on the current
+    stream with no host data (capturable in a CUDA graph).  Results are li4_int4_linear's up to
+    the order of the fp32 sums."""
+
+    def __init__(self, problems, group_size: int = 128):
+        lib = _native.lib()
+        if not problems:
+            raise ValueError("GroupedGemv: no problems")
+        M = problems[0][0].shape[0]
+        self.device = problems[0][0].device
+        arr = (_native.GemvProblem * len(problems))()
+        for i, (x, p, s, z, y) in enumerate(problems):
+            if x.shape[0] != M or y.shape != (M, p.shape[0]) or x.dtype != torch.float16 or y.dtype != torch.float16:
+                raise RuntimeError(f"GroupedGemv: problem {i}: x [{M}, K] and y [{M}, N] fp16 expected")
+            p, s, z = _check_operands(x, p, s, z)
+            arr[i] = _native.GemvProblem(x.data_ptr(), p.data_ptr(), s.data_ptr(), z.data_ptr(), y.data_ptr(),
+                                         p.shape[0], x.shape[1], x.stride(0), p.stride(0), s.stride(0), y.stride(0))
+        units = ctypes.c_int()
+        nbytes = lib.li4_int4_linear_grouped_table_bytes(arr, len(problems), M, ctypes.byref(units))
+        if nbytes == 0:
+            _native.check(_native.LI4_ERR_INVALID_ARG, "int4_linear_grouped_table_bytes")
+        self.table = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        _native.check(lib.li4_int4_linear_grouped_build(arr, len(problems), M, group_size, self.table.data_ptr(),
+                                                        nbytes), "int4_linear_grouped_build")
+        self.n, self.units, self.M = len(problems), units.value, M
+        self._keep = problems  # the tensors the table points at
+
+    def __call__(self) -> None:
+        _native.check(_native.lib().li4_int4_linear_grouped(self.table.data_ptr(), self.n, self.units, self.M,
+                                                            _native.stream_ptr(self.device)), "int4_linear_grouped")
 
 
 def int4_gemm(x, packed, scale, zp, group_size=128):

@@ -167,6 +167,31 @@ def test_argmax_allreduce_validates(native):
     assert call(recv=(ctypes.c_void_p * 2)(256, 514)) == native.LI4_ERR_ALIGNMENT
 
 
+def test_grouped_validates(native):
+    """li4_int4_linear_grouped_* reject bad problem lists before any copy or launch."""
+    lib = native.lib()
+
+    def probs(**kw):
+        base = dict(x=256, packed=512, scale=768, zero=1024, y=1280, N=64, K=256, stride_xm=256, stride_pn=128,
+                    stride_sn=2, stride_ym=64)
+        base.update(kw)
+        arr = (native.GemvProblem * 1)()
+        arr[0] = native.GemvProblem(**base)
+        return arr
+
+    units = ctypes.c_int()
+    assert lib.li4_int4_linear_grouped_table_bytes(probs(), 1, 1, ctypes.byref(units)) > 0 and units.value == 1
+    assert lib.li4_int4_linear_grouped_table_bytes(probs(), 1, 9, None) == 0          # M above 8
+    assert lib.li4_int4_linear_grouped_table_bytes(probs(K=200), 1, 1, None) == 0     # K % 128
+    assert lib.li4_int4_linear_grouped_table_bytes(probs(K=16384 + 128, stride_xm=16512, stride_pn=8256,
+                                                         stride_sn=129), 1, 1, None) == 0  # x staging
+    assert lib.li4_int4_linear_grouped_build(probs(y=0), 1, 1, 128, 4096, 1 << 20) == native.LI4_ERR_INVALID_ARG
+    assert lib.li4_int4_linear_grouped_build(probs(packed=520), 1, 1, 128, 4096, 1 << 20) == native.LI4_ERR_ALIGNMENT
+    assert lib.li4_int4_linear_grouped_build(probs(), 1, 1, 64, 4096, 1 << 20) == native.LI4_ERR_UNSUPPORTED
+    assert lib.li4_int4_linear_grouped_build(probs(), 1, 1, 128, 4096, 16) == native.LI4_ERR_WORKSPACE  # table
+    assert lib.li4_int4_linear_grouped(None, 1, 1, 1, None) == native.LI4_ERR_INVALID_ARG
+
+
 def test_dispatch_plans_b200(native):
     """The automatic kernel choice on a 148-SM B200 for the Llama-3.2-1B decode shapes (from a measured
     sweep of every family and split at M = 1..16): streaming warps for the narrow shapes at every M,
