@@ -57,9 +57,13 @@ typedef enum li4_kernel {
   LI4_KERNEL_SLAB = 6,       /* whole weight slice of a CTA resident in shared
                                 memory, K split across its warps: group 128, up to
                                 16 row tiles per CTA                              */
-  LI4_KERNEL_ROWS = 7        /* a warp's two rows unpacked in registers before the
+  LI4_KERNEL_ROWS = 7,       /* a warp's two rows unpacked in registers before the
                                 dependency wait: M = 1, group 128, K = 1024 or 2048,
                                 16-byte aligned x; no RMSNorm prologue or argmax  */
+  LI4_KERNEL_RING = 8        /* shared-memory ring of 16/32/64-row stages filled by
+                                bulk copies, 16 consumer warps per SM: group 128,
+                                M <= 8, K % 1024 == 0, M * K <= 32768, 16-byte
+                                aligned rows; rows_per_cta picks the stage rows   */
 } li4_kernel;
 
 /* Library version, (major << 16) | (minor << 8) | patch.  0.2: li4_fusion has the argmax_*

@@ -1206,8 +1206,9 @@ struct Plan {
   bool stream_ksplit;  // LI4_KERNEL_STREAM: K-split mode
   int stages;          // LI4_KERNEL_BULK: shared-memory ring stages
   bool bulk_contig;    // LI4_KERNEL_BULK: tiles move as three contiguous copies (set at launch from the strides)
-  int slots;           // LI4_KERNEL_SLAB: warps sharing one tile's ksteps (stages = tiles per CTA)
-  int pitch;           // LI4_KERNEL_SLAB: bytes between packed rows of a stage
+  int slots;           // LI4_KERNEL_SLAB: warps sharing one tile's ksteps (stages = tiles per CTA);
+                       // LI4_KERNEL_RING: 16-row tiles per stage
+  int pitch;           // LI4_KERNEL_SLAB / RING: bytes between packed rows of a stage
 };
 
 static inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -1262,6 +1263,57 @@ static bool slab_shape(int64_t M, int64_t N, int64_t K, int sm, int split_req, i
   return true;
 }
 
+// Launch shape of the ring kernel (li4_ring.cu), or false when the problem does not fit it:
+// group 128, M <= 8, K a multiple of 1024 with the staged x (M x K fp16) within 64 KiB, one K
+// range; T = rows_req / 16 tiles per stage (1, 2 or 4; 0 takes the first of 4, 2, 1 that gives
+// every consumer warp a kstep and two stages room), as many stages as fit next to the staged x
+// (2 at least), one CTA per SM (max_ctas caps it) and never more CTAs than stage units.
+static bool ring_fits(int64_t M, int ks, int T) {
+  if ((T != 1 && T != 2 && T != 4) || (ks * T) % kRingWarps != 0) return false;
+  const int stage = ring_stage_bytes(ks, T, ks * 64 + 64);
+  return ring_smem_bytes((int)M, ks, 2, stage) <= kRingSmemCap;
+}
+
+static bool ring_shape(int64_t M, int64_t N, int64_t K, int sm, int rows_req, int max_ctas, Plan* p) {
+  if (M < 1 || M > 8 || K <= 0 || K % 1024 != 0 || M * K * 2 > 65536 || rows_req % 16 != 0) return false;
+  const int ks = (int)(K / 128);
+  int T = rows_req / 16;
+  if (rows_req == 0) {
+    for (int t : {4, 2, 1})
+      if (ring_fits(M, ks, t)) { T = t; break; }
+  }
+  if (!ring_fits(M, ks, T)) return false;
+  const int pitch = ks * 64 + 64;
+  const int stage = ring_stage_bytes(ks, T, pitch);
+  const size_t fixed = ring_smem_bytes((int)M, ks, 0, stage);
+  const int n_tiles = (int)((N + 15) / 16);
+  const int n_su = (n_tiles + T - 1) / T;
+  int gx = std::min(sm, n_su);
+  if (max_ctas > 0) gx = std::max(1, std::min(gx, max_ctas));
+  const int per_cta = (n_su + gx - 1) / gx;
+  int stages = (int)std::min<size_t>(kRingMaxStages, (kRingSmemCap - fixed) / stage);
+  stages = std::max(2, std::min(stages, per_cta));
+  p->kernel = LI4_KERNEL_RING;
+  p->rt = 1;
+  p->nt = 1;
+  p->scale_in_a = false;
+  p->n_ks = ks;
+  p->split = 1;
+  p->ks_per_split = ks;
+  p->n_tiles = n_tiles;
+  p->grid_x = gx;
+  p->auto_grid = false;
+  p->sm = sm;
+  p->smem = ring_smem_bytes((int)M, ks, stages, stage);
+  p->stream_ksplit = false;
+  p->stages = stages;
+  p->slots = T;
+  p->pitch = pitch;
+  p->ws_counters = 0;
+  p->ws_bytes = 0;
+  return true;
+}
+
 static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int kernel_req, int rows_req,
                      int split_req, int max_ctas, Plan* p, bool fused = false) {
   if (M < 1 || M > LI4_MAX_M)
@@ -1298,16 +1350,24 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
     const int64_t tiles_2048 = tiles * std::max<int64_t>(1, K / 2048);
     const bool bulk_plain = (M >= 2 && tiles >= 2LL * sm) || tiles >= 4LL * sm;
     const bool bulk_fused = (M >= 2 && M <= 8) || tiles_2048 >= 4LL * sm || (M > 8 && tiles_2048 >= 2LL * sm);
+    // Long K over few row tiles (down_proj: 2048 x 8192) at M = 1 and, without a prologue or
+    // epilogue, M <= 4: the shared-memory ring with one 16-row x 8192-k stage per CTA and no
+    // split-K (M = 1 5.4 against 6.4 us on the streaming warps, M = 2 5.6 against 7.0, M = 4 6.9
+    // against 8.5).  Everywhere else the ring measured slower (lm_head 36.6 against 33.7 us).
+    Plan rp = {};
+    const bool ring_long_k = group == 128 && K >= 4096 && tiles <= sm && (M == 1 || (!fused && M <= 4)) &&
+                             split_req <= 1 && rows_req == 0 && ring_shape(M, N, K, sm, 0, max_ctas, &rp);
     if (group == 128 && K > 0 && K % 2048 == 0 && tiles_2048 >= 32LL * sm && M <= 8) kernel = LI4_KERNEL_TILE;
+    else if (ring_long_k) kernel = LI4_KERNEL_RING;
     else if (group == 128 && K > 0 && K % 1024 == 0 && (fused ? bulk_fused : bulk_plain))
       kernel = LI4_KERNEL_BULK;
     else if (group >= 128 && K > 0) kernel = LI4_KERNEL_STREAM;
     else kernel = (M <= 8) ? LI4_KERNEL_CUDA_CORE : LI4_KERNEL_MMA;
   }
   if (fused && kernel != LI4_KERNEL_STREAM && kernel != LI4_KERNEL_TILE && kernel != LI4_KERNEL_BULK &&
-      kernel != LI4_KERNEL_SLAB && kernel != LI4_KERNEL_ROWS)
+      kernel != LI4_KERNEL_SLAB && kernel != LI4_KERNEL_ROWS && kernel != LI4_KERNEL_RING)
     return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: fused prologues / epilogues run on the streaming-warp, "
-                     "tile, bulk-copy and slab kernels (group_size >= 128)");
+                     "tile, bulk-copy, slab and ring kernels (group_size >= 128)");
   if (kernel == LI4_KERNEL_CUDA_CORE && M > 8)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: CUDA-core kernel takes M <= 8 (M=%lld)", (long long)M);
   if (kernel == LI4_KERNEL_STREAM && (group < 128 || K == 0))
@@ -1318,8 +1378,15 @@ static int make_plan(int64_t M, int64_t N, int64_t K, int64_t group, int sm, int
   if (kernel == LI4_KERNEL_BULK && (group != 128 || K == 0 || (K / 128) % 8 != 0))
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the bulk-copy kernel needs group_size 128 and K a multiple "
                      "of 1024");
-  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_ROWS)
+  if (kernel < LI4_KERNEL_CUDA_CORE || kernel > LI4_KERNEL_RING)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear: unknown kernel %d", kernel);
+  if (kernel == LI4_KERNEL_RING) {
+    if (group != 128 || split_req > 1 || !ring_shape(M, N, K, sm, rows_req, max_ctas, p))
+      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear: M=%lld N=%lld K=%lld (rows %d, split %d) does not fit the "
+                       "ring kernel (group 128, M <= 8, K a multiple of 1024, M x K <= 32768, 16 / 32 / 64 rows per "
+                       "stage, one K range)", (long long)M, (long long)N, (long long)K, rows_req, split_req);
+    return LI4_OK;
+  }
   if (kernel == LI4_KERNEL_ROWS) {
     if (M != 1 || group != 128 || (K != 1024 && K != 2048))
       return set_error(LI4_ERR_INVALID_ARG, "int4_linear: the register-rows kernel takes M = 1, group_size 128 and "
@@ -1617,6 +1684,8 @@ static int launch_bulk_kernel(KernelT kernel, const Plan& p, const GemvArgs& arg
 
 static int launch_plan(const Plan& p, const GemvArgs& args, cudaStream_t s) {
   const bool fused = args.norm_w != nullptr || args.epi != LI4_EPI_STORE;
+  if (p.kernel == LI4_KERNEL_RING)
+    return launch_ring(args, fused, p.grid_x, p.slots, p.stages, p.pitch, p.smem, s);
   if (p.kernel == LI4_KERNEL_SLAB)
     return launch_slab(args, p.nt, fused, p.grid_x, p.stages, p.slots, p.pitch, p.smem, s);
   if (p.kernel == LI4_KERNEL_ROWS) return launch_rows(args, fused, s);
@@ -1881,7 +1950,7 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     if (rc != LI4_OK) return rc;
   }
   if (kernel == LI4_KERNEL_AUTO && f != nullptr && f->argmax_out != nullptr && p.kernel != LI4_KERNEL_TILE &&
-      M <= 8) {
+      p.kernel != LI4_KERNEL_RING && M <= 8) {
     // the fused greedy argmax runs on the tile kernel at M <= 8; where that does not take the
     // problem, the check below reports the fusion as unsupported (callers then run the argmax
     // separately)
@@ -1907,9 +1976,18 @@ static int int4_linear_impl(const void* x, const void* packed, const void* scale
     rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
     if (rc != LI4_OK) return rc;
   }
-  if (args.am_keys != nullptr && (p.kernel != LI4_KERNEL_TILE || p.split != 1))
-    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: the fused argmax runs on the tile kernel without a "
-                     "K split (lm_head-sized N at M <= 8); this launch plan has neither");
+  if (p.kernel == LI4_KERNEL_RING &&
+      (!aligned16(packed) || spn % 16 != 0 || !aligned16(scale) || !aligned16(zero) || ssn % 8 != 0)) {
+    // packed rows and scale / zero rows move as 16-byte-aligned bulk copies
+    if (kernel != LI4_KERNEL_AUTO)
+      return set_error(LI4_ERR_ALIGNMENT, "int4_linear: the ring kernel needs 16-byte aligned packed, scale and "
+                       "zero rows (packed row stride %% 16 == 0, scale row stride %% 8 == 0)");
+    rc = make_plan(M, N, K, group, sm, LI4_KERNEL_STREAM, rows_req, split_req, max_ctas, &p, fused);
+    if (rc != LI4_OK) return rc;
+  }
+  if (args.am_keys != nullptr && ((p.kernel != LI4_KERNEL_TILE && p.kernel != LI4_KERNEL_RING) || p.split != 1))
+    return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_fused: the fused argmax runs on the tile and ring kernels "
+                     "without a K split (lm_head-sized N at M <= 8); this launch plan has neither");
   if (p.ws_bytes > 0) {
     if (!workspace || workspace_bytes < p.ws_bytes)
       return set_error(LI4_ERR_WORKSPACE, "int4_linear: split-K (%d ranges) needs a %zu-byte zero-initialised "
@@ -1992,7 +2070,8 @@ extern "C" int li4_device_errors(unsigned* flags, int reset) {
   if (rc == LI4_OK) *flags |= gemm;
   // the error words of the other translation units (GEMV code, the argmax key exchange)
   int (*const readers[])(unsigned*, bool) = {li4::slab_device_errors, li4::rows_device_errors,
-                                             li4::program_gemv_device_errors, li4::sample_device_errors};
+                                             li4::ring_device_errors, li4::program_gemv_device_errors,
+                                             li4::sample_device_errors};
   for (auto read : readers) {
     unsigned f = 0;
     if (rc == LI4_OK) rc = read(&f, reset != 0);

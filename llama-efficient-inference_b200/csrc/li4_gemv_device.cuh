@@ -694,6 +694,22 @@ int launch_slab(const GemvArgs& a, int nt, bool fused, int grid_x, int tiles_max
 // Host: launch the register-rows kernel (li4_rows.cu): M = 1, K = 1024 or 2048, 16-byte aligned x.
 int launch_rows(const GemvArgs& a, bool fused, cudaStream_t stream);
 
+// Ring kernel (li4_ring.cu): 16 consumer warps and one bulk-copy producer warp per CTA, one CTA
+// per SM, a ring of up to kRingMaxStages shared-memory stages of T 16-row tiles each.
+constexpr int kRingWarps = 16;
+constexpr int kRingThreads = (kRingWarps + 1) * 32;
+constexpr int kRingMaxStages = 8;
+constexpr size_t kRingSmemCap = 227 * 1024;  // dynamic shared memory one ring CTA may take
+
+// Host: bytes of one ring stage (T tiles of `ks` ksteps at a row pitch of `pitch` bytes) and of
+// the whole dynamic shared memory of one ring CTA.
+int ring_stage_bytes(int ks, int T, int pitch);
+size_t ring_smem_bytes(int M, int ks, int stages, int stage_bytes);
+
+// Host: launch the ring kernel (group 128, M <= 8, one K range: a.ks_per_split == K / 128).
+int launch_ring(const GemvArgs& a, bool fused, int grid_x, int T, int stages, int pitch, size_t smem,
+                cudaStream_t stream);
+
 // Host: validate one linear (and its fusion) as li4_int4_linear_fused does and fill the
 // GemvArgs fields that do not depend on the launch plan (li4_gemv.cu).
 int prepare_linear(const void* x, const void* packed, const void* scale, const void* zero, void* y, int64_t M,

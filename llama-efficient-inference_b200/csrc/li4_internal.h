@@ -23,9 +23,10 @@ int comm_device_errors(unsigned* flags, bool reset);
 int program_device_errors(unsigned* flags, bool reset);
 // Device error word of the tensor-core GEMM (li4_gemm.cu); reset clears it.
 int gemm_device_errors(unsigned* flags, bool reset);
-// The GEMV device error words of the slab, register-rows and program translation units.
+// The GEMV device error words of the slab, register-rows, ring and program translation units.
 int slab_device_errors(unsigned* flags, bool reset);
 int rows_device_errors(unsigned* flags, bool reset);
+int ring_device_errors(unsigned* flags, bool reset);
 int program_gemv_device_errors(unsigned* flags, bool reset);
 // Device error word of the argmax kernels (bit 6) and the poll limit of their key exchange.
 int sample_device_errors(unsigned* flags, bool reset);

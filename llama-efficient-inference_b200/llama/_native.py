@@ -24,8 +24,8 @@ LI4_ERR_CUDA = 5
 
 LI4_F16, LI4_BF16, LI4_F32 = 0, 1, 2
 WORKSPACE_COUNTER_BYTES = 65536  # LI4_WORKSPACE_COUNTER_BYTES
-KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA, KERNEL_STREAM, KERNEL_TILE, KERNEL_BULK, KERNEL_SLAB, KERNEL_ROWS = \
-    0, 1, 2, 3, 4, 5, 6, 7
+KERNEL_AUTO, KERNEL_CUDA_CORE, KERNEL_MMA, KERNEL_STREAM, KERNEL_TILE, KERNEL_BULK, KERNEL_SLAB, KERNEL_ROWS, \
+    KERNEL_RING = 0, 1, 2, 3, 4, 5, 6, 7, 8
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -177,10 +177,10 @@ def device_errors(reset: bool = True) -> int:
 
 
 KERNEL_NAMES = {KERNEL_CUDA_CORE: "cuda_core", KERNEL_MMA: "mma", KERNEL_STREAM: "stream", KERNEL_TILE: "tile",
-                KERNEL_BULK: "bulk", KERNEL_SLAB: "slab", KERNEL_ROWS: "rows"}
+                KERNEL_BULK: "bulk", KERNEL_SLAB: "slab", KERNEL_ROWS: "rows", KERNEL_RING: "ring"}
 KERNEL_SYMBOLS = {KERNEL_CUDA_CORE: "gemv_cc_kernel", KERNEL_MMA: "gemv_mma_kernel", KERNEL_STREAM: "gemv_stream_kernel",
                   KERNEL_TILE: "gemv_tile_kernel", KERNEL_BULK: "gemv_bulk_kernel", KERNEL_SLAB: "gemv_slab_kernel",
-                  KERNEL_ROWS: "gemv_rows_kernel"}
+                  KERNEL_ROWS: "gemv_rows_kernel", KERNEL_RING: "gemv_ring_kernel"}
 
 
 def plan(M: int, N: int, K: int, group_size: int = 128, sm_count: int = 0) -> dict:

@@ -196,12 +196,12 @@ def test_dispatch_plans_b200(native):
     """The automatic kernel choice on a 148-SM B200 for the Llama-3.2-1B decode shapes (from a measured
     sweep of every family and split at M = 1..16): streaming warps for the narrow shapes at every M,
     the bulk-copy ring for gate / up at M >= 2 and the fused gate-up at every M, the tile kernel for
-    lm_head at M <= 8 and the bulk ring at M = 16."""
+    lm_head at M <= 8 and the bulk ring at M = 16, the shared-memory ring for down at M <= 4."""
     want = {
         (2048, 2048): ["stream"] * 5,                        # q / o
         (512, 2048): ["stream"] * 5,                         # k / v
         (3072, 2048): ["stream"] * 5,                        # fused qkv
-        (2048, 8192): ["stream"] * 5,                        # down
+        (2048, 8192): ["ring"] * 3 + ["stream"] * 2,         # down
         (8192, 2048): ["stream"] + ["bulk"] * 4,             # gate / up
         (16384, 2048): ["bulk"] * 5,                         # fused gate-up
         (128256, 2048): ["tile"] * 4 + ["bulk"],             # lm_head

@@ -21,7 +21,7 @@ LLAMA_SHAPES = [  # (name, N = out_features, K = in_features)
     ("q_proj", 2048, 2048), ("k_proj", 512, 2048), ("v_proj", 512, 2048), ("o_proj", 2048, 2048),
     ("gate_proj", 8192, 2048), ("up_proj", 8192, 2048), ("down_proj", 2048, 8192), ("lm_head", 128256, 2048),
 ]
-KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5, "slab": 6, "rows": 7}
+KERNELS = {"auto": 0, "cuda_core": 1, "mma": 2, "stream": 3, "tile": 4, "bulk": 5, "slab": 6, "rows": 7, "ring": 8}
 
 
 def sm_count() -> int:
@@ -61,6 +61,25 @@ def slab_fits(M: int, N: int, K: int, group: int = 128, split: int = 0, max_ctas
     return tiles <= 16 and smem <= 200 * 1024
 
 
+def ring_fits(M: int, K: int, rows: int = 0) -> bool:
+    """The ring kernel's planning rule (li4_gemv.cu ring_shape): group 128, M <= 8, K a multiple of 1024
+    with M x K fp16 within 64 KiB, 16 / 32 / 64-row stages whose ksteps split over the 16 consumer warps,
+    and two stages beside the staged x, the warp partials and the mbarriers within 227 KiB."""
+    if M > 8 or K <= 0 or K % 1024 or M * K * 2 > 65536 or rows % 16:
+        return False
+    ks = K // 128
+
+    def fits(T):
+        if T not in (1, 2, 4) or (ks * T) % 16:
+            return False
+        pitch = ks * 64 + 64
+        stage = (16 * T * pitch + 64 * T * ks + 127) & ~127
+        fixed = ((ks * M * 256 + 127) & ~127) + 2 * 16 * 16 * M * 4 + 2 * 8 * 8
+        return fixed + 2 * stage <= 227 * 1024
+
+    return fits(rows // 16) if rows else any(fits(t) for t in (4, 2, 1))
+
+
 def supported(kernel: str, M: int, group: int = 128, K: int = 2048, N: int = 300) -> bool:
     """Which forced kernel families take the problem."""
     if kernel == "slab":
@@ -75,6 +94,8 @@ def supported(kernel: str, M: int, group: int = 128, K: int = 2048, N: int = 300
         return group == 128 and K > 0 and K % 2048 == 0
     if kernel == "bulk":
         return group == 128 and K > 0 and K % 1024 == 0
+    if kernel == "ring":
+        return group == 128 and ring_fits(M, K)
     return True
 
 
@@ -272,6 +293,63 @@ def test_bulk_launch_shapes(M, split, max_ctas, N, K, g, cuda_device):
     int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["bulk"], split=split, max_ctas=max_ctas)
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
     assert native.device_errors() == 0
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("rows", [0, 16, 32, 64])
+@pytest.mark.parametrize("max_ctas", [0, 1, 5])
+@pytest.mark.parametrize("N,K", [(17, 2048), (300, 1024), (4100, 2048), (20000, 2048), (2049, 8192), (40, 4096)])
+def test_ring_launch_shapes(M, rows, max_ctas, N, K, g, cuda_device):
+    """Ring kernel: 16-, 32- and 64-row stages (consumer warps sharing a tile's ksteps 16, 8 or 4 ways),
+    one to many stage units per CTA (short grids wrap the ring around its stages many times), partial last
+    tiles and stage units, K from 1024 to 8192; deterministic, and no device-side wait ran out."""
+    int4_gemv, native = g
+    if not ring_fits(M, K, rows):
+        pytest.skip("x above the 64 KiB staging, a consumer warp without a kstep, or two stages beyond 227 KiB")
+    x, p, s, z, host = make_problem(N, K, M, seed=N + K + M + rows + max_ctas)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["ring"], rows_per_cta=rows, max_ctas=max_ctas)
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["ring"], rows_per_cta=rows, max_ctas=max_ctas)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+    assert native.device_errors() == 0
+
+
+@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("rows", [16, 64])
+@pytest.mark.parametrize("N,K", [(300, 2048), (2049, 8192)])
+def test_ring_strided_rows(M, rows, N, K, g, cuda_device):
+    """Ring kernel on packed / scale / zero rows with padded row strides: the per-row copies into padded
+    shared-memory rows instead of the three block copies of contiguous tensors."""
+    int4_gemv, native = g
+    if not ring_fits(M, K, rows):
+        pytest.skip("does not fit the ring kernel")
+    x, p, s, z, host = make_problem(N, K, M, seed=N + K + M + rows)
+    pw = torch.zeros(N, K // 2 + 48, dtype=torch.uint8, device=cuda_device)[:, :K // 2]
+    sw = torch.zeros(N, K // 128 + 8, dtype=torch.float16, device=cuda_device)[:, :K // 128]
+    zw = torch.zeros_like(sw)
+    pw.copy_(p), sw.copy_(s), zw.copy_(z)
+    y_ref, y32 = oracle.linear(*host)
+    y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+    int4_gemv.int4_linear_out(x, pw, sw, zw, y, 128, kernel=KERNELS["ring"], rows_per_cta=rows)
+    check_close(y, y_ref, y32, host)
+    y2 = torch.empty_like(y)
+    int4_gemv.int4_linear_out(x, p, s, z, y2, 128, kernel=KERNELS["ring"], rows_per_cta=rows)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "strided and contiguous rows differ"
+    assert native.device_errors() == 0
+
+
+def test_ring_rejects_what_does_not_fit(g, cuda_device):
+    """A forced ring launch outside its range (M > 8, K not a multiple of 1024, x above 64 KiB, a K split)
+    fails with a clear error and launches nothing."""
+    int4_gemv, native = g
+    for M, N, K, kw in ((16, 512, 2048, {}), (1, 512, 1536, {}), (8, 512, 8192, {}), (1, 512, 2048, {"split": 2})):
+        x, p, s, z, _ = make_problem(N, K, M, seed=M + K)
+        y = torch.empty(M, N, dtype=torch.float16, device=cuda_device)
+        with pytest.raises(native.Li4Error, match="ring kernel"):
+            int4_gemv.int4_linear_out(x, p, s, z, y, 128, kernel=KERNELS["ring"], **kw)
 
 
 @pytest.mark.parametrize("M", [1, 5, 9, 16])
