@@ -312,9 +312,10 @@ def time_grouped(stream: Stream, reps: int = 50) -> dict:
     diff = float((stream.y_flat.float() - y_step.float()).abs().max())
     gbps = stream.bytes_per_step / (us * 1e-6) / 1e9
     return {"ms_per_step": round(us / 1e3, 4), "GBps": round(gbps, 1), "frac": round(gbps / measured_peak()[0], 4),
-            "units": grouped.units, "max_abs_diff_vs_step": diff,
-            "how": "the step's 113 GEMVs are independent (each its own x): one persistent launch streams them all "
-                   "from a work queue of 128-row units, largest K first"}
+            "ranges": grouped.units, "max_abs_diff_vs_step": diff,
+            "how": "the step's 113 GEMVs are independent (each its own x): one persistent launch streams them all, "
+                   "their 16-row tiles cut into per-CTA ranges of equal weight bytes, each warp's tiles through one "
+                   "register ring"}
 
 
 def time_e2e(stream: Stream, steps: int, warmup: int, world: int, eager: bool = False):
@@ -530,12 +531,27 @@ def profile_shape(a):
     del w
     x = torch.randn(a.m, K, generator=gen, device=dev).half()
     y = torch.empty(a.m, N, dtype=torch.float16, device=dev)
-    kernel = {"auto": 0, "stream": 3, "tile": 4, "bulk": 5, "slab": 6}[a.kernel]
+    kernel = {"auto": 0, "stream": 3, "tile": 4, "bulk": 5, "slab": 6, "ring": 8}[a.kernel]
     for _ in range(a.launches):
         int4_linear_out(x, p, s, z, y, GROUP, kernel=kernel)
     torch.cuda.synchronize(dev)
     print(json.dumps({"profile_shape": a.profile_shape, "N": N, "K": K, "M": a.m, "launches": a.launches,
                       "kernel": a.kernel, "bytes_per_launch": gemv_bytes(N, K, a.m)}))
+
+
+def profile_grouped(a):
+    """--profile-grouped: `--launches` grouped launches of the 113-GEMV workload (a case for ncu captures of
+    gemv_grouped_kernel; 658 MB of weights on the device)."""
+    from llama.int4_gemv import GroupedGemv
+
+    dev = torch.device("cuda", 0)
+    stream = Stream(dev, a.m)
+    grouped = GroupedGemv([(stream.xs[i], *stream.weights[i], stream.ys[i]) for i in range(len(stream.shapes))])
+    for _ in range(a.launches):
+        grouped()
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_grouped": len(stream.shapes), "M": a.m, "launches": a.launches, "ranges": grouped.units,
+                      "bytes_per_launch": stream.bytes_per_step}))
 
 
 def profile_gemm(a):
@@ -1112,13 +1128,18 @@ def main():
     ap.add_argument("--profile-gemm", default=None, metavar="M,N,K",
                     help="only run --launches tensor-core INT4 GEMM launches of one shape (for ncu), no timing")
     ap.add_argument("--launches", type=int, default=3)
-    ap.add_argument("--kernel", default="auto", choices=["auto", "stream", "tile", "bulk", "slab"],
+    ap.add_argument("--profile-grouped", action="store_true",
+                    help="run --launches grouped launches of the 113-GEMV workload (for ncu captures)")
+    ap.add_argument("--kernel", default="auto", choices=["auto", "stream", "tile", "bulk", "slab", "ring"],
                     help="kernel family for --profile-shape (default: the dispatcher's choice)")
     ap.add_argument("--only-decode", action="store_true",
                     help="only the full-model decode measurement (one JSON line with the decode rows)")
     a = ap.parse_args()
     if a.reference_cpu_child:
         reference_cpu_child(a)
+        return
+    if a.profile_grouped:
+        profile_grouped(a)
         return
     if a.profile_shape:
         profile_shape(a)

@@ -139,16 +139,19 @@ typedef struct li4_gemv_problem {
   int64_t stride_xm, stride_pn, stride_sn, stride_ym;
 } li4_gemv_problem;
 
-/* Many independent INT4 GEMVs in one persistent launch.  The work is cut into units of one
- * problem's 128 output rows over its whole K; the launch's CTAs take units from a queue in
- * the device table (largest K first), so the weight stream of every problem runs in one
- * kernel with no launch boundary between problems.  Same math and rounding as li4_int4_linear.
- * M in 1..8, group_size 128, K a multiple of 128 with M * K * 2 <= 32768 bytes, packed rows
- * 16-byte aligned.  li4_int4_linear_grouped_table_bytes gives the size of the device table
- * (0 for an invalid list) and the number of units; li4_int4_linear_grouped_build validates the
- * list and writes the table (a synchronous host-to-device copy: build once, launch many);
- * li4_int4_linear_grouped launches (no host data: capturable in a CUDA graph).  Launches that
- * may overlap need their own tables.
+/* Many independent INT4 GEMVs in one persistent launch.  The problems' 16-row tiles, in list
+ * order, are cut into contiguous ranges of about equal weight bytes, one per CTA of a full wave;
+ * a CTA stages the x of the few problems its range touches once and each of its warps streams
+ * its tiles through one register ring that runs on across tile and problem boundaries, so the
+ * weight stream of every problem runs in one kernel with no launch boundary or barrier between
+ * tiles.  Same math and rounding as li4_int4_linear.  M in 1..8, group_size 128, K a multiple
+ * of 128 with M * K * 2 <= 32768 bytes, packed rows 16-byte aligned.
+ * li4_int4_linear_grouped_table_bytes gives the size of the device table (0 for an invalid
+ * list) and in *units the number of ranges (the ranges depend on the current device's SM
+ * count: build and launch on the same kind of device); li4_int4_linear_grouped_build validates
+ * the list and writes the table (a synchronous host-to-device copy: build once, launch many);
+ * li4_int4_linear_grouped launches with that `units` (no host data; a launch writes only the
+ * outputs, so launches repeat and overlap freely on one table).
  * Replaces: a sequence of the reference's int4_linear calls (llama/int4_gemv.py:105-140) on
  * independent inputs, one kernel launch each. */
 size_t li4_int4_linear_grouped_table_bytes(const li4_gemv_problem* problems, int n, int64_t M, int* units);

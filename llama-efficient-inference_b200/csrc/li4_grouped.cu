@@ -2,19 +2,19 @@
 //
 // A decode step's linears depend on each other, so each is its own launch and pays the
 // launch-chain latency.  Independent GEMVs (different weights, inputs and outputs) need not:
-// here one launch streams all of them.  The work is cut into units of one problem's 128 rows
-// (8 warps x 16-row tiles) over its whole K; CTAs take units from a queue -- the first from
-// their index, the rest from an atomic counter, largest K first -- so the HBM stream runs from
-// the first weight byte to the last without a kernel boundary.  Per unit the CTA stages the
-// problem's x once in shared memory (the layout of the streaming kernel), each warp walks its
-// tile's ksteps through a register ring D units deep (the first units of the first unit are
-// requested before the dependency wait), and the math is the streaming kernel's: exact
-// q - zero in fp16, m16n8k16 MMAs with fp32 accumulation per kstep, the group scale in fp32,
-// one fp16 rounding per output.
+// here one launch streams all of them.  The problems' 16-row tiles, in problem order, are cut
+// into contiguous ranges of about equal weight bytes, one per CTA of a full wave (two CTAs per
+// SM); a range stages the x of the few problems it touches once, and each of its 8 warps takes
+// tiles w, w + 8, ... of the range and streams their (tile, kstep) units through ONE register
+// ring D units deep that runs on across tile and problem boundaries -- the next tile's first
+// weights are in flight while the last ksteps of the current one are computed, and nothing
+// waits on a barrier between tiles.  The first units are requested before the dependency wait.
+// Math as the streaming kernel's: exact q - zero in fp16, m16n8k16 MMAs with fp32 accumulation
+// per kstep, the group scale in fp32, one fp16 rounding per output.
 //
-// The problems, the unit list and the queue counters live in a caller-owned device table built
-// once (li4_int4_linear_grouped_build); a launch then needs no host data and can be captured in
-// a CUDA graph.  The last CTA to finish resets the counters.
+// The problems and the ranges live in a caller-owned device table built once
+// (li4_int4_linear_grouped_build); a launch needs no host data, writes nothing but the outputs
+// and can be repeated or captured in a CUDA graph.
 #include "li4_common.cuh"
 #include "li4_gemv_device.cuh"
 #include "li4_internal.h"
@@ -28,9 +28,12 @@ namespace li4 {
 
 constexpr int kGroupWarps = 8;
 constexpr int kGroupThreads = kGroupWarps * 32;
-constexpr int kGroupDepth = 5;                 // ring units (16 rows x 128 k) in flight per warp
-constexpr int kGroupXBytes = 32768;            // x staging per buffer: M * K * 2 bytes at most
-constexpr int kGroupUnitRows = 16 * kGroupWarps;
+constexpr int kGroupDepth = 4;                 // ring units (16 rows x 128 k) in flight per warp
+constexpr int kGroupProblemX = 32768;          // x of one problem: M * K * 2 bytes at most
+constexpr int kGroupXBytes = 65536;            // x staging of one range (all its problems)
+constexpr int kGroupRangeProblems = 16;        // problems one range may touch
+constexpr int kGroupMinRangeUnits = 64;        // a range moves at least ~64 KB of weights
+constexpr int kGroupCtasPerSm = 2;
 
 struct GroupedProblem {
   const __half* x;
@@ -40,24 +43,27 @@ struct GroupedProblem {
   __half* y;
   int N, K;
   long long sxm, spn, ssn, sym;
+  int tile0;  // first flattened 16-row tile of this problem
+  int pad;
 };
 
 struct GroupedHeader {
-  int n_problems, n_units, M, pad0;
-  unsigned next;  // units handed out after the first `grid` (queue counter)
-  unsigned done;  // CTAs finished (the last one resets both)
-  unsigned pad[2];
+  int n_problems, n_ranges, M, pad;
 };
 
-// Table layout: header, problems[n_problems], units[n_units] (problem << 16 | 128-row group).
+// One CTA's work: flattened tiles [t0, t1), of problems p0 .. p1.
+struct GroupedRange {
+  int t0, t1, p0, p1;
+};
+
+// Table layout: header, problems[n_problems], ranges[n_ranges].
 struct GroupedArgs {
-  GroupedHeader* hdr;
   const GroupedProblem* problems;
-  const unsigned* units;
-  int n_units, M, log2_group;
+  const GroupedRange* ranges;
+  int n_ranges, M;
 };
 
-__device__ __forceinline__ GemvArgs grouped_problem_args(const GroupedProblem& p, int M, int log2_group) {
+__device__ __forceinline__ GemvArgs grouped_problem_args(const GroupedProblem& p, int M) {
   GemvArgs a = {};
   a.x = p.x;
   a.packed = p.packed;
@@ -67,7 +73,7 @@ __device__ __forceinline__ GemvArgs grouped_problem_args(const GroupedProblem& p
   a.M = M;
   a.N = p.N;
   a.K = p.K;
-  a.log2_group = log2_group;
+  a.log2_group = 7;
   a.sxm = p.sxm;
   a.spn = p.spn;
   a.ssn = p.ssn;
@@ -75,98 +81,145 @@ __device__ __forceinline__ GemvArgs grouped_problem_args(const GroupedProblem& p
   return a;
 }
 
-__global__ void __launch_bounds__(kGroupThreads, 2) gemv_grouped_kernel(const __grid_constant__ GroupedArgs g) {
+__host__ __device__ inline int grouped_x_bytes(int K, int M) { return ((K / 128) * M * 256 + 127) & ~127; }
+
+// A warp's walk over its (tile, kstep) units of one range: tiles first, first + 8, ... < end.
+struct GroupCursor {
+  int tile;       // flattened tile (>= end: done)
+  int ks, nks;    // kstep and ksteps of the tile's problem
+  int p;          // problem of `tile`
+  int tile0;      // its first flattened tile
+  int tile_end;   // one past its last
+  int xoff;       // its x in the range's staging
+  StreamRows rows;
+};
+
+__device__ __forceinline__ void cursor_problem(GroupCursor& c, const GroupedArgs& g, int M) {
+  const GroupedProblem& pr = g.problems[c.p];
+  c.tile0 = pr.tile0;
+  c.nks = pr.K / 128;
+  c.tile_end = pr.tile0 + (pr.N + 15) / 16;
+}
+
+__device__ __forceinline__ void cursor_rows(GroupCursor& c, const GroupedArgs& g, int M, int grp, int quad) {
+  const GemvArgs a = grouped_problem_args(g.problems[c.p], M);
+  c.rows = stream_rows(a, c.tile - c.tile0, 0, grp, quad);
+}
+
+// Move to the warp's next tile (8 tiles on), crossing into later problems of the range.
+__device__ __forceinline__ void cursor_next_tile(GroupCursor& c, const GroupedArgs& g, int M, int end, int grp,
+                                                 int quad) {
+  c.tile += kGroupWarps;
+  c.ks = 0;
+  if (c.tile >= end) return;
+  while (c.tile >= c.tile_end) {
+    c.xoff += grouped_x_bytes(c.nks * 128, M);
+    ++c.p;
+    cursor_problem(c, g, M);
+  }
+  cursor_rows(c, g, M, grp, quad);
+}
+
+__device__ __forceinline__ void cursor_advance(GroupCursor& c, const GroupedArgs& g, int M, int end, int grp,
+                                               int quad) {
+  if (++c.ks == c.nks) cursor_next_tile(c, g, M, end, grp, quad);
+}
+
+__device__ __forceinline__ void group_load(StreamUnit& u, const GroupCursor& c) {
+  u.lo = ldg_stream_v4(c.rows.p_lo + c.ks * 64);
+  u.hi = ldg_stream_v4(c.rows.p_hi + c.ks * 64);
+  u.sz_lo = ldg_u16(c.rows.s_lo + c.ks) | (ldg_u16(c.rows.z_lo + c.ks) << 16);
+  u.sz_hi = ldg_u16(c.rows.s_hi + c.ks) | (ldg_u16(c.rows.z_hi + c.ks) << 16);
+}
+
+__global__ void __launch_bounds__(kGroupThreads, kGroupCtasPerSm) gemv_grouped_kernel(const __grid_constant__ GroupedArgs g) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int D = kGroupDepth;
-  __shared__ unsigned s_unit[2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = lane >> 2, quad = lane & 3;
   const int M = g.M;
-
-  // this warp's tile of the first unit: its first D ksteps are requested before the wait
-  unsigned unit = blockIdx.x;
-  StreamUnit buf[D];
-  {
-    const unsigned u = g.units[unit];
-    const GemvArgs a = grouped_problem_args(g.problems[u >> 16], M, g.log2_group);
-    const int tile = (int)(u & 0xFFFFu) * kGroupWarps + warp;
-    const int nks = a.K / 128;
-    if (tile * 16 < a.N) {
-      const StreamRows r = stream_rows(a, tile, 0, grp, quad);
-#pragma unroll
-      for (int d = 0; d < D; ++d)
-        if (d < nks) stream_load(a, buf[d], r, d);
-    }
-  }
-  pdl_launch_dependents();
-  pdl_wait_primary();  // the inputs may come from the preceding kernel
-
   const bool bvalid = grp < M;
   int boff[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) boff[w] = (grp * 4 + quad) * 64 + ((w ^ xs_key(grp, quad)) << 4);
-  const int ks_stride = M * 256;
-  // (Requesting the next unit's first ksteps during this unit's last ones needs a ring depth that
-  // divides K / 128; with a 4-deep ring that measured slower than a 5-deep one without it:
-  // 0.209 against 0.197 ms for the 113 Llama-3.2-1B GEMVs.)
-  for (int it = 0;; ++it) {
-    // the unit after this one, taken now (the atomic's wait hides behind the staging); x of this
-    // unit staged into its half of the double buffer
-    uint8_t* xs = smem + (it & 1) * kGroupXBytes;
-    const unsigned u = g.units[unit];
-    const GemvArgs a = grouped_problem_args(g.problems[u >> 16], M, g.log2_group);
-    if (threadIdx.x == 0) s_unit[it & 1] = gridDim.x + atomicAdd(&g.hdr->next, 1u);
-    stage_x<1, kGroupThreads, false>(a, 0, a.K / 128, M, xs);
-    __syncthreads();
-    const unsigned next = s_unit[it & 1];
+  const int nt_stride = M * 256;
 
-    const int tile = (int)(u & 0xFFFFu) * kGroupWarps + warp;
-    const int nks = a.K / 128;
-    if (tile * 16 < a.N) {
-      const StreamRows r = stream_rows(a, tile, 0, grp, quad);
-      if (it > 0) {  // (the first unit's first ksteps were requested before the wait)
-#pragma unroll
-        for (int d = 0; d < D; ++d)
-          if (d < nks) stream_load(a, buf[d], r, d);
+  for (int ri = blockIdx.x; ri < g.n_ranges; ri += gridDim.x) {
+    const GroupedRange R = g.ranges[ri];
+    const bool first = ri == (int)blockIdx.x;
+    // this warp's units: the load cursor runs D units ahead of the compute cursor
+    GroupCursor cc;
+    cc.tile = R.t0 + warp;
+    cc.ks = 0;
+    cc.p = R.p0;
+    cc.xoff = 0;
+    cc.nks = 1;
+    if (cc.tile < R.t1) {
+      cursor_problem(cc, g, M);
+      while (cc.tile >= cc.tile_end) {
+        cc.xoff += grouped_x_bytes(cc.nks * 128, M);
+        ++cc.p;
+        cursor_problem(cc, g, M);
       }
-      float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-      for (int ks0 = 0; ks0 < nks; ks0 += D) {
-#pragma unroll
-        for (int d = 0; d < D; ++d) {
-          const int ks = ks0 + d;
-          if (ks < nks) {
-            stream_compute<1>(buf[d], xs + ks * ks_stride, M * 256, boff, bvalid, acc);
-            if (ks + D < nks) stream_load(a, buf[d], r, ks + D);
-          }
-        }
-      }
-      emit_warp_tile<false, 1>(a, tile, acc, grp, quad);
+      cursor_rows(cc, g, M, grp, quad);
     }
-    if (next >= (unsigned)g.n_units) break;
-    unit = next;
-  }
-  // the last CTA out resets the queue for the next launch
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(&g.hdr->done, 1u) == (unsigned)gridDim.x - 1) {
-      g.hdr->next = 0u;
-      g.hdr->done = 0u;
-      __threadfence();
+    GroupCursor lc = cc;
+    StreamUnit buf[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      if (lc.tile < R.t1) {
+        group_load(buf[d], lc);
+        cursor_advance(lc, g, M, R.t1, grp, quad);
+      }
+    if (first) {
+      pdl_launch_dependents();
+      pdl_wait_primary();  // the inputs may come from the preceding kernel
+    } else {
+      __syncthreads();  // every warp is done with the previous range's x
+    }
+    // x of the range's problems, back to back in the staging layout of the streaming kernel
+    {
+      int off = 0;
+      for (int p = R.p0; p <= R.p1; ++p) {
+        const GemvArgs a = grouped_problem_args(g.problems[p], M);
+        stage_x<1, kGroupThreads, false>(a, 0, a.K / 128, M, smem + off);
+        off += grouped_x_bytes(a.K, M);
+      }
+    }
+    __syncthreads();
+
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    while (cc.tile < R.t1) {
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        if (cc.tile >= R.t1) break;
+        stream_compute<1>(buf[d], smem + cc.xoff + cc.ks * nt_stride, nt_stride, boff, bvalid, acc);
+        if (lc.tile < R.t1) {
+          group_load(buf[d], lc);
+          cursor_advance(lc, g, M, R.t1, grp, quad);
+        }
+        if (cc.ks == cc.nks - 1) {  // the tile is complete
+          const GemvArgs a = grouped_problem_args(g.problems[cc.p], M);
+          emit_warp_tile<false, 1>(a, cc.tile - cc.tile0, acc, grp, quad);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[0][e] = 0.f;
+        }
+        cursor_advance(cc, g, M, R.t1, grp, quad);
+      }
     }
   }
 }
 
-// Table layout on the device: header | problems | units.
+// Table layout on the device: header | problems | ranges.
 static size_t grouped_offset_problems() { return (sizeof(GroupedHeader) + 15) & ~size_t(15); }
-static size_t grouped_offset_units(int n) { return grouped_offset_problems() + ((size_t)n * sizeof(GroupedProblem) + 15) / 16 * 16; }
-static size_t grouped_bytes(int n, int units) { return grouped_offset_units(n) + (size_t)units * sizeof(unsigned); }
+static size_t grouped_offset_ranges(int n) { return grouped_offset_problems() + ((size_t)n * sizeof(GroupedProblem) + 15) / 16 * 16; }
+static size_t grouped_bytes(int n, int ranges) { return grouped_offset_ranges(n) + (size_t)ranges * sizeof(GroupedRange); }
 
-static int grouped_check(const li4_gemv_problem* problems, int n, int64_t M, int* units) {
+static int grouped_check(const li4_gemv_problem* problems, int n, int64_t M) {
   if (!problems || n < 1 || n > 65535)
     return set_error(LI4_ERR_INVALID_ARG, "int4_linear_grouped: %d problems (1..65535, non-null)", n);
   if (M < 1 || M > 8) return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_grouped: M=%lld (1..8)", (long long)M);
-  int64_t total = 0;
+  int64_t tiles = 0;
   for (int i = 0; i < n; ++i) {
     const li4_gemv_problem& p = problems[i];
     if (!p.x || !p.packed || !p.scale || !p.zero || !p.y)
@@ -174,9 +227,9 @@ static int grouped_check(const li4_gemv_problem* problems, int n, int64_t M, int
     if (p.N < 1 || p.K < 128 || p.K % 128 != 0 || p.N > (int64_t(1) << 30))
       return set_error(LI4_ERR_INVALID_ARG, "int4_linear_grouped: problem %d: N=%lld K=%lld (K a multiple of 128)", i,
                        (long long)p.N, (long long)p.K);
-    if (M * p.K * 2 > kGroupXBytes)
+    if (M * p.K * 2 > kGroupProblemX)
       return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_grouped: problem %d: M x K = %lld x %lld is above the %d-byte "
-                       "x staging", i, (long long)M, (long long)p.K, kGroupXBytes);
+                       "x staging", i, (long long)M, (long long)p.K, kGroupProblemX);
     if (p.stride_xm < p.K || p.stride_pn < p.K / 2 || p.stride_sn < p.K / 128 || p.stride_ym < p.N)
       return set_error(LI4_ERR_INVALID_ARG, "int4_linear_grouped: problem %d: row strides smaller than the rows", i);
     if (!aligned16(p.packed) || p.stride_pn % 16 != 0)
@@ -185,24 +238,80 @@ static int grouped_check(const li4_gemv_problem* problems, int n, int64_t M, int
     if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.y) | reinterpret_cast<uintptr_t>(p.scale) |
          reinterpret_cast<uintptr_t>(p.zero)) & 1u)
       return set_error(LI4_ERR_ALIGNMENT, "int4_linear_grouped: problem %d: fp16 tensors must be 2-byte aligned", i);
-    const int64_t groups = (p.N + kGroupUnitRows - 1) / kGroupUnitRows;
-    if (groups > 65536)
-      return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_grouped: problem %d: N=%lld above %d rows", i,
-                       (long long)p.N, 65536 * kGroupUnitRows);
-    total += groups;
+    tiles += (p.N + 15) / 16;
   }
-  if (total > (int64_t(1) << 30)) return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_grouped: too many units");
-  *units = (int)total;
+  if (tiles > (int64_t(1) << 30)) return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_grouped: too many row tiles");
   return LI4_OK;
 }
 
-static int grouped_grid(int units, int* grid) {
+// CTAs of one full wave on the current device (the SM count of a B200 where no device answers).
+static int grouped_wave() {
+  const int sm = current_sm_count();
+  return kGroupCtasPerSm * (sm > 0 ? sm : 148);
+}
+
+// The flattened tiles cut into ranges of about equal weight bytes (a tile of problem p costs its
+// K / 128 ksteps), one per CTA of a wave -- fewer for small lists, so that a range moves at least
+// kGroupMinRangeUnits ksteps -- and each range cut again where its problems' x would pass the
+// staging limit or their count kGroupRangeProblems.  Deterministic: the same list and device give
+// the same ranges.
+static std::vector<GroupedRange> grouped_ranges(const li4_gemv_problem* problems, int n, int64_t M,
+                                                std::vector<int>* tile0) {
+  tile0->assign(n, 0);
+  int64_t total = 0;
+  int tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    (*tile0)[i] = tiles;
+    const int t = (int)((problems[i].N + 15) / 16);
+    tiles += t;
+    total += (int64_t)t * (problems[i].K / 128);
+  }
+  const int64_t parts = std::max<int64_t>(1, std::min<int64_t>(grouped_wave(), total / kGroupMinRangeUnits));
+  std::vector<GroupedRange> out;
+  GroupedRange cur = {0, 0, 0, 0};
+  int64_t cost = 0;        // cost of the tiles before the current one
+  int64_t xbytes = 0;      // x staging of the current range
+  int part = 0;            // index of the current cost part
+  bool open = false;
+  for (int p = 0; p < n; ++p) {
+    const int nt = (int)((problems[p].N + 15) / 16);
+    const int64_t c = problems[p].K / 128;
+    const int64_t xb = grouped_x_bytes((int)problems[p].K, (int)M);
+    for (int t = 0; t < nt; ++t) {
+      const int ft = (*tile0)[p] + t;
+      // the part this tile falls in: where the middle of its cost lies
+      const int tp = (int)std::min<int64_t>(parts - 1, ((2 * cost + c) * parts) / (2 * total));
+      const bool new_problem = open && cur.p1 != p;
+      const bool cut = open && (tp != part || (new_problem && (xbytes + xb > kGroupXBytes ||
+                                                               p - cur.p0 + 1 > kGroupRangeProblems)));
+      if (cut) {
+        out.push_back(cur);
+        open = false;
+      }
+      if (!open) {
+        cur = GroupedRange{ft, ft, p, p};
+        xbytes = xb;
+        part = tp;
+        open = true;
+      } else if (new_problem) {
+        cur.p1 = p;
+        xbytes += xb;
+      }
+      cur.t1 = ft + 1;
+      cost += c;
+    }
+  }
+  if (open) out.push_back(cur);
+  return out;
+}
+
+static int grouped_grid(int ranges, int* grid) {
   static std::mutex mu;
   static std::vector<std::pair<int, int>> cache;  // (device, CTAs per SM)
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "int4_linear_grouped: cudaGetDevice");
   if (rc != LI4_OK) return rc;
-  const size_t smem = 2 * (size_t)kGroupXBytes;
+  const size_t smem = kGroupXBytes;
   std::lock_guard<std::mutex> lock(mu);
   int occ = 0;
   for (auto& e : cache)
@@ -217,18 +326,19 @@ static int grouped_grid(int units, int* grid) {
     if (occ < 1) return set_error(LI4_ERR_CUDA, "int4_linear_grouped: the kernel does not fit on an SM");
     cache.emplace_back(dev, occ);
   }
-  *grid = std::min(units, occ * current_sm_count());
+  *grid = std::min(ranges, occ * current_sm_count());
   return LI4_OK;
 }
 
 }  // namespace li4
 
 extern "C" size_t li4_int4_linear_grouped_table_bytes(const li4_gemv_problem* problems, int n, int64_t M, int* units) {
-  int u = 0;
-  if (li4::grouped_check(problems, n, M, &u) != LI4_OK) return 0;
-  if (units) *units = u;
+  if (li4::grouped_check(problems, n, M) != LI4_OK) return 0;
+  std::vector<int> tile0;
+  const std::vector<li4::GroupedRange> ranges = li4::grouped_ranges(problems, n, M, &tile0);
+  if (units) *units = (int)ranges.size();
   li4::clear_error();
-  return li4::grouped_bytes(n, u);
+  return li4::grouped_bytes(n, (int)ranges.size());
 }
 
 extern "C" int li4_int4_linear_grouped_build(const li4_gemv_problem* problems, int n, int64_t M, int64_t group_size,
@@ -236,17 +346,18 @@ extern "C" int li4_int4_linear_grouped_build(const li4_gemv_problem* problems, i
   using namespace li4;
   if (group_size != 128)
     return set_error(LI4_ERR_UNSUPPORTED, "int4_linear_grouped: group_size=%lld (128)", (long long)group_size);
-  int units = 0;
-  int rc = grouped_check(problems, n, M, &units);
+  int rc = grouped_check(problems, n, M);
   if (rc != LI4_OK) return rc;
-  const size_t bytes = grouped_bytes(n, units);
+  std::vector<int> tile0;
+  const std::vector<GroupedRange> ranges = grouped_ranges(problems, n, M, &tile0);
+  const size_t bytes = grouped_bytes(n, (int)ranges.size());
   if (!table || table_bytes < bytes || !aligned16(table))
     return set_error(LI4_ERR_WORKSPACE, "int4_linear_grouped: a 16-byte aligned table of %zu bytes is needed (got %zu)",
                      bytes, table ? table_bytes : (size_t)0);
   std::vector<uint8_t> host(bytes, 0);
   GroupedHeader h = {};
   h.n_problems = n;
-  h.n_units = units;
+  h.n_ranges = (int)ranges.size();
   h.M = (int)M;
   memcpy(host.data(), &h, sizeof(h));
   GroupedProblem* gp = reinterpret_cast<GroupedProblem*>(host.data() + grouped_offset_problems());
@@ -255,18 +366,9 @@ extern "C" int li4_int4_linear_grouped_build(const li4_gemv_problem* problems, i
     gp[i] = GroupedProblem{static_cast<const __half*>(p.x), static_cast<const uint8_t*>(p.packed),
                            static_cast<const __half*>(p.scale), static_cast<const __half*>(p.zero),
                            static_cast<__half*>(p.y), (int)p.N, (int)p.K, p.stride_xm, p.stride_pn, p.stride_sn,
-                           p.stride_ym};
+                           p.stride_ym, tile0[i], 0};
   }
-  // units: largest K first (the long units start early, the short ones fill the tail), then in order
-  std::vector<int> order(n);
-  for (int i = 0; i < n; ++i) order[i] = i;
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return problems[a].K > problems[b].K; });
-  unsigned* up = reinterpret_cast<unsigned*>(host.data() + grouped_offset_units(n));
-  int k = 0;
-  for (int i : order) {
-    const int64_t groups = (problems[i].N + kGroupUnitRows - 1) / kGroupUnitRows;
-    for (int64_t gi = 0; gi < groups; ++gi) up[k++] = ((unsigned)i << 16) | (unsigned)gi;
-  }
+  memcpy(host.data() + grouped_offset_ranges(n), ranges.data(), ranges.size() * sizeof(GroupedRange));
   rc = check_cuda(cudaMemcpy(table, host.data(), bytes, cudaMemcpyHostToDevice), "int4_linear_grouped: table upload");
   if (rc == LI4_OK) clear_error();
   return rc;
@@ -275,23 +377,21 @@ extern "C" int li4_int4_linear_grouped_build(const li4_gemv_problem* problems, i
 extern "C" int li4_int4_linear_grouped(const void* table, int n, int units, int64_t M, void* stream) {
   using namespace li4;
   if (!table || n < 1 || units < 1 || M < 1 || M > 8)
-    return set_error(LI4_ERR_INVALID_ARG, "int4_linear_grouped: table=%p n=%d units=%d M=%lld", table, n, units,
+    return set_error(LI4_ERR_INVALID_ARG, "int4_linear_grouped: table=%p n=%d ranges=%d M=%lld", table, n, units,
                      (long long)M);
   int grid = 0;
   int rc = grouped_grid(units, &grid);
   if (rc != LI4_OK) return rc;
-  uint8_t* base = static_cast<uint8_t*>(const_cast<void*>(table));
+  const uint8_t* base = static_cast<const uint8_t*>(table);
   GroupedArgs g;
-  g.hdr = reinterpret_cast<GroupedHeader*>(base);
   g.problems = reinterpret_cast<const GroupedProblem*>(base + grouped_offset_problems());
-  g.units = reinterpret_cast<const unsigned*>(base + grouped_offset_units(n));
-  g.n_units = units;
+  g.ranges = reinterpret_cast<const GroupedRange*>(base + grouped_offset_ranges(n));
+  g.n_ranges = units;
   g.M = (int)M;
-  g.log2_group = 7;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3(kGroupThreads, 1, 1);
-  cfg.dynamicSmemBytes = 2 * (size_t)kGroupXBytes;
+  cfg.dynamicSmemBytes = kGroupXBytes;
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

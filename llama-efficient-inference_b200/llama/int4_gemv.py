@@ -131,9 +131,10 @@ class GroupedGemv:
     """Many independent INT4 GEMVs in one persistent launch (li4_int4_linear_grouped).
 
     problems: (x [M, K] fp16, packed, scale, zp, y [M, N] fp16) tuples on one device, every x with
-    the same M (1..8).  The device table is built once here; each call launches on the current
-    stream with no host data (capturable in a CUDA graph).  Results are li4_int4_linear's up to
-    the order of the fp32 sums."""
+    the same M (1..8).  The device table (the problems and their tiles cut into per-CTA ranges of
+    about equal weight bytes) is built once here; each call launches on the current stream with no
+    host data (capturable in a CUDA graph).  Results are li4_int4_linear's up to the order of the
+    fp32 sums."""
 
     def __init__(self, problems, group_size: int = 128):
         lib = _native.lib()

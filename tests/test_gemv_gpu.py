@@ -427,13 +427,15 @@ def test_slab_fits_every_layer_shape(g, cuda_device):
 
 
 def test_auto_dispatch_plans(g, cuda_device):
-    """The dispatcher's measured choices at M = 1: streaming warps for the layer shapes, the tile kernel
-    for lm_head (li4_int4_linear_plan reports what li4_int4_linear launches)."""
+    """The dispatcher's measured choices at M = 1: streaming warps for the layer shapes, the shared-memory
+    ring for down_proj, the tile kernel for lm_head (li4_int4_linear_plan reports what li4_int4_linear
+    launches)."""
     from llama import _native
 
+    want = {"lm_head": "tile", "down_proj": "ring"}
     for name, N, K in LLAMA_SHAPES:
         k = _native.plan(1, N, K)["kernel"]
-        assert k == ("tile" if name == "lm_head" else "stream"), (name, k)
+        assert k == want.get(name, "stream"), (name, k)
 
 
 def test_split_counters_reset_across_launches(g, cuda_device):

@@ -1,6 +1,5 @@
 """Grouped GEMVs (li4_int4_linear_grouped): many independent INT4 GEMVs in one persistent launch,
-each checked against the oracle; repeated launches (the work queue resets itself) and graph
-replays give the same bits."""
+each checked against the oracle; repeated launches and graph replays give the same bits."""
 import pytest
 import torch
 

@@ -19,7 +19,8 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 SHAPES = [  # (M, N, K, uses the scratch)
-    (4, 2048, 8192, True),    # down_proj at batch 4: two K ranges reduced by the last-arriving CTA
+    (4, 3000, 8192, True),    # a ragged K = 8192 linear at batch 4: two K ranges reduced by the last-arriving CTA
+    (4, 2048, 8192, False),   # down_proj at batch 4: the shared-memory ring, one K range, no scratch
     (8, 2048, 8192, True),    # down_proj at batch 8: four K ranges
     (16, 2048, 8192, True),   # down_proj at batch 16
     (1, 512, 2048, False),    # k_proj / v_proj at batch 1: one K range, no scratch
