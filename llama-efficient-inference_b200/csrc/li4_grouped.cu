@@ -9,8 +9,9 @@
 // ring D units deep that runs on across tile and problem boundaries -- the next tile's first
 // weights are in flight while the last ksteps of the current one are computed, and nothing
 // waits on a barrier between tiles.  The first units are requested before the dependency wait.
-// Math as the streaming kernel's: exact q - zero in fp16, m16n8k16 MMAs with fp32 accumulation
-// per kstep, the group scale in fp32, one fp16 rounding per output.
+// Math: m16n8k16 MMAs on the biased unpack below (1024 + q halves straight from the LOP3, the
+// zero and the bias taken off in fp32 per kstep), fp32 accumulation, the group scale in fp32, one
+// fp16 rounding per output.
 //
 // The problems and the ranges live in a caller-owned device table built once
 // (li4_int4_linear_grouped_build); a launch needs no host data, writes nothing but the outputs
@@ -81,7 +82,102 @@ __device__ __forceinline__ GemvArgs grouped_problem_args(const GroupedProblem& p
   return a;
 }
 
-__host__ __device__ inline int grouped_x_bytes(int K, int M) { return ((K / 128) * M * 256 + 127) & ~127; }
+// Staging of one problem's x in a range: the permuted x (the streaming kernel's layout, odd-k halves
+// scaled by 1/16), then per kstep and row m < 8 the sums the biased unpack needs (float2 [ks][8]).
+__host__ __device__ inline int grouped_x_bytes(int K, int M) {
+  return (((K / 128) * M * 256 + 127) & ~127) + (K / 128) * 8 * (int)sizeof(float2);
+}
+__host__ __device__ inline int grouped_sums_offset(int K, int M) { return ((K / 128) * M * 256 + 127) & ~127; }
+
+// ---------------------------------------------------------------------------
+// Biased unpack.  The exact unpack of the other kernels forms q - z in fp16 with a LOP3 and a
+// half2 subtract / FMA per pair of nibbles (9 instructions per 8 weights).  Here the MMA takes the
+// magic-number halves as they come out of the LOP3 -- 1024 + q for a low nibble (even k) and
+// 1024 + 16 q for a high nibble (odd k), both exact in fp16 -- against x with its odd-k entries
+// scaled by 1/16 (exact for |x| >= 2^-10), so a unit costs 5 instructions per 8 weights, and the
+// bias comes off in fp32 afterwards:
+//   sum_k (q_k - z) x_k = C - P - z Q,  C = the MMA result,
+//   P = 1024 (S_even + S'_odd),  Q = S_even + 16 S'_odd,
+// with S_even the kstep's even-k x and S'_odd its scaled odd-k x, summed in fp32 at staging.
+// C carries the bias (about 1024 |x| per term), so the fp32 sums of a unit lose ~10 bits to the
+// cancellation: absolute errors of ~1e-3 per unit before the group scale, far inside the
+// acceptance bound.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void grouped_stage_x(const GemvArgs& a, int M, uint8_t* xs, float2* sums) {
+  const int nks = a.K / 128;
+  const __half2 inv16 = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.sxm & 7) == 0);
+  for (int i = threadIdx.x; i < nks * 8; i += kGroupThreads)  // rows past M read as zero sums
+    if ((i & 7) >= M) sums[i] = make_float2(0.f, 0.f);
+  // item (ks, m, j), j = 16-byte chunk of the kstep (quad * 4 + w) fastest: the 16 chunks of one
+  // (kstep, row) sit on 16 consecutive lanes, which sum them with a fixed butterfly
+  const int items = nks * M * 16;
+  for (int base = 0; base < items; base += kGroupThreads) {
+    const int i = base + (int)threadIdx.x;
+    const bool live = i < items;
+    const int j = i & 15, km = i >> 4;
+    const int ks = km / M, m = km - ks * M;
+    const int quad = j >> 2, w = j & 3;
+    float se = 0.f, so = 0.f;
+    if (live) {
+      const __half* src = a.x + (long long)m * a.sxm + ks * 128 + 32 * quad + 8 * w;
+      uint32_t u[4];
+      if (vec_ok) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src);
+        u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          u[e] = (uint32_t)__half_as_ushort(src[2 * e]) | ((uint32_t)__half_as_ushort(src[2 * e + 1]) << 16);
+      }
+      uint4 out;
+      out.x = __byte_perm(u[0], u[2], 0x5410);                                     // (x0, x4)
+      out.y = h2_as_u32(__hmul2(u32_as_h2(__byte_perm(u[0], u[2], 0x7632)), inv16));  // (x1, x5) / 16
+      out.z = __byte_perm(u[1], u[3], 0x5410);                                     // (x2, x6)
+      out.w = h2_as_u32(__hmul2(u32_as_h2(__byte_perm(u[1], u[3], 0x7632)), inv16));  // (x3, x7) / 16
+      const float2 e0 = __half22float2(u32_as_h2(out.x)), e1 = __half22float2(u32_as_h2(out.z));
+      const float2 o0 = __half22float2(u32_as_h2(out.y)), o1 = __half22float2(u32_as_h2(out.w));
+      se = (e0.x + e0.y) + (e1.x + e1.y);
+      so = (o0.x + o0.y) + (o1.x + o1.y);
+      *reinterpret_cast<uint4*>(xs + xs_chunk_offset((ks * M + m) * 4 + quad, w, m)) = out;
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      se += __shfl_xor_sync(0xffffffffu, se, o);
+      so += __shfl_xor_sync(0xffffffffu, so, o);
+    }
+    if (live && j == 0) sums[ks * 8 + m] = make_float2(1024.f * (se + so), se + 16.f * so);
+  }
+}
+
+// acc += s * sum_k (q - z) x over one 16-row x 128-k unit with the biased unpack; sums_ks: the
+// kstep's (P, Q) for rows 0..7 of x.
+__device__ __forceinline__ void grouped_compute(const StreamUnit& u, const uint8_t* xs_ks, const float2* sums_ks,
+                                                const int boff[4], bool bvalid, int quad, float acc[4]) {
+  constexpr uint32_t MAGIC = 0x64006400u;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t wl = (w == 0) ? u.lo.x : (w == 1) ? u.lo.y : (w == 2) ? u.lo.z : u.lo.w;
+    const uint32_t wh = (w == 0) ? u.hi.x : (w == 1) ? u.hi.y : (w == 2) ? u.hi.z : u.hi.w;
+    const uint32_t wl8 = wl >> 8, wh8 = wh >> 8;
+    uint4 bq = make_uint4(0u, 0u, 0u, 0u);
+    if (bvalid) bq = lds128(xs_ks + boff[w]);
+    mma_16816(c, lop3_and_or(wl, 0x000F000Fu, MAGIC), lop3_and_or(wh, 0x000F000Fu, MAGIC),
+              lop3_and_or(wl, 0x00F000F0u, MAGIC), lop3_and_or(wh, 0x00F000F0u, MAGIC), bq.x, bq.y);
+    mma_16816(c, lop3_and_or(wl8, 0x000F000Fu, MAGIC), lop3_and_or(wh8, 0x000F000Fu, MAGIC),
+              lop3_and_or(wl8, 0x00F000F0u, MAGIC), lop3_and_or(wh8, 0x00F000F0u, MAGIC), bq.z, bq.w);
+  }
+  const float4 pq = *reinterpret_cast<const float4*>(sums_ks + 2 * quad);  // (P, Q) of x rows 2 quad, 2 quad + 1
+  const float sl = __half2float(__ushort_as_half((unsigned short)(u.sz_lo & 0xFFFFu)));
+  const float sh = __half2float(__ushort_as_half((unsigned short)(u.sz_hi & 0xFFFFu)));
+  const float zl = __half2float(__ushort_as_half((unsigned short)(u.sz_lo >> 16)));
+  const float zh = __half2float(__ushort_as_half((unsigned short)(u.sz_hi >> 16)));
+  acc[0] = fmaf(sl, fmaf(-zl, pq.y, c[0] - pq.x), acc[0]);
+  acc[1] = fmaf(sl, fmaf(-zl, pq.w, c[1] - pq.z), acc[1]);
+  acc[2] = fmaf(sh, fmaf(-zh, pq.y, c[2] - pq.x), acc[2]);
+  acc[3] = fmaf(sh, fmaf(-zh, pq.w, c[3] - pq.z), acc[3]);
+}
 
 // A warp's walk over its (tile, kstep) units of one range: tiles first, first + 8, ... < end.
 struct GroupCursor {
@@ -91,6 +187,7 @@ struct GroupCursor {
   int tile0;      // its first flattened tile
   int tile_end;   // one past its last
   int xoff;       // its x in the range's staging
+  int sums;       // its (P, Q) sums, bytes after xoff
   StreamRows rows;
 };
 
@@ -99,6 +196,7 @@ __device__ __forceinline__ void cursor_problem(GroupCursor& c, const GroupedArgs
   c.tile0 = pr.tile0;
   c.nks = pr.K / 128;
   c.tile_end = pr.tile0 + (pr.N + 15) / 16;
+  c.sums = grouped_sums_offset(pr.K, M);
 }
 
 __device__ __forceinline__ void cursor_rows(GroupCursor& c, const GroupedArgs& g, int M, int grp, int quad) {
@@ -182,7 +280,7 @@ __global__ void __launch_bounds__(kGroupThreads, kGroupCtasPerSm) gemv_grouped_k
       int off = 0;
       for (int p = R.p0; p <= R.p1; ++p) {
         const GemvArgs a = grouped_problem_args(g.problems[p], M);
-        stage_x<1, kGroupThreads, false>(a, 0, a.K / 128, M, smem + off);
+        grouped_stage_x(a, M, smem + off, reinterpret_cast<float2*>(smem + off + grouped_sums_offset(a.K, M)));
         off += grouped_x_bytes(a.K, M);
       }
     }
@@ -193,7 +291,9 @@ __global__ void __launch_bounds__(kGroupThreads, kGroupCtasPerSm) gemv_grouped_k
 #pragma unroll
       for (int d = 0; d < D; ++d) {
         if (cc.tile >= R.t1) break;
-        stream_compute<1>(buf[d], smem + cc.xoff + cc.ks * nt_stride, nt_stride, boff, bvalid, acc);
+        grouped_compute(buf[d], smem + cc.xoff + cc.ks * nt_stride,
+                        reinterpret_cast<const float2*>(smem + cc.xoff + cc.sums) + cc.ks * 8, boff, bvalid, quad,
+                        acc[0]);
         if (lc.tile < R.t1) {
           group_load(buf[d], lc);
           cursor_advance(lc, g, M, R.t1, grp, quad);
