@@ -351,10 +351,10 @@ static int grouped_wave() {
 }
 
 // The flattened tiles cut into ranges of about equal weight bytes (a tile of problem p costs its
-// K / 128 ksteps), one per CTA of a wave -- fewer for small lists, so that a range moves at least
-// kGroupMinRangeUnits ksteps -- and each range cut again where its problems' x would pass the
-// staging limit or their count kGroupRangeProblems.  Deterministic: the same list and device give
-// the same ranges.
+// K / 128 ksteps), about one per CTA of a wave -- fewer for small lists, so that a range moves at
+// least kGroupMinRangeUnits ksteps -- and each range cut again where its problems' x would pass
+// the staging limit or their count kGroupRangeProblems.  Deterministic: the same list and device
+// give the same ranges.
 static std::vector<GroupedRange> grouped_ranges(const li4_gemv_problem* problems, int n, int64_t M,
                                                 std::vector<int>* tile0) {
   tile0->assign(n, 0);
@@ -366,7 +366,13 @@ static std::vector<GroupedRange> grouped_ranges(const li4_gemv_problem* problems
     tiles += t;
     total += (int64_t)t * (problems[i].K / 128);
   }
-  const int64_t parts = std::max<int64_t>(1, std::min<int64_t>(grouped_wave(), total / kGroupMinRangeUnits));
+  // Range size: the wave's share of the ksteps, rounded up to a multiple of 512 (eight 16-row
+  // tiles of K = 8192, or 32 of K = 2048), so that a range of a long-K problem holds whole groups
+  // of 8 tiles -- the same number per warp: the Llama-3.2-1B step's 33-tile down_proj ranges gave
+  // some warps 5 tiles and others 4, and the slowest range sets the launch's time.
+  const int64_t wave = grouped_wave();
+  int64_t target = std::max<int64_t>(kGroupMinRangeUnits, (total + wave - 1) / wave);
+  if (target >= 512) target = (target + 511) / 512 * 512;
   std::vector<GroupedRange> out;
   GroupedRange cur = {0, 0, 0, 0};
   int64_t cost = 0;        // cost of the tiles before the current one
@@ -379,8 +385,8 @@ static std::vector<GroupedRange> grouped_ranges(const li4_gemv_problem* problems
     const int64_t xb = grouped_x_bytes((int)problems[p].K, (int)M);
     for (int t = 0; t < nt; ++t) {
       const int ft = (*tile0)[p] + t;
-      // the part this tile falls in: where the middle of its cost lies
-      const int tp = (int)std::min<int64_t>(parts - 1, ((2 * cost + c) * parts) / (2 * total));
+      // the part this tile falls in: where its cost starts
+      const int tp = (int)(cost / target);
       const bool new_problem = open && cur.p1 != p;
       const bool cut = open && (tp != part || (new_problem && (xbytes + xb > kGroupXBytes ||
                                                                p - cur.p0 + 1 > kGroupRangeProblems)));
