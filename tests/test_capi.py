@@ -192,6 +192,47 @@ def test_grouped_validates(native):
     assert lib.li4_int4_linear_grouped(None, 1, 1, 1, None) == native.LI4_ERR_INVALID_ARG
 
 
+def grouped_ranges_mirror(shapes, wave=296):
+    """The range cut of li4_int4_linear_grouped_build (li4_grouped.cu grouped_ranges), for lists whose
+    x staging never forces an extra cut: each tile starts a new range when its starting kstep count
+    crosses a multiple of the target (the wave's share, rounded up to a multiple of 512)."""
+    tiles = [(N + 15) // 16 for N, K in shapes]
+    costs = [K // 128 for N, K in shapes]
+    total = sum(t * c for t, c in zip(tiles, costs))
+    target = max(64, -(-total // wave))
+    if target >= 512:
+        target = -(-target // 512) * 512
+    ranges, cost, part = [], 0, None
+    for t, c in zip(tiles, costs):
+        for _ in range(t):
+            if part != cost // target:
+                ranges.append([])
+                part = cost // target
+            ranges[-1].append(c)
+            cost += c
+    return ranges
+
+
+def test_grouped_ranges_balanced(native):
+    """The grouped launch's ranges for the 113 Llama-3.2-1B decode GEMVs (no GPU: a 148-SM wave of
+    296 CTAs): 295 ranges, and within every range each of the 8 warps gets the same kstep count --
+    the slowest warp of the slowest range sets the launch's time."""
+    lib = native.lib()
+    shapes = [(2048, 2048), (512, 2048), (512, 2048), (2048, 2048), (8192, 2048), (8192, 2048),
+              (2048, 8192)] * 16 + [(128256, 2048)]
+    arr = (native.GemvProblem * len(shapes))()
+    for i, (N, K) in enumerate(shapes):
+        arr[i] = native.GemvProblem(x=256, packed=512, scale=768, zero=1024, y=1280, N=N, K=K, stride_xm=K,
+                                    stride_pn=K // 2, stride_sn=K // 128, stride_ym=N)
+    units = ctypes.c_int()
+    assert lib.li4_int4_linear_grouped_table_bytes(arr, len(shapes), 1, ctypes.byref(units)) > 0
+    ranges = grouped_ranges_mirror(shapes)
+    assert units.value == len(ranges) == 295
+    per_warp = [max(sum(r[w::8]) for w in range(8)) for r in ranges]
+    assert max(per_warp) == 256  # 2048 ksteps per range, 256 per warp
+    assert sum(map(sum, ranges)) == sum(((N + 15) // 16) * (K // 128) for N, K in shapes)
+
+
 def test_dispatch_plans_b200(native):
     """The automatic kernel choice on a 148-SM B200 for the Llama-3.2-1B decode shapes (from a measured
     sweep of every family and split at M = 1..16): streaming warps for the narrow shapes at every M,
